@@ -1,0 +1,112 @@
+"""The grouped product with LoRA adapters and the SwiGLU gate, in float32 numpy (test infrastructure).
+
+Follows ``meepsquared/_grouped.py``: the forward of ``reference_lora`` (:431-444), the per-expert base product of
+``reference`` (:420-428), and the gradients ``_LoraGroupedProduct.backward`` returns (:385-405): the input's and
+the adapters' (PEFT's lhs / rhs), none for the frozen stack, its scale, the offsets or the bias.
+"""
+
+import numpy as np
+
+
+def _segments(offsets):
+    start = 0
+    for e, end in enumerate(np.asarray(offsets, dtype=np.int64).tolist()):
+        yield e, start, end
+        start = end
+
+
+def _effective(weight, scale, e, lhs, rhs, scaling):
+    w = np.asarray(weight[e], dtype=np.float32)
+    if scale is not None:
+        w = w * np.float32(scale[e])
+    if lhs is not None:
+        w = w + np.float32(scaling) * (np.asarray(lhs[e], dtype=np.float32) @ np.asarray(rhs[e], dtype=np.float32))
+    return w
+
+
+def lora_forward(x, weight, scale, offsets, is_transposed, lhs=None, rhs=None, scaling=1.0, bias=None):
+    """reference_lora: per expert w = W_e * scale_e + s * lhs_e @ rhs_e, y = x_e @ (w or w^T) + bias_e (float32).
+
+    Rows past offsets[-1] (sentinels) come out zero. Returns (rows, N) float32.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    n = weight.shape[2] if is_transposed else weight.shape[1]
+    out = np.zeros((x.shape[0], n), dtype=np.float32)
+    for e, start, end in _segments(offsets):
+        if end == start:
+            continue
+        w = _effective(weight, scale, e, lhs, rhs, scaling)
+        y = x[start:end] @ (w if is_transposed else w.T)
+        if bias is not None:
+            y = y + np.asarray(bias[e], dtype=np.float32)
+        out[start:end] = y
+    return out
+
+
+def lora_low(x, offsets, is_transposed, lhs, rhs):
+    """The rank panel x_e @ A_e^T the kernel keeps for the backward pass (_grouped.py:168,208,212-214)."""
+    x = np.asarray(x, dtype=np.float32)
+    rank = lhs.shape[2]
+    low = np.zeros((x.shape[0], rank), dtype=np.float32)
+    for e, start, end in _segments(offsets):
+        a = np.asarray(lhs[e], dtype=np.float32) if is_transposed else np.asarray(rhs[e], dtype=np.float32).T
+        low[start:end] = x[start:end] @ a
+    return low
+
+
+def lora_backward(x, grad, weight, scale, offsets, is_transposed, lhs=None, rhs=None, scaling=1.0):
+    """Gradients of lora_forward: (grad_x, grad_lhs, grad_rhs), float32; grad_lhs/rhs None without adapters."""
+    x = np.asarray(x, dtype=np.float32)
+    g = np.asarray(grad, dtype=np.float32)
+    grad_x = np.zeros_like(x)
+    grad_lhs = np.zeros(lhs.shape, dtype=np.float32) if lhs is not None else None
+    grad_rhs = np.zeros(rhs.shape, dtype=np.float32) if rhs is not None else None
+    s = np.float32(scaling)
+    for e, start, end in _segments(offsets):
+        if end == start:
+            continue
+        w = _effective(weight, scale, e, lhs, rhs, scaling)
+        xe, ge = x[start:end], g[start:end]
+        grad_x[start:end] = ge @ (w.T if is_transposed else w)
+        if lhs is not None:
+            # the delta's gradient in the stack's layout: (out, in) = g^T x, or (in, out) = x^T g
+            d_delta = (xe.T @ ge) if is_transposed else (ge.T @ xe)
+            l, r = np.asarray(lhs[e], dtype=np.float32), np.asarray(rhs[e], dtype=np.float32)
+            grad_lhs[e] = s * (d_delta @ r.T)
+            grad_rhs[e] = s * (l.T @ d_delta)
+    return grad_x, grad_lhs, grad_rhs
+
+
+def silu(v):
+    v = np.asarray(v, dtype=np.float32)
+    return (v / (np.float32(1.0) + np.exp(-v))).astype(np.float32)
+
+
+def swiglu(gate_up):
+    """Transformers' _default_apply_gate: gate, up = chunk(2, -1); silu(gate) * up."""
+    gu = np.asarray(gate_up, dtype=np.float32)
+    i = gu.shape[1] // 2
+    return silu(gu[:, :i]) * gu[:, i:]
+
+
+def swiglu_backward(gate_up, grad_h):
+    """d/d(gate, up) of silu(gate) * up: (dh * up * silu'(gate), dh * silu(gate)) concatenated."""
+    gu = np.asarray(gate_up, dtype=np.float32)
+    i = gu.shape[1] // 2
+    g, u = gu[:, :i], gu[:, i:]
+    sig = (np.float32(1.0) / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+    dh = np.asarray(grad_h, dtype=np.float32)
+    dg = dh * u * sig * (np.float32(1.0) + g * (np.float32(1.0) - sig))
+    du = dh * g * sig
+    return np.concatenate([dg, du], axis=1).astype(np.float32)
+
+
+def reduce_adapter(g, low, offsets, scaling):
+    """_grouped._reduce (_grouped.py:233-256,362-370): out[e, n, r] = s * sum over expert e's rows of g[row, n] * low[row, r]."""
+    g = np.asarray(g, dtype=np.float32)
+    low = np.asarray(low, dtype=np.float32)
+    offs = np.asarray(offsets)
+    out = np.zeros((offs.size, g.shape[1], low.shape[1]), dtype=np.float32)
+    for e, start, end in _segments(offs):
+        out[e] = np.float32(scaling) * (g[start:end].T @ low[start:end])
+    return out
