@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""Benchmark of the grouped MoE-LoRA expert layer, forward + backward, on B200s (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl meep2b|reference] [--config qwen3_30b|...]
+
+A step is one forward + backward of the routed layer (routing, gather, gate/up with SwiGLU, down, un-permute and
+the whole backward, adapters' gradients included) over one batch of T tokens of BASELINE config 2 (Qwen3-30B-A3B:
+T=16384, hidden 2048, moe_intermediate 768, 128 experts, top-8, LoRA r=16 alpha 32, bf16). Synthetic seeded data
+(router logits ~N(0,1), stacks ~N(0,0.02)); every per-step tensor is far larger than the 126 MB L2, so no flush.
+At N>1 each rank runs its own batch (weak scaling) and the LoRA gradients are averaged with one NCCL all-reduce
+per step (the reference's DDP exchange). Rank 0 prints one JSON line.
+
+--impl reference times the reference path's CPU implementation (the numpy oracle port of _moe._routed_forward,
+float32, all host threads) on a bounded sample of the same workload; rank 0 alone runs it.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "qwen3_30b": dict(tokens=16384, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
+    "mixtral": dict(tokens=8192, hidden=4096, inter=14336, experts=8, top_k=2, rank=16, alpha=32),
+    "qwen3_235b_fp8": dict(tokens=32768, hidden=4096, inter=1536, experts=128, top_k=8, rank=16, alpha=32, zipf=1.1),
+    "small": dict(tokens=2048, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
+    "half": dict(tokens=8192, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
+}
+METRIC = "MoE-LoRA layer fwd+bwd tokens/s"
+# DRAM bytes (read + write) of one launch of the grouped product, from the ncu capture summarised in
+# profiles/grouped_gemm_qwen3_30b.md, scaled to the full workload there; None until captured.
+GEMM_TRAFFIC_BYTES_PER_STEP = None
+
+
+def flop_per_token(c):
+    """k [12 H I + 6 r (2H + 3I)]: frozen base forward + input gradient, LoRA forward, input gradient and dA/dB."""
+    return c["top_k"] * (12 * c["hidden"] * c["inter"] + 6 * c["rank"] * (2 * c["hidden"] + 3 * c["inter"]))
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return float(p["bf16_tflops_sustained"]), float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class GemmTimer:
+    """CUDA events around every grouped-product launch, on the launching stream; totals over the timed steps."""
+
+    def __init__(self):
+        import torch
+
+        self.torch = torch
+        self.pending = []
+        self.active = False
+
+    def before(self, x):
+        if self.active:
+            ev = self.torch.cuda.Event(enable_timing=True)
+            ev.record(self.torch.cuda.current_stream(x.device))
+            self._start = ev
+
+    def after(self, x, flops):
+        if self.active:
+            ev = self.torch.cuda.Event(enable_timing=True)
+            ev.record(self.torch.cuda.current_stream(x.device))
+            self.pending.append((self._start, ev, flops))
+
+    def totals(self):
+        ms = sum(a.elapsed_time(b) for a, b, _ in self.pending)
+        return ms, sum(f for _, _, f in self.pending), len(self.pending)
+
+
+def setup_dist():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def make_layer(c, device, seed):
+    import torch
+
+    import meepsquared_b200 as mb  # noqa: F401
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    T, H, I, E, k, r = c["tokens"], c["hidden"], c["inter"], c["experts"], c["top_k"], c["rank"]
+    logits = torch.randn(T, E, device=device, generator=g)
+    if c.get("zipf"):
+        order = torch.randperm(E, device=device, generator=g)
+        p = torch.arange(1, E + 1, device=device, dtype=torch.float32) ** (-c["zipf"])
+        logits = logits + torch.log(p / p.sum())[order]
+    probs = torch.softmax(logits, dim=-1, dtype=torch.float32)
+    w, idx = torch.topk(probs, k, dim=-1)
+    w = w / w.sum(dim=-1, keepdim=True)
+
+    class Experts(torch.nn.Module):
+        pass
+
+    ex = Experts()
+    ex.num_experts, ex.has_gate, ex.has_bias, ex.is_transposed = E, True, False, False
+    ex.gate_up_proj = (torch.randn(E, 2 * I, H, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    ex.down_proj = (torch.randn(E, H, I, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    bound1, bound2 = 1.0 / H ** 0.5, 1.0 / I ** 0.5
+    lora = {
+        "lhs1": (torch.randn(E, 2 * I, r, device=device, generator=g) * 0.01).to(torch.bfloat16),
+        "rhs1": ((torch.rand(E, r, H, device=device, generator=g) * 2 - 1) * bound1).to(torch.bfloat16),
+        "lhs2": (torch.randn(E, H, r, device=device, generator=g) * 0.01).to(torch.bfloat16),
+        "rhs2": ((torch.rand(E, r, I, device=device, generator=g) * 2 - 1) * bound2).to(torch.bfloat16),
+    }
+    for t in lora.values():
+        t.requires_grad_()
+    hidden = torch.randn(T, H, device=device, generator=g).to(torch.bfloat16)
+    grad = torch.randn(T, H, device=device, generator=g).to(torch.bfloat16)
+    return ex, lora, hidden, idx, w, grad
+
+
+def run_meep2b(a):
+    import torch
+    import torch.distributed as dist
+
+    import meepsquared_b200 as mb
+    from meepsquared_b200 import _grouped, ddp
+
+    world, rank, local = setup_dist()
+    c = CONFIGS[a.config]
+    device = torch.device("cuda", local)
+    ex, lora, hidden, idx, w, grad = make_layer(c, device, seed=1234 + rank)
+    s = c["alpha"] / c["rank"]
+    factors = {"gate_up_proj": (lora["lhs1"], lora["rhs1"], s), "down_proj": (lora["lhs2"], lora["rhs2"], s)}
+    bucket = ddp.LoraGradBucket(list(lora.values()))
+    hidden_leaf = hidden.clone().requires_grad_()
+
+    def step(h, ids, wts, g):
+        bucket.zero()
+        out = mb.routed_forward(ex, h, ids, wts, factors)
+        out.backward(g)
+        bucket.reduce()
+        return out
+
+    def sync():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize(device)
+
+    for _ in range(a.warmup):
+        step(hidden_leaf, idx, w, grad)
+    sync()
+
+    timer = GemmTimer()
+    _grouped.set_launch_observer(timer)
+    timer.active = True
+    stream = torch.cuda.current_stream(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        sync()
+        start.record(stream)
+        for _ in range(a.steps):
+            step(hidden_leaf, idx, w, grad)
+        stop.record(stream)
+        sync()
+    timer.active = False
+    _grouped.set_launch_observer(None)
+    ms = start.elapsed_time(stop)
+    gemm_ms, gemm_flops, gemm_launches = timer.totals()
+
+    # end to end through the public API with host buffers: pinned host inputs copied in, results read back
+    h_host = hidden.cpu().pin_memory()
+    i_host = idx.cpu().pin_memory()
+    w_host = w.cpu().pin_memory()
+    g_host = grad.cpu().pin_memory()
+    out_host = torch.empty(hidden.shape, dtype=torch.bfloat16).pin_memory()
+    gh_host = torch.empty(hidden.shape, dtype=torch.bfloat16).pin_memory()
+    lg_host = torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory()
+
+    def e2e_step():
+        h = h_host.to(device, non_blocking=True).requires_grad_()
+        ids = i_host.to(device, non_blocking=True)
+        wts = w_host.to(device, non_blocking=True)
+        g = g_host.to(device, non_blocking=True)
+        out = step(h, ids, wts, g)
+        out_host.copy_(out.detach(), non_blocking=True)
+        gh_host.copy_(h.grad, non_blocking=True)
+        lg_host.copy_(bucket.flat, non_blocking=True)
+
+    for _ in range(max(2, a.warmup // 2)):
+        e2e_step()
+    sync()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(3, a.steps // 2)
+    sync()
+    e_start.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e_stop.record(stream)
+    sync()
+    e_ms = e_start.elapsed_time(e_stop)
+
+    times = torch.tensor([ms, e_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e_ms = times.tolist()
+    T = c["tokens"]
+    value = world * T * a.steps / (ms / 1e3)
+    e_value = world * T * e_steps / (e_ms / 1e3)
+    sustained, burst, hbm, peak_kind = peaks()
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    layer_tflops = flop_per_token(c) * value / world / 1e12
+    h2d = hidden.numel() * 2 + idx.numel() * idx.element_size() + w.numel() * 4 + grad.numel() * 2
+    d2h = hidden.numel() * 2 * 2 + bucket.flat.numel() * bucket.flat.element_size()
+    launches_per_step = 16  # route 3, gather, tile map, 2 products, un-permute, its backward, 2 products, 4 reductions, gather backward
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE config shapes)",
+        "config": {"workload": a.config + " routed MoE-LoRA layer fwd+bwd", **c, "tokens_per_gpu": T,
+                   "parallelism": f"dp{world}", "l2": "per-step tensors >> 126 MB L2, no flush"},
+        "tensor_tflops_layer": round(layer_tflops, 1),
+        "frac_of_bf16_peak_layer": round(layer_tflops / sustained, 4),
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm (tcgen05), all product launches of the step",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": sustained,
+                     "unit": "TFLOP/s", "frac": round(achieved / sustained, 4) if achieved else None,
+                     "peak_kind": f"bf16 sustained, {peak_kind}",
+                     "launches_timed": gemm_launches, "gemm_ms_per_step": round(gemm_ms / a.steps, 4),
+                     "traffic": GEMM_TRAFFIC_BYTES_PER_STEP},
+        "e2e": {"value": round(e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": launches_per_step * a.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(c, a.cpu_tokens)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def cpu_baseline(c, tokens):
+    """The oracle port (numpy float32, the reference path's algorithm) on `tokens` tokens of the workload."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import layer_inputs
+    from oracle import layer as olayer
+
+    cfg = {k: v for k, v in c.items()}
+    cfg["tokens"] = tokens
+    inp = layer_inputs.layer(**cfg)
+    fac = {"gate_up_proj": (inp["gate_up_lhs"].numpy(), inp["gate_up_rhs"].numpy(), inp["scaling"]),
+           "down_proj": (inp["down_lhs"].numpy(), inp["down_rhs"].numpy(), inp["scaling"])}
+    args = (inp["hidden"].numpy(), inp["top_k_index"].numpy(), inp["top_k_weights"].numpy(), inp["gate_up"].numpy(),
+            inp["down"].numpy(), fac)
+
+    def once():
+        out, saved = olayer.forward(*args)
+        olayer.backward(inp["grad"].numpy(), saved, inp["gate_up"].numpy(), inp["down"].numpy(), fac)
+
+    once()
+    reps = []
+    t_end = time.perf_counter() + 10.0
+    while len(reps) < 3 or (time.perf_counter() < t_end and len(reps) < 20):
+        t0 = time.perf_counter()
+        once()
+        reps.append(time.perf_counter() - t0)
+    sec = statistics.median(reps)
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        cores = os.cpu_count()
+    del np
+    return {"value": round(tokens / sec, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{tokens} tokens of the workload (all {c['experts']} experts), fwd+bwd, float32 numpy, "
+                      f"median of {len(reps)}"}
+
+
+def run_reference(a):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    c = CONFIGS[a.config]
+    cb = cpu_baseline(c, a.cpu_tokens)
+    value = cb["value"]
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": round(1e3 * a.cpu_tokens / value, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config shapes)", "impl": "reference",
+        "config": {"workload": a.config + " routed MoE-LoRA layer fwd+bwd", **c},
+        "cpu_baseline": cb, "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                    "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="meep2b", choices=["meep2b", "reference"])
+    ap.add_argument("--config", default="qwen3_30b", choices=sorted(CONFIGS))
+    ap.add_argument("--cpu-tokens", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    if a.warmup < 3 and a.impl == "meep2b":
+        a.warmup = 3
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_meep2b(a)
+
+
+if __name__ == "__main__":
+    main()

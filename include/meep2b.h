@@ -1,0 +1,176 @@
+/* libmeep2b: B200 (sm_100a) kernels of the grouped MoE-LoRA expert layer, behind a plain C ABI.
+ *
+ * Every entry point takes device pointers, sizes and a CUDA stream (a cudaStream_t passed as void*), launches
+ * asynchronously on that stream, allocates no device memory (buffers, including workspaces, come from the caller)
+ * and returns a status: 0 on success, one of MEEP2B_ERR_* otherwise.  The Python host layer
+ * (meepsquared_b200/_grouped.py, _moe.py, _fp8.py, _nf4.py) maps those statuses onto the reference's exceptions.
+ *
+ * Element types: "bf16" buffers hold IEEE bfloat16, "e4m3" buffers OCP FP8 E4M3 codes, one byte each.
+ * Citations are file:line within thinkube/meepsquared (src/meepsquared/...).
+ */
+#ifndef MEEP2B_H
+#define MEEP2B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum meep2b_status {
+  MEEP2B_OK = 0,
+  MEEP2B_ERR_SHAPE = 1,       /* sizes that do not fit together: ValueError in the host layer */
+  MEEP2B_ERR_DTYPE = 2,       /* an element type the entry point does not take: TypeError */
+  MEEP2B_ERR_LAUNCH = 3,      /* a CUDA runtime or driver call failed: RuntimeError */
+  MEEP2B_ERR_TIMEOUT = 4,     /* a bounded device-side wait ran out (see meep2b_device_error): RuntimeError */
+  MEEP2B_ERR_UNSUPPORTED = 5, /* a combination the kernels do not implement: NotImplementedError */
+  MEEP2B_ERR_ALIGN = 6,       /* a pointer or row stride that TMA cannot address (16-byte rule): ValueError */
+  MEEP2B_ERR_DEVICE = 7       /* no compute capability 10.0 GPU: RuntimeError */
+};
+
+enum meep2b_dtype { MEEP2B_F32 = 0, MEEP2B_BF16 = 1, MEEP2B_E4M3 = 2 };
+
+enum meep2b_epilogue {
+  MEEP2B_EPI_PLAIN = 0,   /* out = scale_e * (x W^T) + s (x A^T) B^T + bias_e                                   */
+  MEEP2B_EPI_SWIGLU = 1,  /* gate_up forward: aux = pre-activation (rows, n), out = silu(gate) * up (rows, n/2)  */
+  MEEP2B_EPI_DSWIGLU = 2  /* down backward: the product is dh (rows, n); aux = pre-activation (rows, 2n) read;
+                             out = d(gate, up) (rows, 2n)                                                      */
+};
+
+/* ---------------------------------------------------------------------------------------------- library */
+
+/* Version string of the library. */
+const char* meep2b_version(void);
+/* Message for a status code. */
+const char* meep2b_status_string(int status);
+/* MEEP2B_OK when `device` is a compute capability 10.0 GPU the kernels run on; replaces _grouped.available()
+ * (_grouped.py:259-261) and the capability test of _grouped.wanted() (_grouped.py:57-67). */
+int meep2b_device_ok(int device);
+/* Reads and clears the device's error word, where a kernel records a bounded wait that ran out. Synchronous. */
+int meep2b_device_error(int device, int* code);
+/* Number of streaming multiprocessors of the device (the persistent kernels' grid). */
+int meep2b_sm_count(int device, int* count);
+
+/* ---------------------------------------------------------------------------------------------- routing */
+
+/* Workspace bytes meep2b_route needs for `assignments` = tokens * top_k routed rows over `experts`. */
+size_t meep2b_route_workspace_bytes(int64_t assignments, int32_t experts);
+
+/* The permutation of _moe._routed_forward (_moe.py:77-86): a stable counting sort of the flat expert ids.
+ * perm[i] = flat index of the i-th assignment in expert order (ties keep their flat order; ids >= experts, and
+ * negative ids, are sentinels and sort last), expert_ids_g[i] = min(id, experts - 1), offsets[e] = inclusive
+ * cumulative row count of experts 0..e (int32, sentinels not counted), inverse[perm[i]] = i (_moe.py:124-125).
+ * expert_ids_g and inverse may be NULL. */
+int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
+                 int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* The gather of _moe.py:80-81,87: selected[i] = hidden[perm[i] / top_k] (bf16 rows of hidden_dim), zero for the
+ * sentinel rows i >= offsets[experts-1]; weights_g[i] = weights[perm[i]] (weights_dtype F32 or BF16, same type
+ * out; both may be NULL). */
+int meep2b_gather(const void* hidden, int64_t tokens, int64_t hidden_dim, int32_t top_k, const int64_t* perm,
+                  const int32_t* offsets, int32_t experts, const void* weights, int32_t weights_dtype,
+                  void* weights_g, void* selected, void* stream);
+
+/* The weighted un-permute of _moe.py:123-126: out[t] = bf16(sum_j y[r] * w_g[r]), r = inverse[t*top_k + j],
+ * the sum in float32 over j in order; rows r >= offsets[experts-1] (sentinels) count as zero. weights_g NULL
+ * means weight 1 (the backward of the gather, _moe.py:80). */
+int meep2b_unpermute(const void* y, const int64_t* inverse, const void* weights_g, int32_t weights_dtype,
+                     const int32_t* offsets, int32_t experts, int64_t tokens, int32_t top_k, int64_t hidden_dim,
+                     void* out, void* stream);
+
+/* Backward of the un-permute (autograd of _moe.py:123-126): grad_y[i] = bf16(grad_out[perm[i]/top_k] * w_g[i]),
+ * grad_weights[perm[i]] = sum_h grad_out[perm[i]/top_k][h] * y[i][h] (float32); sentinel rows give zeros. */
+int meep2b_unpermute_backward(const void* grad_out, const void* y, const int64_t* perm, const void* weights_g,
+                              int32_t weights_dtype, const int32_t* offsets, int32_t experts, int64_t assignments,
+                              int32_t top_k, int64_t hidden_dim, void* grad_y, float* grad_weights, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- tile map */
+
+/* _grouped.tile_map (_grouped.py:88-103) on the device: tile_expert / tile_row get max_tiles(rows, experts,
+ * block_m) = rows / block_m + experts entries (spares hold the last expert), *tiles the real count. */
+int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32_t block_m, int32_t* tile_expert,
+                    int32_t* tile_row, int32_t* tiles, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- grouped product */
+
+/* One launch of the grouped product, the replacement of _grouped._launch (_grouped.py:313-345) and of
+ * _grouped_gemm_kernel (_grouped.py:121-221): for each tile of 128 rows of one expert e, over the expert's rows
+ *   acc  = x W_e^T           (tcgen05 MMA, float32 accumulator in tensor memory)
+ *   low  = x P_e^T           (the rank-16 panel, in the same MMA: the panel rows ride along W's rows)
+ *   acc += (s low / scale_e) U_e^T   (MMAs of depth 16; the panel as two bf16 planes, hi + lo)
+ *   out  = epilogue(scale_e acc + bias_e)
+ * Layouts (b_mn == 0, "K-major"): weight (experts, n, k), panel (experts, 16, k), up (experts, n, 16).
+ *         (b_mn == 1, "MN-major"): weight (experts, k, n), panel (experts, k, 64) [columns 16..63 zero],
+ *                                  up (experts, 16, n).
+ * The rank is padded to 16 with zeros (_grouped.py:275-282). x is (rows, k) with row stride ldx; rows of one
+ * expert are contiguous, offsets[e] is the end of expert e's rows (int32, inclusive cumsum). tile_expert /
+ * tile_row / tiles come from meep2b_tile_map with block_m = 128. low (rows, 16) receives bf16(x P_e^T) when not
+ * NULL (kept for the backward pass, _grouped.py:212-214). */
+typedef struct meep2b_product {
+  const void* x;
+  int64_t rows, k, ldx;
+  const void* weight;
+  int32_t weight_dtype; /* MEEP2B_BF16 */
+  int32_t experts;
+  int64_t n;
+  int32_t b_mn;
+  const float* scale;   /* (experts,) per-expert scale of the stack, or NULL */
+  const void* panel;    /* NULL: no adapters */
+  const void* up;
+  float scaling;        /* s = alpha / r */
+  const void* bias;     /* (experts, n) bf16 or NULL */
+  const int32_t* offsets;
+  const int32_t* tile_expert;
+  const int32_t* tile_row;
+  const int32_t* tiles;
+  int64_t max_tiles;
+  void* out;
+  int64_t ldo;
+  void* low;            /* (rows, 16) bf16 or NULL */
+  int32_t epilogue;     /* enum meep2b_epilogue */
+  void* aux;            /* SWIGLU: pre-activation out (rows, n); DSWIGLU: pre-activation in (rows, 2n) */
+  int32_t sm_limit;     /* 0: one CTA per SM */
+} meep2b_product;
+
+int meep2b_grouped_product(const meep2b_product* p, void* stream);
+
+/* _grouped._reduce / _grouped_reduce_kernel (_grouped.py:233-256,362-370): the adapters' gradients,
+ * out[e, j, r] = bf16(scaling * sum over expert e's rows of g[row, j] * low[row, r]) for r < 16; g (rows, n) bf16
+ * with row stride ldg, low (rows, 16) bf16, out (experts, n, 16) bf16. */
+int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int64_t ldg, const void* low,
+                          const int32_t* offsets, int32_t experts, float scaling, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- quantised stacks */
+
+/* _fp8.quantize_stack (_fp8.py:122-128): scale[e] = max(amax_e, 1e-12) / 448, codes = e4m3(w / scale[e]) (round
+ * to nearest even). w (experts, per_expert) in bf16 or f32. workspace: experts floats. */
+int meep2b_fp8_stack_quantize(const void* w, int32_t dtype, int32_t experts, int64_t per_expert, uint8_t* codes,
+                              float* scale, float* workspace, void* stream);
+/* _fp8.dequantize_stack (_fp8.py:131-134, _grouped_scale_kernel :69-79): out = bf16(f32(codes) * scale[e]). */
+int meep2b_fp8_stack_dequantize(const uint8_t* codes, const float* scale, int32_t experts, int64_t per_expert,
+                                void* out, void* stream);
+/* axolotl quantize.dequantize_fp8 (_vendor/axolotl/quantize.py:131-157), bf16 out, for `matrices` stacked
+ * (rows, cols) matrices each with an (sr, sc) float32 scale grid: out = bf16(bf16(w) * bf16(scale)), blocks of
+ * ceil(rows/sr) x ceil(cols/sc). */
+int meep2b_fp8_block_dequantize(const uint8_t* codes, int64_t matrices, int64_t rows, int64_t cols,
+                                const float* scale_inv, int32_t sr, int32_t sc, void* out, void* stream);
+/* axolotl quantize.quantize_fp8 (quantize.py:238-263) with a 2-D scale grid, per stacked matrix:
+ * scale = max(amax_block, 1e-12) / 448, codes = e4m3(clamp(w / scale, +-448)); w bf16 or f32. */
+int meep2b_fp8_block_quantize(const void* w, int32_t dtype, int64_t matrices, int64_t rows, int64_t cols,
+                              int32_t sr, int32_t sc, uint8_t* codes, float* scale_inv, void* stream);
+/* The NF4 double dequantisation of axolotl quantize._ctypes_nf4_dequant (quantize.py:52-101), which calls
+ * bitsandbytes' cdequantize_blockwise_fp32 then `+= offset` then cdequantize_blockwise_bf16_nf4:
+ * absmax_out[i] = code2[absmax[i]] * absmax2[i / blocksize2] + offset[0] (two float32 roundings);
+ * out[j] = bf16(NF4[code_j] * absmax_out[j / blocksize]), two codes per byte, the first in the high nibble.
+ * n = number of weights (even); absmax_out: n / blocksize floats (caller-provided workspace). */
+int meep2b_nf4_dequantize(const uint8_t* packed, const uint8_t* absmax, const float* absmax2, const float* code2,
+                          const float* offset, int32_t blocksize, int32_t blocksize2, int64_t n, float* absmax_out,
+                          void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEEP2B_H */

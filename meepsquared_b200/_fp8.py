@@ -1,0 +1,114 @@
+"""Expert stacks held as FP8 (e4m3), on the B200: the stack functions of meepsquared._fp8 and the block FP8 of the
+vendored axolotl quantize module, computed by libmeep2b (csrc/quant.cu).
+
+* ``quantize_stack`` / ``dequantize_stack``: one scale per expert (``meepsquared/_fp8.py:122-134``);
+* ``quantize_blocks`` / ``dequantize_blocks``: a 2-D grid of scales per matrix, 128 x 128 blocks for sizes that are
+  multiples of 128 (``meepsquared/_vendor/axolotl/quantize.py:131-157, 238-263``), here for a stack of matrices;
+* ``convert_stacks``: every frozen 3-D stack of an experts module as FP8 with its scale as ``<name>_scale_inv``
+  (``meepsquared/_fp8.py:167-186``).
+"""
+
+import torch
+from torch import nn
+
+from . import _lib
+
+E4M3_MAX = 448.0
+STACK_SCALE = "_scale_inv"
+
+
+def _cuda(t, what):
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} runs on a CUDA GPU; got a tensor on {t.device}")
+    _lib.load()
+
+
+def _src(weight):
+    w = weight.detach().contiguous()
+    if w.dtype == torch.bfloat16:
+        return w, _lib.BF16
+    if w.dtype == torch.float32:
+        return w, _lib.F32
+    return w.float(), _lib.F32
+
+
+def quantize_stack(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """A stack (experts, ...) as e4m3 with one scale per expert: weight ~= fp8 * scale[expert]."""
+    _cuda(weight, "quantize_stack")
+    w, dtype = _src(weight)
+    experts = w.shape[0]
+    per = w[0].numel()
+    codes = torch.empty(w.shape, device=w.device, dtype=torch.float8_e4m3fn)
+    scale = torch.empty(experts, device=w.device, dtype=torch.float32)
+    work = torch.empty(experts, device=w.device, dtype=torch.float32)
+    _lib.check(_lib.load().meep2b_fp8_stack_quantize(_lib.ptr(w), dtype, experts, per, _lib.ptr(codes),
+                                                     _lib.ptr(scale), _lib.ptr(work), _lib.stream_of(w)),
+               "meep2b_fp8_stack_quantize")
+    return codes, scale
+
+
+def dequantize_stack(weight8: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """The stack back in bf16 for one product: bf16(float32(w8) * scale[expert])."""
+    _cuda(weight8, "dequantize_stack")
+    if dtype != torch.bfloat16:
+        raise TypeError(f"dequantize_stack produces bf16, not {dtype}")
+    w8 = weight8.contiguous()
+    out = torch.empty(w8.shape, device=w8.device, dtype=torch.bfloat16)
+    _lib.check(_lib.load().meep2b_fp8_stack_dequantize(_lib.ptr(w8), _lib.ptr(scale.float().contiguous()),
+                                                       w8.shape[0], w8[0].numel(), _lib.ptr(out),
+                                                       _lib.stream_of(w8)), "meep2b_fp8_stack_dequantize")
+    return out
+
+
+def _as_matrices(t):
+    return t.reshape(-1, t.shape[-2], t.shape[-1])
+
+
+def quantize_blocks(weight: torch.Tensor, grid=None, block: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """Each (rows, cols) matrix of weight (..., rows, cols) as e4m3 with an (sr, sc) grid of float32 scales.
+
+    grid defaults to (ceil(rows/128), ceil(cols/128)); blocks are (ceil(rows/sr), ceil(cols/sc)) as in the
+    reference's quantize_fp8. Returns (codes like weight, scale_inv (..., sr, sc)).
+    """
+    _cuda(weight, "quantize_blocks")
+    w, dtype = _src(weight)
+    rows, cols = w.shape[-2], w.shape[-1]
+    sr, sc = grid if grid is not None else (-(-rows // block), -(-cols // block))
+    m = _as_matrices(w).shape[0]
+    codes = torch.empty(w.shape, device=w.device, dtype=torch.float8_e4m3fn)
+    scale = torch.empty((*w.shape[:-2], sr, sc), device=w.device, dtype=torch.float32)
+    _lib.check(_lib.load().meep2b_fp8_block_quantize(_lib.ptr(w), dtype, m, rows, cols, sr, sc, _lib.ptr(codes),
+                                                     _lib.ptr(scale), _lib.stream_of(w)), "meep2b_fp8_block_quantize")
+    return codes, scale
+
+
+def dequantize_blocks(codes: torch.Tensor, scale_inv: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(w8) * bf16(scale)) per block, the reference's dequantize_fp8 with dtype bf16."""
+    _cuda(codes, "dequantize_blocks")
+    c = codes.contiguous()
+    rows, cols = c.shape[-2], c.shape[-1]
+    sr, sc = scale_inv.shape[-2], scale_inv.shape[-1]
+    out = torch.empty(c.shape, device=c.device, dtype=torch.bfloat16)
+    _lib.check(_lib.load().meep2b_fp8_block_dequantize(_lib.ptr(c), _as_matrices(c).shape[0], rows, cols,
+                                                       _lib.ptr(scale_inv.float().contiguous()), sr, sc,
+                                                       _lib.ptr(out), _lib.stream_of(c)),
+               "meep2b_fp8_block_dequantize")
+    return out
+
+
+def convert_stacks(experts) -> int:
+    """Every frozen stack of an experts module held as FP8, its scale as <name>_scale_inv; returns how many."""
+    converted = 0
+    for name, parameter in list(experts.named_parameters(recurse=False)):
+        if parameter.dim() != 3 or parameter.requires_grad or not parameter.is_floating_point():
+            continue
+        if parameter.dtype == torch.float8_e4m3fn and hasattr(experts, name + STACK_SCALE):
+            converted += 1
+            continue
+        weight8, scale = quantize_stack(parameter.detach())
+        setattr(experts, name, nn.Parameter(weight8, requires_grad=False))
+        experts.register_buffer(name + STACK_SCALE, scale)
+        converted += 1
+    if converted:
+        experts._meepsquared_fp8 = True
+    return converted

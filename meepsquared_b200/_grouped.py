@@ -1,0 +1,382 @@
+"""The experts' products with their LoRA adapters, one launch each, on a B200: the drop-in for meepsquared._grouped.
+
+Same operator API as ``meepsquared/_grouped.py`` (``lora_linear`` :408-417, ``grouped_linear`` :348-359,
+``tile_map`` :88-103, ``max_tiles`` :83-85, ``wanted`` :57-67, ``fp8_products`` :70-80, ``available``
+:259-261, ``reference`` / ``reference_lora`` :420-444, the constants), same argument meaning and errors. The rows
+of x are sorted by expert, offsets[e] is the end of expert e's rows (int32, on the device), and for every expert
+
+    out_e = scale_e * x_e @ W_e^T + s * (x_e @ A_e^T) @ B_e^T + bias_e
+
+with the stack W as (experts, out, in), or (experts, in, out) when is_transposed, addressed through its strides
+(either memory order is read in place). The computation is libmeep2b's persistent tcgen05 GEMM
+(csrc/grouped_gemm.cu): TMA-fed, accumulators in tensor memory, the rank panel x_e @ A_e^T computed by the same
+MMA as the product, the adapter's second factor applied by one more MMA of depth 16. The backward pass is the
+same kernel with the stack read the other way round and the adapters' roles swapped, plus one reduction kernel
+per adapter (csrc/reduce.cu). The frozen stack gets no gradient. There is no other implementation: without the
+library or a compute capability 10.0 GPU the functions raise.
+"""
+
+import os
+
+import torch
+
+from . import _lib
+
+BLOCK_M = 128  # rows per tile: the M of the tcgen05 MMA
+RANK_MULTIPLE = 16  # the rank is padded to one MMA depth
+# PyTorch has grouped matmul kernels of its own for these (the reference's constant, kept for the API)
+TORCH_HAS_GROUPED_MM = (9, 10)
+
+
+def available() -> bool:
+    """Whether the kernels can run here: libmeep2b loads and the current CUDA GPU has compute capability 10.0."""
+    if not torch.cuda.is_available() or not _lib.loaded():
+        return False
+    return _lib.device_ok(torch.cuda.current_device())
+
+
+def wanted(device) -> bool:
+    """Whether the kernels compute the experts on `device`: a compute capability 10.0 GPU with libmeep2b loaded.
+
+    MEEPSQUARED_GROUPED_KERNEL=0 or 1 overrides the decision, as in the reference.
+    """
+    forced = os.environ.get("MEEPSQUARED_GROUPED_KERNEL")
+    if forced in ("0", "1"):
+        return forced == "1"
+    if device.type != "cuda" or not torch.cuda.is_available() or not _lib.loaded():
+        return False
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return _lib.device_ok(index)
+
+
+def fp8_products(device) -> bool:
+    """Whether an FP8 stack's products run on the FP8 tensor cores, activations quantized per row: off unless
+    MEEPSQUARED_FP8_PRODUCTS=1, as in the reference."""
+    return os.environ.get("MEEPSQUARED_FP8_PRODUCTS") == "1"
+
+
+def max_tiles(rows: int, experts: int, block_m: int = BLOCK_M) -> int:
+    """An upper bound on the tiles: every expert's last tile may be partial."""
+    return rows // block_m + experts
+
+
+def _require(t: torch.Tensor, what: str):
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} runs on a CUDA GPU (compute capability 10.0); got a tensor on {t.device}")
+    _lib.load()
+
+
+def tile_map(offsets: torch.Tensor, rows: int, block_m: int = BLOCK_M):
+    """(tile_expert, tile_row, tiles) for `rows` rows sorted by expert, built on the device by one kernel.
+
+    offsets[e] is the end of expert e's rows (int32). The two int32 arrays have max_tiles entries; tiles, a 0-d
+    int32 tensor on the device, says how many are real. Entries beyond that hold the last expert.
+    """
+    _require(offsets, "tile_map")
+    offsets = offsets.to(torch.int32).contiguous()
+    experts = offsets.numel()
+    n = max_tiles(rows, experts, block_m)
+    tile_expert = torch.empty(n, dtype=torch.int32, device=offsets.device)
+    tile_row = torch.empty(n, dtype=torch.int32, device=offsets.device)
+    tiles = torch.empty((), dtype=torch.int32, device=offsets.device)
+    _lib.check(_lib.load().meep2b_tile_map(_lib.ptr(offsets), experts, rows, block_m, _lib.ptr(tile_expert),
+                                           _lib.ptr(tile_row), _lib.ptr(tiles), _lib.stream_of(offsets)),
+               "meep2b_tile_map")
+    return tile_expert, tile_row, tiles
+
+
+# ------------------------------------------------------------------------------------------------ layouts
+
+def _stack_strides(weight: torch.Tensor, K: int, is_transposed: bool) -> int:
+    """N of a stack addressed as (k, n); the reference's ValueErrors for a mismatch (_grouped.py:264-272)."""
+    if is_transposed:
+        if weight.shape[1] != K:
+            raise ValueError(f"a transposed stack (experts, in, out) with in={weight.shape[1]} does not take x with {K} columns")
+        return weight.shape[2]
+    if weight.shape[2] != K:
+        raise ValueError(f"a stack (experts, out, in) with in={weight.shape[2]} does not take x with {K} columns")
+    return weight.shape[1]
+
+
+def _stack_memory(weight: torch.Tensor, k_contiguous_layout: bool):
+    """The stack as the kernel reads it: (tensor, b_mn).
+
+    The product contracts over k. With b_mn=0 the kernel takes (experts, n, k) with k contiguous, with b_mn=1
+    (experts, k, n) with n contiguous. `k_contiguous_layout` says whether the logical layout is (experts, n, k).
+    A stack stored in the other order is read in place with the other mode; any other strides are copied.
+    """
+    if k_contiguous_layout:  # logical (E, n, k)
+        if weight.is_contiguous():
+            return weight, 0
+        t = weight.transpose(1, 2)
+        if t.is_contiguous():
+            return t, 1
+        return weight.contiguous(), 0
+    if weight.is_contiguous():  # logical (E, k, n)
+        return weight, 1
+    t = weight.transpose(1, 2)
+    if t.is_contiguous():
+        return t, 0
+    return weight.contiguous(), 1
+
+
+def _rank_rows(factor: torch.Tensor) -> torch.Tensor:
+    """(E, r, D) -> (E, 16, D) bf16 contiguous, zero rows past the rank."""
+    e, r, d = factor.shape
+    if r == RANK_MULTIPLE and factor.dtype == torch.bfloat16 and factor.is_contiguous():
+        return factor
+    out = factor.new_zeros((e, RANK_MULTIPLE, d), dtype=torch.bfloat16)
+    out[:, :r] = factor
+    return out
+
+
+def _rank_cols(factor: torch.Tensor, width: int) -> torch.Tensor:
+    """(E, D, r) -> (E, D, width) bf16 contiguous, zero columns past the rank (width 16 or 64)."""
+    e, d, r = factor.shape
+    if r == width and factor.dtype == torch.bfloat16 and factor.is_contiguous():
+        return factor
+    out = factor.new_zeros((e, d, width), dtype=torch.bfloat16)
+    out[:, :, :r] = factor
+    return out
+
+
+class _Adapters:
+    """PEFT's factors (lhs, rhs) in the kernel's layouts, for the forward product and for the backward one.
+
+    delta = lhs @ rhs in the layout of the stack (reference _grouped.py:285-310): for a stack (E, out, in)
+    lhs is (E, out, r) and rhs (E, r, in); for (E, in, out) lhs is (E, in, r) and rhs (E, r, out).
+    A product computes rows @ F1 (the rank panel, rows x r) and then panel @ F2, F1 (E, k, r) and F2 (E, r, n).
+    The kernel takes F1 as its panel P and F2 as its up factor U: with b_mn=0 P is (E, 16, k) and U (E, n, 16),
+    with b_mn=1 P is (E, k, 64) and U (E, 16, n); the rank is padded with zeros.
+    """
+
+    def __init__(self, lhs, rhs, is_transposed):
+        self.rank = lhs.shape[2]
+        if self.rank > RANK_MULTIPLE:
+            raise NotImplementedError(f"LoRA rank {self.rank}: the kernels take ranks up to {RANK_MULTIPLE}")
+        self.lhs, self.rhs, self.is_transposed = lhs, rhs, is_transposed
+        self._cache = {}
+
+    def factors(self, backward: bool):
+        """(F1, F2) of the forward product or of the input-gradient product."""
+        lhs, rhs = self.lhs, self.rhs
+        if not self.is_transposed:  # x @ delta^T = (x @ rhs^T) @ lhs^T; g @ delta = (g @ lhs) @ rhs
+            return (lhs, rhs) if backward else (rhs.transpose(1, 2), lhs.transpose(1, 2))
+        # x @ delta = (x @ lhs) @ rhs; g @ delta^T = (g @ rhs^T) @ lhs^T
+        return (rhs.transpose(1, 2), lhs.transpose(1, 2)) if backward else (lhs, rhs)
+
+    def operands(self, b_mn: int, backward: bool):
+        key = (b_mn, backward)
+        if key not in self._cache:
+            f1, f2 = self.factors(backward)
+            if b_mn == 0:
+                self._cache[key] = (_rank_rows(f1.transpose(1, 2)), _rank_cols(f2.transpose(1, 2), 16))
+            else:
+                self._cache[key] = (_rank_cols(f1, 64), _rank_rows(f2))
+        return self._cache[key]
+
+
+def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward=False,
+            tiles=None, epilogue=_lib.EPI_PLAIN, aux=None, out=None):
+    """One launch of the grouped product; returns (out, low). The reference's _launch (_grouped.py:313-345).
+
+    k_contiguous_layout: whether the stack is logically (experts, n, k) for this product.
+    """
+    rows, K = x.shape
+    stack, b_mn = _stack_memory(weight, k_contiguous_layout)
+    N = stack.shape[1] if b_mn == 0 else stack.shape[2]
+    if weight.dtype == torch.float8_e4m3fn:
+        raise NotImplementedError("an FP8 stack is dequantized by the caller (meepsquared_b200._fp8)")
+    if weight.dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+        raise TypeError(f"the grouped kernel computes in bf16: x {x.dtype}, stack {weight.dtype}")
+    if x.stride(1) != 1 or x.stride(0) % 8:
+        x = x.contiguous()
+    if epilogue == _lib.EPI_SWIGLU:
+        width = N // 2
+    elif epilogue == _lib.EPI_DSWIGLU:
+        width = 2 * N
+    else:
+        width = N
+    if out is None:
+        out = torch.empty((rows, width), device=x.device, dtype=x.dtype)
+    low = None
+    if adapters is not None and store_low:
+        low = torch.empty((rows, RANK_MULTIPLE), device=x.device, dtype=torch.bfloat16)
+    if rows == 0:
+        return out, low
+    if tiles is None:
+        tiles = tile_map(offsets, rows)
+    panel = up = None
+    if adapters is not None:
+        panel, up = adapters.operands(b_mn, backward)
+    p = _lib.Product()
+    p.x, p.rows, p.k, p.ldx = x.data_ptr(), rows, K, x.stride(0)
+    p.weight, p.weight_dtype, p.experts, p.n, p.b_mn = stack.data_ptr(), _lib.BF16, stack.shape[0], N, b_mn
+    p.scale = scale.data_ptr() if scale is not None else None
+    p.panel = panel.data_ptr() if panel is not None else None
+    p.up = up.data_ptr() if up is not None else None
+    p.scaling = float(scaling)
+    p.bias = bias.data_ptr() if bias is not None else None
+    p.offsets = offsets.data_ptr()
+    p.tile_expert, p.tile_row, p.tiles = tiles[0].data_ptr(), tiles[1].data_ptr(), tiles[2].data_ptr()
+    p.max_tiles = tiles[0].numel()
+    p.out, p.ldo = out.data_ptr(), out.stride(0)
+    p.low = low.data_ptr() if low is not None else None
+    p.epilogue = epilogue
+    p.aux = aux.data_ptr() if aux is not None else None
+    p.sm_limit = 0
+    observer = _launch_observer
+    if observer is not None:
+        observer.before(x)
+    _lib.check(_lib.load().meep2b_grouped_product(p, _lib.stream_of(x)), "meep2b_grouped_product")
+    if observer is not None:
+        rank = adapters.rank if adapters is not None else 0
+        observer.after(x, 2 * rows * N * K + 2 * rows * rank * (N + K))
+    return out, low
+
+
+# An object with before(x) / after(x, flops) called around every grouped-product launch, on the launching
+# stream's side (the benchmark records CUDA events there to time the kernel inside a step); None normally.
+_launch_observer = None
+
+
+def set_launch_observer(observer):
+    global _launch_observer
+    _launch_observer = observer
+
+
+def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: float) -> torch.Tensor:
+    """(experts, N, 16) bf16: scaling * sum over each expert's rows of g^T @ low (_grouped.py:362-370)."""
+    experts = offsets.numel()
+    rows, N = g.shape
+    if g.stride(1) != 1 or g.stride(0) % 8:
+        g = g.contiguous()
+    out = torch.empty((experts, N, RANK_MULTIPLE), device=g.device, dtype=torch.bfloat16)
+    if rows == 0:
+        return out.zero_()
+    _lib.check(_lib.load().meep2b_grouped_reduce(_lib.ptr(g), rows, N, g.stride(0), _lib.ptr(low.contiguous()),
+                                                 _lib.ptr(offsets), experts, float(scaling), _lib.ptr(out),
+                                                 _lib.stream_of(g)), "meep2b_grouped_reduce")
+    return out
+
+
+def _to_lhs_rhs(grad_rows_k, grad_cols_n, adapters):
+    """Map the reductions back to PEFT's factors (_grouped.py:400-405).
+
+    grad_rows_k (E, K_fwd, 16) is the gradient of the factor read first in the forward, grad_cols_n (E, N_fwd, 16)
+    of the one applied second.
+    """
+    rank = adapters.rank
+    if adapters.is_transposed:  # first = lhs (E, in, r); second = rhs (E, r, out)
+        return grad_rows_k[:, :, :rank], grad_cols_n.transpose(1, 2)[:, :rank, :]
+    return grad_cols_n[:, :, :rank], grad_rows_k.transpose(1, 2)[:, :rank, :]  # lhs (E,out,r), rhs (E,r,in)
+
+
+class _LoraGroupedProduct(torch.autograd.Function):
+    """The experts' product with the adapters; gradients for x and the adapters, none for the frozen stack."""
+
+    @staticmethod
+    def forward(ctx, x, weight, scale, offsets, is_transposed, lhs, rhs, scaling, bias, products_fp8):
+        adapters = _Adapters(lhs.detach(), rhs.detach(), is_transposed) if lhs is not None else None
+        tiles = tile_map(offsets, x.shape[0])
+        out, low = _launch(x, weight, scale, offsets, not is_transposed, adapters, scaling, bias, True, tiles=tiles)
+        ctx.save_for_backward(x, weight, offsets, *((low,) if low is not None else ()))
+        ctx.adapters, ctx.scale, ctx.is_transposed, ctx.scaling, ctx.tiles = adapters, scale, is_transposed, scaling, tiles
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, weight, offsets, *rest = ctx.saved_tensors
+        adapters = ctx.adapters
+        grad_out = grad_out.contiguous()
+        if adapters is None:
+            grad_x, _ = _launch(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, None, 1.0, None, False,
+                                backward=True, tiles=ctx.tiles)
+            return grad_x, None, None, None, None, None, None, None, None, None
+        low = rest[0]
+        # grad_x = grad @ W (the stack read the other way) + s (grad @ B^T) @ A^T: the adapters swap roles
+        grad_x, low2 = _launch(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, adapters, ctx.scaling, None,
+                               True, backward=True, tiles=ctx.tiles)
+        grad_first = _reduce(x, low2, offsets, ctx.scaling)        # (E, K_fwd, 16)
+        grad_second = _reduce(grad_out, low, offsets, ctx.scaling)  # (E, N_fwd, 16)
+        grad_lhs, grad_rhs = _to_lhs_rhs(grad_first, grad_second, adapters)
+        return grad_x, None, None, None, None, grad_lhs, grad_rhs, None, None, None
+
+
+def _check_fp8_products(weight, products_fp8, device):
+    if weight.dtype == torch.float8_e4m3fn and (fp8_products(device) if products_fp8 is None else products_fp8):
+        raise NotImplementedError("FP8 tensor-core products (activations quantized per row) are not built yet; "
+                                  "an FP8 stack is dequantized to bf16 (products_fp8=False)")
+
+
+def _dequantized(weight, scale):
+    """An FP8 stack as bf16 for one product: (bf16 stack, the scale left for the kernel to apply)."""
+    if weight.dtype != torch.float8_e4m3fn:
+        return weight, scale
+    from . import _fp8
+
+    ones = torch.ones(weight.shape[0], device=weight.device, dtype=torch.float32)
+    return _fp8.dequantize_stack(weight, ones, torch.bfloat16), scale
+
+
+def grouped_linear(x: torch.Tensor, weight: torch.Tensor, offsets: torch.Tensor, is_transposed: bool,
+                   block_m: int = BLOCK_M, products_fp8=None) -> torch.Tensor:
+    """x (rows, in) by the stack (experts, out, in), or (experts, in, out) when is_transposed, per expert group.
+
+    offsets (experts,) int32 on the device: the end of each expert's rows. Returns (rows, out) in x's dtype. An
+    FP8 stack is converted exactly, without a scale: the caller folds the scale in. The base product alone, for
+    the tests and the benchmark. block_m is accepted for the reference's signature; the tile height is 128.
+    """
+    _require(x, "grouped_linear")
+    _stack_strides(weight, x.shape[1], is_transposed)
+    _check_fp8_products(weight, products_fp8, x.device)
+    weight, _ = _dequantized(weight, None)
+    return _launch(x, weight, None, offsets, not is_transposed, None, 1.0, None, False)[0]
+
+
+def lora_linear(x, weight, scale, offsets, is_transposed: bool, lhs=None, rhs=None, scaling: float = 1.0, bias=None,
+                products_fp8=None):
+    """The experts' product of x with the stack, the adapters (PEFT's lhs, rhs, scaling) and the bias stack.
+
+    scale (experts,) is the FP8 stack's per-expert scale, None for a BF16 stack. products_fp8 says whether an FP8
+    stack's products run on the FP8 tensor cores; None lets fp8_products decide for the device.
+    """
+    _require(x, "lora_linear")
+    _stack_strides(weight, x.shape[1], is_transposed)
+    _check_fp8_products(weight, products_fp8, x.device)
+    weight, scale = _dequantized(weight, scale)
+    if lhs is not None and (lhs.dtype != torch.bfloat16 or rhs.dtype != torch.bfloat16):
+        lhs, rhs = lhs.to(torch.bfloat16), rhs.to(torch.bfloat16)
+    if bias is not None and bias.dtype != torch.bfloat16:
+        bias = bias.to(torch.bfloat16)
+    if scale is not None:
+        scale = scale.to(torch.float32).contiguous()
+    return _LoraGroupedProduct.apply(x, weight, scale, offsets.to(torch.int32), is_transposed, lhs, rhs, scaling,
+                                     bias.contiguous() if bias is not None else None, products_fp8)
+
+
+def reference(x: torch.Tensor, weight: torch.Tensor, offsets: torch.Tensor, is_transposed: bool) -> torch.Tensor:
+    """The base product, one expert at a time, in float32, for the tests (the reference's, _grouped.py:420-428)."""
+    out = torch.empty((x.shape[0], weight.shape[2] if is_transposed else weight.shape[1]), device=x.device, dtype=x.dtype)
+    start = 0
+    for e, end in enumerate(offsets.tolist()):
+        w = weight[e].float()
+        out[start:end] = (x[start:end].float() @ (w if is_transposed else w.t())).to(x.dtype)
+        start = end
+    return out
+
+
+def reference_lora(x, weight, scale, offsets, is_transposed, lhs, rhs, scaling, bias=None):
+    """The whole product with PyTorch operations, differentiable, for the tests (_grouped.py:431-444)."""
+    out = []
+    start = 0
+    for e, end in enumerate(offsets.tolist()):
+        w = weight[e].float() * (scale[e].float() if scale is not None else 1.0)
+        if lhs is not None:
+            w = w + scaling * (lhs[e].float() @ rhs[e].float())
+        y = x[start:end].float() @ (w if is_transposed else w.t())
+        if bias is not None:
+            y = y + bias[e].float()
+        out.append(y)
+        start = end
+    return torch.cat(out).to(x.dtype)

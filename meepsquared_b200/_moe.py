@@ -1,0 +1,219 @@
+"""LoRA on the experts of a mixture of experts, computed on the routed tokens only, on a B200.
+
+The drop-in for ``meepsquared/_moe.py:_routed_forward`` (:70-126): the same function of the inputs, weights and
+PEFT factors, with every step a libmeep2b kernel:
+
+* ``route``      the permutation (:75-87): a stable counting sort of the flat expert ids on the device
+                 (histogram, offset table, scatter), bit-exact with a stable sort, sentinels (ids >= E) last;
+* ``gather``     selected = hidden[perm // k] and the routing weights in expert order;
+* the gate/up projection with its adapters, SwiGLU applied in the product's epilogue (:118-119), which also keeps
+  the pre-activation for the backward pass;
+* the down projection with its adapters (:122);
+* ``unpermute``  the weighted sum over each token's k rows (:123-126).
+
+The backward pass mirrors it: the un-permute's gradient (and the routing weights'), the down projection's input
+gradient with SwiGLU's backward in its epilogue, the gate/up projection's input gradient, the four adapter
+reductions and the gather's gradient. The routing is computed once per layer call and its tile map shared by the
+four grouped products.
+"""
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _grouped, _lib
+
+_WEIGHT_DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+
+
+@dataclass
+class Routing:
+    perm: torch.Tensor          # (S,) int64: flat assignment index of each row in expert order
+    expert_ids_g: torch.Tensor  # (S,) int64: expert of each row, sentinels clamped to E-1
+    offsets: torch.Tensor       # (E,) int32: end of each expert's rows
+    inverse: torch.Tensor       # (S,) int64: row of each flat assignment
+    weights_g: torch.Tensor     # (S,) routing weight of each row (the weights' dtype), or None
+    num_tokens: int
+    top_k: int
+    num_experts: int
+    tiles: tuple = None         # the tile map of the grouped products, built on first use
+
+    def tile_map(self):
+        if self.tiles is None:
+            self.tiles = _grouped.tile_map(self.offsets, self.perm.numel())
+        return self.tiles
+
+
+def route(top_k_index: torch.Tensor, top_k_weights, num_experts: int) -> Routing:
+    """The routing permutation of _moe.py:75-87 for top_k_index (T, k); top_k_weights (T, k) may be None."""
+    if not top_k_index.is_cuda:
+        raise RuntimeError("route runs on a CUDA GPU")
+    lib = _lib.load()
+    tokens, k = top_k_index.shape
+    ids = top_k_index.reshape(-1).to(torch.int64).contiguous()
+    n = ids.numel()
+    dev = ids.device
+    perm = torch.empty(n, dtype=torch.int64, device=dev)
+    ids_g = torch.empty(n, dtype=torch.int64, device=dev)
+    inverse = torch.empty(n, dtype=torch.int64, device=dev)
+    offsets = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    ws_bytes = lib.meep2b_route_workspace_bytes(n, num_experts)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = _lib.stream_of(ids)
+    _lib.check(lib.meep2b_route(_lib.ptr(ids), n, num_experts, _lib.ptr(perm), _lib.ptr(ids_g), _lib.ptr(offsets),
+                                _lib.ptr(inverse), _lib.ptr(ws), ws_bytes, stream), "meep2b_route")
+    weights_g = None
+    if top_k_weights is not None:
+        if top_k_weights.dtype not in _WEIGHT_DTYPES:
+            raise TypeError(f"routing weights in {top_k_weights.dtype}: float32 or bf16 expected")
+        weights_g = torch.empty(n, dtype=top_k_weights.dtype, device=dev)
+    return Routing(perm, ids_g, offsets, inverse, weights_g, tokens, k, num_experts)
+
+
+def gather(hidden: torch.Tensor, routing: Routing, top_k_weights=None) -> torch.Tensor:
+    """selected = hidden[perm // k] with sentinel rows zeroed (_moe.py:80,87); fills routing.weights_g."""
+    if hidden.dtype != torch.bfloat16:
+        raise TypeError(f"the routed layer computes in bf16; hidden states are {hidden.dtype}")
+    hidden = hidden.contiguous()
+    rows = routing.perm.numel()
+    sel = torch.empty((rows, hidden.shape[1]), dtype=hidden.dtype, device=hidden.device)
+    w = top_k_weights.contiguous() if top_k_weights is not None else None
+    wd = _WEIGHT_DTYPES[w.dtype] if w is not None else _lib.F32
+    _lib.check(_lib.load().meep2b_gather(_lib.ptr(hidden), routing.num_tokens, hidden.shape[1], routing.top_k,
+                                         _lib.ptr(routing.perm), _lib.ptr(routing.offsets), routing.num_experts,
+                                         _lib.ptr(w), wd, _lib.ptr(routing.weights_g if w is not None else None),
+                                         _lib.ptr(sel), _lib.stream_of(hidden)), "meep2b_gather")
+    return sel
+
+
+def unpermute(y: torch.Tensor, routing: Routing, weights_g=None) -> torch.Tensor:
+    """(T, H) bf16: sum over each token's k rows of y[row] * weights_g[row] (unweighted when weights_g is None)."""
+    y = y.contiguous()
+    out = torch.empty((routing.num_tokens, y.shape[1]), dtype=torch.bfloat16, device=y.device)
+    wd = _WEIGHT_DTYPES[weights_g.dtype] if weights_g is not None else _lib.F32
+    _lib.check(_lib.load().meep2b_unpermute(_lib.ptr(y), _lib.ptr(routing.inverse), _lib.ptr(weights_g), wd,
+                                            _lib.ptr(routing.offsets), routing.num_experts, routing.num_tokens,
+                                            routing.top_k, y.shape[1], _lib.ptr(out), _lib.stream_of(y)),
+               "meep2b_unpermute")
+    return out
+
+
+def unpermute_backward(grad_out: torch.Tensor, y: torch.Tensor, routing: Routing):
+    """(grad_y (S, H) bf16, grad_top_k_weights (T, k) float32) of unpermute with routing.weights_g."""
+    grad_out = grad_out.contiguous()
+    rows = routing.perm.numel()
+    grad_y = torch.empty((rows, y.shape[1]), dtype=torch.bfloat16, device=y.device)
+    grad_w = torch.empty(rows, dtype=torch.float32, device=y.device)
+    w = routing.weights_g
+    _lib.check(_lib.load().meep2b_unpermute_backward(_lib.ptr(grad_out), _lib.ptr(y), _lib.ptr(routing.perm),
+                                                     _lib.ptr(w), _WEIGHT_DTYPES[w.dtype], _lib.ptr(routing.offsets),
+                                                     routing.num_experts, rows, routing.top_k, y.shape[1],
+                                                     _lib.ptr(grad_y), _lib.ptr(grad_w), _lib.stream_of(y)),
+               "meep2b_unpermute_backward")
+    return grad_y, grad_w.view(routing.num_tokens, routing.top_k)
+
+
+@dataclass
+class _Stacks:
+    gate_up: torch.Tensor
+    down: torch.Tensor
+    gate_up_scale: torch.Tensor
+    down_scale: torch.Tensor
+    gate_up_bias: torch.Tensor
+    down_bias: torch.Tensor
+    is_transposed: bool
+    num_experts: int
+    scaling1: float
+    scaling2: float
+
+
+class _RoutedExperts(torch.autograd.Function):
+    """The whole routed layer: gradients for the hidden states, the routing weights and the four LoRA factors."""
+
+    @staticmethod
+    def forward(ctx, hidden, top_k_weights, lhs1, rhs1, lhs2, rhs2, top_k_index, st: _Stacks):
+        routing = route(top_k_index, top_k_weights, st.num_experts)
+        sel = gather(hidden, routing, top_k_weights)
+        tiles = routing.tile_map()
+        rows = sel.shape[0]
+        t = st.is_transposed
+        ad1 = _grouped._Adapters(lhs1.detach(), rhs1.detach(), t) if lhs1 is not None else None
+        ad2 = _grouped._Adapters(lhs2.detach(), rhs2.detach(), t) if lhs2 is not None else None
+        _, b_mn = _grouped._stack_memory(st.gate_up, not t)
+        if b_mn != 0:
+            raise NotImplementedError("SwiGLU is fused for a gate/up stack stored (experts, 2I, hidden), k contiguous")
+        two_i = st.gate_up.shape[2] if t else st.gate_up.shape[1]
+        gu = torch.empty((rows, two_i), dtype=torch.bfloat16, device=sel.device)
+        h, low1 = _grouped._launch(sel, st.gate_up, st.gate_up_scale, routing.offsets, not t, ad1, st.scaling1,
+                                   st.gate_up_bias, True, tiles=tiles, epilogue=_lib.EPI_SWIGLU, aux=gu)
+        y, low2 = _grouped._launch(h, st.down, st.down_scale, routing.offsets, not t, ad2, st.scaling2,
+                                   st.down_bias, True, tiles=tiles)
+        out = unpermute(y, routing, routing.weights_g)
+        ctx.save_for_backward(sel, gu, h, y, *(v for v in (low1, low2) if v is not None))
+        ctx.routing, ctx.st, ctx.ad1, ctx.ad2 = routing, st, ad1, ad2
+        ctx.has_low = (low1 is not None, low2 is not None)
+        ctx.weights_dtype = top_k_weights.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        sel, gu, h, y, *lows = ctx.saved_tensors
+        low1 = lows.pop(0) if ctx.has_low[0] else None
+        low2 = lows.pop(0) if ctx.has_low[1] else None
+        routing, st, ad1, ad2 = ctx.routing, ctx.st, ctx.ad1, ctx.ad2
+        tiles = routing.tile_map()
+        t = st.is_transposed
+        grad_y, grad_w = unpermute_backward(grad_out, y, routing)
+        # down projection: dh = grad_y @ W_down (read the other way), SwiGLU's backward in the epilogue -> d(gate, up)
+        dgu, low2b = _grouped._launch(grad_y, st.down, st.down_scale, routing.offsets, t, ad2, st.scaling2, None,
+                                      True, backward=True, tiles=tiles, epilogue=_lib.EPI_DSWIGLU, aux=gu)
+        dsel, low1b = _grouped._launch(dgu, st.gate_up, st.gate_up_scale, routing.offsets, t, ad1, st.scaling1, None,
+                                       True, backward=True, tiles=tiles)
+        grads = [None, None, None, None]
+        if ad1 is not None:
+            g_first = _grouped._reduce(sel, low1b, routing.offsets, st.scaling1)
+            g_second = _grouped._reduce(dgu, low1, routing.offsets, st.scaling1)
+            grads[0], grads[1] = _grouped._to_lhs_rhs(g_first, g_second, ad1)
+        if ad2 is not None:
+            g_first = _grouped._reduce(h, low2b, routing.offsets, st.scaling2)
+            g_second = _grouped._reduce(grad_y, low2, routing.offsets, st.scaling2)
+            grads[2], grads[3] = _grouped._to_lhs_rhs(g_first, g_second, ad2)
+        grad_hidden = unpermute(dsel, routing, None)
+        return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None)
+
+
+def _bf16_stack(weight, scale):
+    """A stack for the kernels: bf16 as it is, or an FP8 stack dequantized for this call (its scale applied)."""
+    if weight.dtype == torch.float8_e4m3fn:
+        from . import _fp8
+
+        return _fp8.dequantize_stack(weight, scale, torch.bfloat16)
+    if weight.dtype != torch.bfloat16:
+        raise TypeError(f"expert stacks in bf16 or FP8 (e4m3); got {weight.dtype}")
+    return weight
+
+
+def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
+    """The routed layer of a gated experts module with its adapters: _moe._routed_forward's contract.
+
+    experts: a Transformers experts module (num_experts, has_gate, has_bias, is_transposed, gate_up_proj,
+    down_proj; FP8 stacks with ``<name>_scale_inv``). factors: {stack name: (lhs, rhs, scaling)} in PEFT's layout.
+    """
+    if not experts.has_gate:
+        raise NotImplementedError("the fused layer needs a gated experts module (gate_up_proj)")
+    if not hidden_states.is_cuda:
+        raise RuntimeError("the routed layer runs on a CUDA GPU (compute capability 10.0)")
+    gate_up, down = experts.gate_up_proj, experts.down_proj
+    scale1 = getattr(experts, "gate_up_proj_scale_inv", None) if gate_up.dtype == torch.float8_e4m3fn else None
+    scale2 = getattr(experts, "down_proj_scale_inv", None) if down.dtype == torch.float8_e4m3fn else None
+    bias1 = experts.gate_up_proj_bias if experts.has_bias else None
+    bias2 = experts.down_proj_bias if experts.has_bias else None
+    lhs1, rhs1, s1 = factors.get("gate_up_proj", (None, None, 1.0))
+    lhs2, rhs2, s2 = factors.get("down_proj", (None, None, 1.0))
+    cast = lambda f: f.to(torch.bfloat16) if f is not None and f.dtype != torch.bfloat16 else f  # noqa: E731
+    st = _Stacks(_bf16_stack(gate_up.detach(), scale1), _bf16_stack(down.detach(), scale2), None, None,
+                 bias1.detach().to(torch.bfloat16).contiguous() if bias1 is not None else None,
+                 bias2.detach().to(torch.bfloat16).contiguous() if bias2 is not None else None,
+                 bool(experts.is_transposed), int(experts.num_experts), float(s1), float(s2))
+    return _RoutedExperts.apply(hidden_states.to(torch.bfloat16), top_k_weights, cast(lhs1), cast(rhs1), cast(lhs2),
+                                cast(rhs2), top_k_index, st)

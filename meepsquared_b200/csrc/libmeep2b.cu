@@ -1,0 +1,6 @@
+// Single translation unit of libmeep2b: the device error word and every kernel share one module.
+#include "capi.cu"
+#include "route.cu"
+#include "grouped_gemm.cu"
+#include "reduce.cu"
+#include "quant.cu"

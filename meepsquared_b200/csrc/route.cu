@@ -1,0 +1,384 @@
+// Routing kernels of the expert layer: the stable counting sort of the expert ids (histogram, offset table,
+// scatter), the gather of hidden rows into expert order, the weighted un-permute and its backward, and the tile
+// map of the grouped product. All HBM- or latency-bound integer and byte work: coalesced 16-byte accesses, no
+// tensor cores.
+//
+// Replaces _moe._routed_forward's sort / histc / cumsum / gather / weighted sum (meepsquared/_moe.py:75-87,
+// 123-126) and _grouped.tile_map (meepsquared/_grouped.py:88-103).
+#include "common.cuh"
+#include "host.hpp"
+
+namespace meep2b {
+
+constexpr int kRouteChunk = 4096;   // assignments per CTA of the histogram and scatter passes
+constexpr int kRouteThreads = 256;  // 8 warps: a round of the scatter places 256 assignments
+constexpr int kMaxBuckets = 1025;   // experts + 1 (the sentinel bucket)
+
+__device__ __forceinline__ int bucket_of(int64_t id, int experts) {
+  return (id >= 0 && id < experts) ? static_cast<int>(id) : experts;
+}
+
+// Per-CTA bucket counts of its chunk: counts[block * buckets + b].
+__global__ void __launch_bounds__(kRouteThreads) route_histogram(const int64_t* __restrict__ ids, int64_t n,
+                                                                 int experts, int* __restrict__ counts) {
+  extern __shared__ int hist[];
+  const int buckets = experts + 1;
+  for (int b = threadIdx.x; b < buckets; b += blockDim.x) hist[b] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk;
+  const int64_t end = min(base + kRouteChunk, n);
+  for (int64_t i = base + threadIdx.x; i < end; i += blockDim.x) atomicAdd(&hist[bucket_of(ids[i], experts)], 1);
+  __syncthreads();
+  for (int b = threadIdx.x; b < buckets; b += blockDim.x) counts[static_cast<int64_t>(blockIdx.x) * buckets + b] = hist[b];
+}
+
+// One CTA: turns the per-CTA counts into per-CTA starting positions (bucket-major, then CTA order: this is what
+// makes the sort stable) and writes the inclusive int32 offsets of the real experts.
+__global__ void __launch_bounds__(1024) route_scan(int* __restrict__ counts, int blocks, int experts,
+                                                   int32_t* __restrict__ offsets) {
+  __shared__ int totals[kMaxBuckets];
+  __shared__ int starts[kMaxBuckets];
+  const int buckets = experts + 1;
+  for (int b = threadIdx.x; b < buckets; b += blockDim.x) {
+    int s = 0;
+    for (int k = 0; k < blocks; ++k) s += counts[static_cast<int64_t>(k) * buckets + b];
+    totals[b] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int b = 0; b < buckets; ++b) {
+      starts[b] = run;
+      run += totals[b];
+    }
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < buckets; b += blockDim.x) {
+    int run = starts[b];
+    for (int k = 0; k < blocks; ++k) {
+      const int64_t at = static_cast<int64_t>(k) * buckets + b;
+      const int c = counts[at];
+      counts[at] = run;
+      run += c;
+    }
+    if (b < experts) offsets[b] = starts[b] + totals[b];
+  }
+}
+
+// Places each assignment of the CTA's chunk at its stable position: CTA start of its bucket + the number of
+// earlier assignments of the same bucket in the chunk. Rounds of 256: within a warp the rank comes from
+// __match_any_sync, across the warps of a round from per-warp bucket counts.
+__global__ void __launch_bounds__(kRouteThreads) route_scatter(const int64_t* __restrict__ ids, int64_t n,
+                                                               int experts, const int* __restrict__ starts,
+                                                               int64_t* __restrict__ perm,
+                                                               int64_t* __restrict__ ids_g,
+                                                               int64_t* __restrict__ inverse) {
+  extern __shared__ int smem[];
+  const int buckets = experts + 1;
+  int* running = smem;                        // [buckets]
+  int* warp_counts = smem + buckets;          // [8][buckets]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int b = threadIdx.x; b < buckets; b += blockDim.x) running[b] = starts[static_cast<int64_t>(blockIdx.x) * buckets + b];
+  for (int b = threadIdx.x; b < 8 * buckets; b += blockDim.x) warp_counts[b] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk;
+  const int64_t end = min(base + kRouteChunk, n);
+  for (int64_t round = base; round < end; round += kRouteThreads) {
+    const int64_t i = round + threadIdx.x;
+    const bool live = i < end;
+    const int64_t id = live ? ids[i] : -1;
+    const int b = live ? bucket_of(id, experts) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, b);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (live && rank == 0) warp_counts[warp * buckets + b] = __popc(peers);
+    __syncthreads();
+    if (live) {
+      int pos = running[b] + rank;
+      for (int w = 0; w < warp; ++w) pos += warp_counts[w * buckets + b];
+      perm[pos] = i;
+      if (ids_g) ids_g[pos] = (b == experts) ? static_cast<int64_t>(experts - 1) : id;
+      if (inverse) inverse[i] = pos;
+    }
+    __syncthreads();
+    for (int bb = threadIdx.x; bb < buckets; bb += blockDim.x) {
+      int add = 0;
+      for (int w = 0; w < 8; ++w) {
+        add += warp_counts[w * buckets + bb];
+        warp_counts[w * buckets + bb] = 0;
+      }
+      running[bb] += add;
+    }
+    __syncthreads();
+  }
+}
+
+// selected[i] = hidden[perm[i] / top_k] (zero past the real rows); weights_g[i] = weights[perm[i]].
+// One warp per row, 16-byte vectors.
+template <typename W>
+__global__ void __launch_bounds__(256) gather_rows(const uint4* __restrict__ hidden, int64_t vec_per_row,
+                                                   int top_k, const int64_t* __restrict__ perm,
+                                                   const int32_t* __restrict__ offsets, int experts, int64_t rows,
+                                                   const W* __restrict__ weights, W* __restrict__ weights_g,
+                                                   uint4* __restrict__ selected) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t valid = offsets[experts - 1];
+  const int64_t src = perm[row];
+  uint4* dst = selected + row * vec_per_row;
+  if (weights_g != nullptr && lane == 0) weights_g[row] = weights[src];
+  if (row < valid) {
+    const uint4* s = hidden + (src / top_k) * vec_per_row;
+    for (int64_t v = lane; v < vec_per_row; v += 32) dst[v] = __ldg(s + v);
+  } else {
+    for (int64_t v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ float weight_value(const float* w, int64_t i) { return w[i]; }
+__device__ __forceinline__ float weight_value(const __nv_bfloat16* w, int64_t i) { return __bfloat162float(w[i]); }
+
+// out[t] = bf16(sum_j y[r_j] * w_g[r_j]), r_j = inverse[t * top_k + j]. One CTA per token, 8 bf16 per thread
+// and step. F32 weights: each product rounded to float32 (bf16 * f32 promotes), summed in float32. BF16 weights:
+// each product rounded to bf16 (bf16 * bf16), summed in float32. No weights: a plain float32 sum.
+template <typename W>
+__global__ void __launch_bounds__(256) unpermute_rows(const uint4* __restrict__ y, const int64_t* __restrict__ inverse,
+                                                     const W* __restrict__ weights_g,
+                                                     const int32_t* __restrict__ offsets, int experts,
+                                                     int top_k, int64_t vec_per_row, uint4* __restrict__ out) {
+  const int64_t t = blockIdx.x;
+  const int64_t valid = offsets[experts - 1];
+  for (int64_t v = threadIdx.x; v < vec_per_row; v += blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < top_k; ++j) {
+      const int64_t r = inverse[t * top_k + j];
+      if (r >= valid) continue;  // a sentinel row: masked to zero (_moe.py:116)
+      const uint4 q = __ldg(y + r * vec_per_row + v);
+      const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+      if (weights_g == nullptr) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[2 * e] = __fadd_rn(acc[2 * e], bf16_lo(words[e]));
+          acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], bf16_hi(words[e]));
+        }
+      } else {
+        const float w = weight_value(weights_g, r);
+        const bool round_bf16 = sizeof(W) == 2;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float p0 = __fmul_rn(bf16_lo(words[e]), w), p1 = __fmul_rn(bf16_hi(words[e]), w);
+          if (round_bf16) {
+            p0 = bf16_round(p0);
+            p1 = bf16_round(p1);
+          }
+          acc[2 * e] = __fadd_rn(acc[2 * e], p0);
+          acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], p1);
+        }
+      }
+    }
+    out[t * vec_per_row + v] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                          pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+  }
+}
+
+// grad_y[i] = bf16(grad_out[tok] * w_g[i]); grad_weights[perm[i]] = sum_h grad_out[tok][h] * y[i][h]. One CTA per
+// routed row.
+template <typename W>
+__global__ void __launch_bounds__(256) unpermute_backward_rows(const uint4* __restrict__ grad_out,
+                                                               const uint4* __restrict__ y,
+                                                               const int64_t* __restrict__ perm,
+                                                               const W* __restrict__ weights_g,
+                                                               const int32_t* __restrict__ offsets, int experts,
+                                                               int top_k, int64_t vec_per_row,
+                                                               uint4* __restrict__ grad_y,
+                                                               float* __restrict__ grad_weights) {
+  __shared__ float partial[8];
+  const int64_t i = blockIdx.x;
+  const int64_t valid = offsets[experts - 1];
+  const int64_t src = perm[i];
+  const bool live = i < valid;
+  const float w = live ? weight_value(weights_g, i) : 0.f;
+  const bool round_bf16 = sizeof(W) == 2;
+  float dot = 0.f;
+  for (int64_t v = threadIdx.x; v < vec_per_row; v += blockDim.x) {
+    uint4 o = make_uint4(0, 0, 0, 0);
+    if (live) {
+      const uint4 g = __ldg(grad_out + (src / top_k) * vec_per_row + v);
+      const uint4 q = __ldg(y + i * vec_per_row + v);
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      const uint32_t yw[4] = {q.x, q.y, q.z, q.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float g0 = bf16_lo(gw[e]), g1 = bf16_hi(gw[e]);
+        ow[e] = pack_bf16x2(__fmul_rn(g0, w), __fmul_rn(g1, w));
+        if (round_bf16) {  // bf16 weights: autograd's sum of bf16 products
+          dot = __fadd_rn(dot, bf16_round(__fmul_rn(g0, bf16_lo(yw[e]))));
+          dot = __fadd_rn(dot, bf16_round(__fmul_rn(g1, bf16_hi(yw[e]))));
+        } else {
+          dot = fmaf(g0, bf16_lo(yw[e]), dot);
+          dot = fmaf(g1, bf16_hi(yw[e]), dot);
+        }
+      }
+      o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+    grad_y[i * vec_per_row + v] = o;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = dot;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) s += partial[k];
+    grad_weights[src] = live ? s : 0.f;
+  }
+}
+
+// The tile map: tiles per expert, their running sum, and for every tile index t < max_tiles the expert (by binary
+// search over the running sums; spares clamp to the last expert) and the first row.
+__global__ void __launch_bounds__(1024) tile_map_kernel(const int32_t* __restrict__ offsets, int experts,
+                                                        int block_m, int64_t max_tiles,
+                                                        int32_t* __restrict__ tile_expert,
+                                                        int32_t* __restrict__ tile_row, int32_t* __restrict__ tiles) {
+  extern __shared__ int tm[];
+  int* ends = tm;              // inclusive running tile count per expert
+  int* starts = tm + experts;  // first row per expert
+  if (threadIdx.x == 0) {
+    int run = 0, prev = 0;
+    for (int e = 0; e < experts; ++e) {
+      const int end = offsets[e];
+      starts[e] = prev;
+      run += (end - prev + block_m - 1) / block_m;
+      ends[e] = run;
+      prev = end;
+    }
+    *tiles = run;
+  }
+  __syncthreads();
+  for (int64_t t = threadIdx.x; t < max_tiles; t += blockDim.x) {
+    int lo = 0, hi = experts;  // first e with ends[e] > t
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (ends[mid] > t) hi = mid; else lo = mid + 1;
+    }
+    const int e = lo < experts ? lo : experts - 1;
+    const int before = ends[e] - (ends[e] - (e > 0 ? ends[e - 1] : 0));
+    tile_expert[t] = e;
+    tile_row[t] = starts[e] + static_cast<int>(t - before) * block_m;
+  }
+}
+
+}  // namespace meep2b
+
+using namespace meep2b;
+
+extern "C" {
+
+size_t meep2b_route_workspace_bytes(int64_t assignments, int32_t experts) {
+  const int64_t blocks = (assignments + kRouteChunk - 1) / kRouteChunk;
+  return static_cast<size_t>((blocks > 0 ? blocks : 1) * (experts + 1)) * sizeof(int);
+}
+
+int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
+                 int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  if (experts < 1 || experts + 1 > kMaxBuckets || assignments < 0) return MEEP2B_ERR_SHAPE;
+  if (workspace_bytes < meep2b_route_workspace_bytes(assignments, experts)) return MEEP2B_ERR_SHAPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  if (assignments == 0) {
+    cudaMemsetAsync(offsets, 0, sizeof(int32_t) * experts, s);
+    return launch_status();
+  }
+  const int blocks = static_cast<int>((assignments + kRouteChunk - 1) / kRouteChunk);
+  int* counts = static_cast<int*>(workspace);
+  const size_t hist_smem = sizeof(int) * (experts + 1);
+  route_histogram<<<blocks, kRouteThreads, hist_smem, s>>>(expert_ids, assignments, experts, counts);
+  route_scan<<<1, 1024, 0, s>>>(counts, blocks, experts, offsets);
+  const size_t scatter_smem = sizeof(int) * 9 * (experts + 1);
+  route_scatter<<<blocks, kRouteThreads, scatter_smem, s>>>(expert_ids, assignments, experts, counts, perm,
+                                                            expert_ids_g, inverse);
+  return launch_status();
+}
+
+int meep2b_gather(const void* hidden, int64_t tokens, int64_t hidden_dim, int32_t top_k, const int64_t* perm,
+                  const int32_t* offsets, int32_t experts, const void* weights, int32_t weights_dtype,
+                  void* weights_g, void* selected, void* stream) {
+  if (top_k < 1 || experts < 1 || tokens < 0 || hidden_dim % 8 != 0) return MEEP2B_ERR_SHAPE;
+  if (!aligned16(hidden) || !aligned16(selected)) return MEEP2B_ERR_ALIGN;
+  if ((weights_g != nullptr) && weights_dtype != MEEP2B_F32 && weights_dtype != MEEP2B_BF16) return MEEP2B_ERR_DTYPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  const int64_t rows = tokens * top_k;
+  if (rows == 0) return MEEP2B_OK;
+  const int64_t vec = hidden_dim / 8;
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  if (weights_dtype == MEEP2B_BF16)
+    gather_rows<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        static_cast<const uint4*>(hidden), vec, top_k, perm, offsets, experts, rows,
+        static_cast<const __nv_bfloat16*>(weights), static_cast<__nv_bfloat16*>(weights_g),
+        static_cast<uint4*>(selected));
+  else
+    gather_rows<float><<<grid, 256, 0, s>>>(static_cast<const uint4*>(hidden), vec, top_k, perm, offsets, experts,
+                                            rows, static_cast<const float*>(weights), static_cast<float*>(weights_g),
+                                            static_cast<uint4*>(selected));
+  return launch_status();
+}
+
+int meep2b_unpermute(const void* y, const int64_t* inverse, const void* weights_g, int32_t weights_dtype,
+                     const int32_t* offsets, int32_t experts, int64_t tokens, int32_t top_k, int64_t hidden_dim,
+                     void* out, void* stream) {
+  if (top_k < 1 || experts < 1 || tokens < 0 || hidden_dim % 8 != 0) return MEEP2B_ERR_SHAPE;
+  if (!aligned16(y) || !aligned16(out)) return MEEP2B_ERR_ALIGN;
+  if (weights_g != nullptr && weights_dtype != MEEP2B_F32 && weights_dtype != MEEP2B_BF16) return MEEP2B_ERR_DTYPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  if (tokens == 0) return MEEP2B_OK;
+  const int64_t vec = hidden_dim / 8;
+  const int threads = vec >= 256 ? 256 : static_cast<int>(((vec + 31) / 32) * 32);
+  if (weights_g != nullptr && weights_dtype == MEEP2B_BF16)
+    unpermute_rows<__nv_bfloat16><<<static_cast<unsigned>(tokens), threads, 0, s>>>(
+        static_cast<const uint4*>(y), inverse, static_cast<const __nv_bfloat16*>(weights_g), offsets, experts, top_k,
+        vec, static_cast<uint4*>(out));
+  else
+    unpermute_rows<float><<<static_cast<unsigned>(tokens), threads, 0, s>>>(
+        static_cast<const uint4*>(y), inverse, static_cast<const float*>(weights_g), offsets, experts, top_k, vec,
+        static_cast<uint4*>(out));
+  return launch_status();
+}
+
+int meep2b_unpermute_backward(const void* grad_out, const void* y, const int64_t* perm, const void* weights_g,
+                              int32_t weights_dtype, const int32_t* offsets, int32_t experts, int64_t assignments,
+                              int32_t top_k, int64_t hidden_dim, void* grad_y, float* grad_weights, void* stream) {
+  if (top_k < 1 || experts < 1 || assignments < 0 || hidden_dim % 8 != 0) return MEEP2B_ERR_SHAPE;
+  if (!aligned16(grad_out) || !aligned16(y) || !aligned16(grad_y)) return MEEP2B_ERR_ALIGN;
+  if (weights_dtype != MEEP2B_F32 && weights_dtype != MEEP2B_BF16) return MEEP2B_ERR_DTYPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  if (assignments == 0) return MEEP2B_OK;
+  const int64_t vec = hidden_dim / 8;
+  if (weights_dtype == MEEP2B_BF16)
+    unpermute_backward_rows<__nv_bfloat16><<<static_cast<unsigned>(assignments), 256, 0, s>>>(
+        static_cast<const uint4*>(grad_out), static_cast<const uint4*>(y), perm,
+        static_cast<const __nv_bfloat16*>(weights_g), offsets, experts, top_k, vec, static_cast<uint4*>(grad_y),
+        grad_weights);
+  else
+    unpermute_backward_rows<float><<<static_cast<unsigned>(assignments), 256, 0, s>>>(
+        static_cast<const uint4*>(grad_out), static_cast<const uint4*>(y), perm, static_cast<const float*>(weights_g),
+        offsets, experts, top_k, vec, static_cast<uint4*>(grad_y), grad_weights);
+  return launch_status();
+}
+
+int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32_t block_m, int32_t* tile_expert,
+                    int32_t* tile_row, int32_t* tiles, void* stream) {
+  if (experts < 1 || rows < 0 || block_m < 1 || experts > 16384) return MEEP2B_ERR_SHAPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  const int64_t max_tiles = rows / block_m + experts;
+  tile_map_kernel<<<1, 1024, sizeof(int) * 2 * experts, s>>>(offsets, experts, block_m, max_tiles, tile_expert,
+                                                             tile_row, tiles);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -15,19 +15,23 @@ def _segments(offsets):
         start = end
 
 
-def _effective(weight, scale, e, lhs, rhs, scaling):
+def _base(weight, scale, e):
     w = np.asarray(weight[e], dtype=np.float32)
     if scale is not None:
         w = w * np.float32(scale[e])
-    if lhs is not None:
-        w = w + np.float32(scaling) * (np.asarray(lhs[e], dtype=np.float32) @ np.asarray(rhs[e], dtype=np.float32))
     return w
 
 
-def lora_forward(x, weight, scale, offsets, is_transposed, lhs=None, rhs=None, scaling=1.0, bias=None):
-    """reference_lora: per expert w = W_e * scale_e + s * lhs_e @ rhs_e, y = x_e @ (w or w^T) + bias_e (float32).
+def _factors(lhs, rhs, e, is_transposed):
+    """(F1 (in, r), F2 (r, out)) with x @ delta^T (or x @ delta) = (x @ F1) @ F2."""
+    l, r = np.asarray(lhs[e], dtype=np.float32), np.asarray(rhs[e], dtype=np.float32)
+    return (l, r) if is_transposed else (r.T, l.T)
 
-    Rows past offsets[-1] (sentinels) come out zero. Returns (rows, N) float32.
+
+def lora_forward(x, weight, scale, offsets, is_transposed, lhs=None, rhs=None, scaling=1.0, bias=None):
+    """Per expert y = x_e @ (W_e * scale_e)^T + s * (x_e @ F1_e) @ F2_e + bias_e (float32), the adapters applied
+    as two products of rank depth as _moe._grouped_lora does (_moe.py:48-67); equal to reference_lora's
+    x @ (W + s lhs @ rhs)^T (_grouped.py:431-444) up to float32 rounding. Rows past offsets[-1] come out zero.
     """
     x = np.asarray(x, dtype=np.float32)
     n = weight.shape[2] if is_transposed else weight.shape[1]
@@ -35,8 +39,12 @@ def lora_forward(x, weight, scale, offsets, is_transposed, lhs=None, rhs=None, s
     for e, start, end in _segments(offsets):
         if end == start:
             continue
-        w = _effective(weight, scale, e, lhs, rhs, scaling)
-        y = x[start:end] @ (w if is_transposed else w.T)
+        w = _base(weight, scale, e)
+        xe = x[start:end]
+        y = xe @ (w if is_transposed else w.T)
+        if lhs is not None:
+            f1, f2 = _factors(lhs, rhs, e, is_transposed)
+            y = y + np.float32(scaling) * ((xe @ f1) @ f2)
         if bias is not None:
             y = y + np.asarray(bias[e], dtype=np.float32)
         out[start:end] = y
@@ -55,7 +63,11 @@ def lora_low(x, offsets, is_transposed, lhs, rhs):
 
 
 def lora_backward(x, grad, weight, scale, offsets, is_transposed, lhs=None, rhs=None, scaling=1.0):
-    """Gradients of lora_forward: (grad_x, grad_lhs, grad_rhs), float32; grad_lhs/rhs None without adapters."""
+    """Gradients of lora_forward: (grad_x, grad_lhs, grad_rhs), float32; grad_lhs/rhs None without adapters.
+
+    grad_x = g @ W_e (the stack read the other way) + s (g @ F2^T) @ F1^T; dF1 = s x^T (g @ F2^T),
+    dF2 = s (x @ F1)^T g, mapped back to PEFT's lhs / rhs (_grouped.py:385-405).
+    """
     x = np.asarray(x, dtype=np.float32)
     g = np.asarray(grad, dtype=np.float32)
     grad_x = np.zeros_like(x)
@@ -65,15 +77,20 @@ def lora_backward(x, grad, weight, scale, offsets, is_transposed, lhs=None, rhs=
     for e, start, end in _segments(offsets):
         if end == start:
             continue
-        w = _effective(weight, scale, e, lhs, rhs, scaling)
+        w = _base(weight, scale, e)
         xe, ge = x[start:end], g[start:end]
-        grad_x[start:end] = ge @ (w.T if is_transposed else w)
+        gx = ge @ (w.T if is_transposed else w)
         if lhs is not None:
-            # the delta's gradient in the stack's layout: (out, in) = g^T x, or (in, out) = x^T g
-            d_delta = (xe.T @ ge) if is_transposed else (ge.T @ xe)
-            l, r = np.asarray(lhs[e], dtype=np.float32), np.asarray(rhs[e], dtype=np.float32)
-            grad_lhs[e] = s * (d_delta @ r.T)
-            grad_rhs[e] = s * (l.T @ d_delta)
+            f1, f2 = _factors(lhs, rhs, e, is_transposed)
+            g2 = ge @ f2.T                      # (rows, r)
+            gx = gx + s * (g2 @ f1.T)
+            d_f1 = s * (xe.T @ g2)              # (in, r)
+            d_f2 = s * ((xe @ f1).T @ ge)       # (r, out)
+            if is_transposed:                    # F1 = lhs, F2 = rhs
+                grad_lhs[e], grad_rhs[e] = d_f1, d_f2
+            else:                                # F1 = rhs^T, F2 = lhs^T
+                grad_lhs[e], grad_rhs[e] = d_f2.T, d_f1.T
+        grad_x[start:end] = gx
     return grad_x, grad_lhs, grad_rhs
 
 

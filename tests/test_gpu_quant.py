@@ -1,0 +1,65 @@
+"""Quantised stacks on the GPU: FP8 per expert and 128x128 block FP8 bit-exact with the reference's golden
+vectors, NF4 double dequantisation bit-exact with the oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+import meepsquared_b200 as mb
+from meepsquared_b200 import _fp8, _nf4
+from oracle import quant
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("name", ["test", "big"])
+def test_fp8_stack_is_bit_exact_with_the_reference(golden, name):
+    g = golden("fp8_stack")
+    w = torch.from_numpy(g[f"{name}_weight"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    codes, scale = _fp8.quantize_stack(w)
+    np.testing.assert_array_equal(scale.cpu().numpy(), g[f"{name}_scale"])
+    np.testing.assert_array_equal(codes.view(torch.uint8).cpu().numpy(), g[f"{name}_codes"])
+    np.testing.assert_array_equal(bits(_fp8.dequantize_stack(codes, scale, torch.bfloat16)), g[f"{name}_dequant"])
+
+
+@pytest.mark.parametrize("name", ["even", "tail"])
+def test_fp8_blocks_are_bit_exact_with_the_reference(golden, name):
+    g = golden("fp8_block")
+    w = torch.from_numpy(g[f"{name}_weight"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    codes, scale = _fp8.quantize_blocks(w, g[f"{name}_scale"].shape)
+    np.testing.assert_array_equal(scale.cpu().numpy(), g[f"{name}_scale"])
+    np.testing.assert_array_equal(codes.view(torch.uint8).cpu().numpy(), g[f"{name}_codes"])
+    c = torch.from_numpy(g[f"{name}_codes"]).to(DEV).view(torch.float8_e4m3fn)
+    np.testing.assert_array_equal(bits(_fp8.dequantize_blocks(c, torch.from_numpy(g[f"{name}_scale"]).to(DEV))),
+                                  g[f"{name}_dequant"])
+
+
+def test_fp8_blocks_of_a_config5_stack_match_the_oracle():
+    """A stack of BASELINE config 5's down projection (a few experts of (4096, 1536), 128x128 blocks)."""
+    gen = torch.Generator().manual_seed(5)
+    w = (torch.randn(3, 4096, 1536, generator=gen) * 0.02).to(torch.bfloat16)
+    codes, scale = _fp8.quantize_blocks(w.to(DEV))
+    deq = bits(_fp8.dequantize_blocks(codes, scale))
+    for e in range(3):
+        c_ref, s_ref = quant.quantize_fp8_blocks(w[e].float().numpy())
+        np.testing.assert_array_equal(scale[e].cpu().numpy(), s_ref)
+        np.testing.assert_array_equal(codes[e].view(torch.uint8).cpu().numpy(), c_ref)
+        np.testing.assert_array_equal(deq[e], quant.dequantize_fp8_blocks(c_ref, s_ref))
+
+
+@pytest.mark.parametrize("shape", [(4, 96, 128), (2, 1536, 2048), (3, 64 * 5)])
+def test_nf4_dequantisation_is_bit_exact_with_the_oracle(shape):
+    rng = np.random.default_rng(sum(shape))
+    w = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+    if int(np.prod(shape)) % 64:
+        pytest.skip("whole blocks only")
+    st = quant.quantize_nf4(w)
+    state = _nf4.NF4State(torch.from_numpy(st["packed"]), torch.from_numpy(st["absmax"]),
+                          torch.from_numpy(st["absmax2"]), torch.from_numpy(st["code2"]),
+                          torch.tensor([st["offset"]], dtype=torch.float32), tuple(shape)).to(DEV)
+    np.testing.assert_array_equal(bits(_nf4.dequantize(state)), quant.dequantize_nf4(st))

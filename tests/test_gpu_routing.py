@@ -1,0 +1,98 @@
+"""Routing kernels on the GPU against the oracle and the reference's golden vectors: bit-exact."""
+
+import numpy as np
+import pytest
+import torch
+
+import layer_inputs
+import meepsquared_b200 as mb
+from meepsquared_b200 import _moe
+from oracle import routing as oroute
+from parity import as_np, assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.mark.parametrize("case", ["small", "config1", "e128", "zipf"])
+def test_route_matches_the_golden_permutation(golden, case):
+    g = golden("routing")
+    experts = int(g[f"{case}_experts"])
+    ids = torch.from_numpy(g[f"{case}_ids"]).to(DEV)
+    r = mb.route(ids.view(-1, 1), None, experts)
+    np.testing.assert_array_equal(r.perm.cpu().numpy(), g[f"{case}_perm_stable"])
+    np.testing.assert_array_equal(r.offsets.cpu().numpy(), g[f"{case}_offsets"])
+    np.testing.assert_array_equal(r.expert_ids_g.cpu().numpy(), np.minimum(g[f"{case}_ids_sorted"], experts - 1))
+    inv = r.inverse.cpu().numpy()
+    np.testing.assert_array_equal(inv[g[f"{case}_perm_stable"]], np.arange(inv.size))
+
+
+@pytest.mark.parametrize("tokens,experts,k", [(16384, 128, 8), (8192, 8, 2), (32768, 128, 8), (1, 4, 2), (3, 1, 1),
+                                              (5000, 1024, 4)])
+def test_route_matches_the_oracle_at_config_sizes(tokens, experts, k):
+    gen = torch.Generator().manual_seed(tokens + experts)
+    idx, _ = layer_inputs.routing(tokens, experts, k, gen, zipf=1.1 if experts == 128 else None)
+    r = mb.route(idx.to(DEV), None, experts)
+    want = oroute.route(idx.numpy(), experts)
+    for name in ("perm", "offsets", "inverse", "expert_ids_g"):
+        np.testing.assert_array_equal(getattr(r, name).cpu().numpy(), want[name], err_msg=name)
+
+
+def test_route_with_sentinels():
+    ids = torch.tensor([[3, 9], [0, 4], [4, 1], [9, 2], [7, 0]], dtype=torch.int64)  # E=5: 9 and 7 are sentinels
+    r = mb.route(ids.to(DEV), None, 5)
+    want = oroute.route(ids.numpy(), 5)
+    np.testing.assert_array_equal(r.offsets.cpu().numpy(), want["offsets"])
+    valid = int(want["offsets"][-1])
+    np.testing.assert_array_equal(r.perm.cpu().numpy()[:valid], want["perm"][:valid])
+    assert sorted(r.perm.cpu().numpy()[valid:].tolist()) == sorted(want["perm"][valid:].tolist())
+
+
+def test_tile_map_matches_the_reference_kats(golden):
+    g = golden("tile_map")
+    for name in sorted({k.rsplit("_", 1)[0] for k in g if k.endswith("_offsets")}):
+        te, tr, tiles = mb.tile_map(torch.from_numpy(g[f"{name}_offsets"]).to(DEV), int(g[f"{name}_rows"]),
+                                    int(g[f"{name}_block_m"]))
+        assert tiles.item() == int(g[f"{name}_tiles"]), name
+        np.testing.assert_array_equal(te.cpu().numpy(), g[f"{name}_tile_expert"], err_msg=name)
+        np.testing.assert_array_equal(tr.cpu().numpy(), g[f"{name}_tile_row"], err_msg=name)
+
+
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.bfloat16])
+def test_gather_and_unpermute_match_the_oracle(wdtype):
+    cfg = dict(layer_inputs.SMALL)
+    inp = layer_inputs.layer(**cfg)
+    idx = inp["top_k_index"].clone()
+    idx[3, 1] = cfg["experts"]  # a sentinel
+    w = inp["top_k_weights"].to(wdtype)
+    hidden = inp["hidden"].to(torch.bfloat16)
+    r = mb.route(idx.to(DEV), w.to(DEV), cfg["experts"])
+    sel = mb.gather(hidden.to(DEV), r, w.to(DEV))
+    want = oroute.route(idx.numpy(), cfg["experts"])
+    np.testing.assert_array_equal(as_np(sel), oroute.gather(as_np(hidden), want["perm"], cfg["top_k"], want["sentinel"]))
+    np.testing.assert_array_equal(as_np(r.weights_g), as_np(w).reshape(-1)[want["perm"]])
+    y = torch.randn(sel.shape, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    y_np = as_np(y)
+    y_np[want["sentinel"]] = 0
+    out = mb.unpermute(y.to(DEV), r, r.weights_g)
+    ref = oroute.unpermute(y_np, as_np(r.weights_g), want["inverse"], cfg["tokens"], cfg["top_k"])
+    # float32 weights: one bf16 rounding of a float32 sum; bf16 weights: each product rounded to bf16 first, as the
+    # reference's bf16 multiply does, so the parity tolerance against float32
+    if wdtype == torch.float32:
+        np.testing.assert_allclose(as_np(out), ref, rtol=8e-3, atol=1e-6)
+    else:
+        assert_close(out, ref, "unpermute")
+    grad = torch.randn(cfg["tokens"], cfg["hidden"], generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    gy, gw = _moe.unpermute_backward(grad.to(DEV), y.to(DEV), r)
+    ref_gy, ref_gw = oroute.unpermute_backward(as_np(grad), y_np, as_np(r.weights_g), want["perm"], cfg["top_k"])
+    ref_gy[want["sentinel"]] = 0
+    ref_gw[want["sentinel"]] = 0
+    assert_close(gy, ref_gy, "grad_y")
+    flat = np.zeros(cfg["tokens"] * cfg["top_k"], dtype=np.float32)
+    flat[want["perm"]] = ref_gw
+    np.testing.assert_allclose(as_np(gw).reshape(-1), flat, rtol=2e-2, atol=1e-3)
+
+
+def test_empty_routing():
+    r = mb.route(torch.zeros((0, 2), dtype=torch.int64, device=DEV), None, 4)
+    assert r.perm.numel() == 0 and r.offsets.cpu().tolist() == [0, 0, 0, 0]
