@@ -106,8 +106,9 @@ int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32
  *                                  up (experts, 16, n).
  * The rank is padded to 16 with zeros (_grouped.py:275-282). x is (rows, k) with row stride ldx; rows of one
  * expert are contiguous, offsets[e] is the end of expert e's rows (int32, inclusive cumsum). tile_expert /
- * tile_row / tiles come from meep2b_tile_map with block_m = 128. low (rows, 16) receives bf16(x P_e^T) when not
- * NULL (kept for the backward pass, _grouped.py:212-214). */
+ * tile_row / tiles come from meep2b_tile_map with the product's block_m: 128 (one CTA per tile) or 256 (a CTA
+ * pair per tile, tcgen05 cta_group::2, for b_mn == 0 only; each SM then stages half of the stack tile).
+ * low (rows, 16) receives bf16(x P_e^T) when not NULL (kept for the backward pass, _grouped.py:212-214). */
 typedef struct meep2b_product {
   const void* x;
   int64_t rows, k, ldx;
@@ -132,6 +133,7 @@ typedef struct meep2b_product {
   int32_t epilogue;     /* enum meep2b_epilogue */
   void* aux;            /* SWIGLU: pre-activation out (rows, n); DSWIGLU: pre-activation in (rows, 2n) */
   int32_t sm_limit;     /* 0: one CTA per SM */
+  int32_t block_m;      /* rows per tile: 128, or 256 for the CTA-pair kernel (b_mn == 0); 0 means 128 */
 } meep2b_product;
 
 int meep2b_grouped_product(const meep2b_product* p, void* stream);

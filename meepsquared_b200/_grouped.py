@@ -85,6 +85,33 @@ def tile_map(offsets: torch.Tensor, rows: int, block_m: int = BLOCK_M):
     return tile_expert, tile_row, tiles
 
 
+class TileMaps:
+    """The tile maps of one set of offsets: built on the device on first use per tile height, then kept.
+
+    Tiles of 128 rows feed the one-CTA kernel; tiles of 256 rows the CTA-pair kernel (stacks read K-major).
+    """
+
+    def __init__(self, offsets: torch.Tensor, rows: int):
+        self.offsets, self.rows, self._maps = offsets, rows, {}
+
+    def get(self, block_m: int):
+        if block_m not in self._maps:
+            self._maps[block_m] = tile_map(self.offsets, self.rows, block_m)
+        return self._maps[block_m]
+
+
+def _pair_tiles(b_mn: int, rows: int, experts: int, k: int) -> bool:
+    """Whether a product runs on CTA pairs (tiles of 256 rows): stacks read K-major, enough rows per expert on
+    average that the wider tiles waste little, and a long enough contraction (k >= 1024) that the pair's
+    cross-CTA hand-offs at the end of each tile stay hidden; MEEP2B_PAIR=0 or 1 overrides."""
+    if b_mn != 0:
+        return False
+    forced = os.environ.get("MEEP2B_PAIR")
+    if forced in ("0", "1"):
+        return forced == "1"
+    return rows >= 384 * experts and k >= 1024
+
+
 # ------------------------------------------------------------------------------------------------ layouts
 
 def _stack_strides(weight: torch.Tensor, K: int, is_transposed: bool) -> int:
@@ -205,7 +232,9 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
     if rows == 0:
         return out, low
     if tiles is None:
-        tiles = tile_map(offsets, rows)
+        tiles = TileMaps(offsets, rows)
+    block_m = 256 if _pair_tiles(b_mn, rows, stack.shape[0], K) else 128
+    tmap = tiles.get(block_m)
     panel = up = None
     if adapters is not None:
         panel, up = adapters.operands(b_mn, backward)
@@ -218,13 +247,14 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
     p.scaling = float(scaling)
     p.bias = bias.data_ptr() if bias is not None else None
     p.offsets = offsets.data_ptr()
-    p.tile_expert, p.tile_row, p.tiles = tiles[0].data_ptr(), tiles[1].data_ptr(), tiles[2].data_ptr()
-    p.max_tiles = tiles[0].numel()
+    p.tile_expert, p.tile_row, p.tiles = tmap[0].data_ptr(), tmap[1].data_ptr(), tmap[2].data_ptr()
+    p.max_tiles = tmap[0].numel()
     p.out, p.ldo = out.data_ptr(), out.stride(0)
     p.low = low.data_ptr() if low is not None else None
     p.epilogue = epilogue
     p.aux = aux.data_ptr() if aux is not None else None
     p.sm_limit = 0
+    p.block_m = block_m
     observer = _launch_observer
     if observer is not None:
         observer.before(x)
@@ -278,7 +308,7 @@ class _LoraGroupedProduct(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, scale, offsets, is_transposed, lhs, rhs, scaling, bias, products_fp8):
         adapters = _Adapters(lhs.detach(), rhs.detach(), is_transposed) if lhs is not None else None
-        tiles = tile_map(offsets, x.shape[0])
+        tiles = TileMaps(offsets, x.shape[0])
         out, low = _launch(x, weight, scale, offsets, not is_transposed, adapters, scaling, bias, True, tiles=tiles)
         ctx.save_for_backward(x, weight, offsets, *((low,) if low is not None else ()))
         ctx.adapters, ctx.scale, ctx.is_transposed, ctx.scaling, ctx.tiles = adapters, scale, is_transposed, scaling, tiles

@@ -28,6 +28,7 @@ class Product(ctypes.Structure):
         ("scale", _p), ("panel", _p), ("up", _p), ("scaling", _f32), ("bias", _p),
         ("offsets", _p), ("tile_expert", _p), ("tile_row", _p), ("tiles", _p), ("max_tiles", _i64),
         ("out", _p), ("ldo", _i64), ("low", _p), ("epilogue", _i32), ("aux", _p), ("sm_limit", _i32),
+        ("block_m", _i32),
     ]
 
 

@@ -40,7 +40,7 @@ class Routing:
 
     def tile_map(self):
         if self.tiles is None:
-            self.tiles = _grouped.tile_map(self.offsets, self.perm.numel())
+            self.tiles = _grouped.TileMaps(self.offsets, self.perm.numel())
         return self.tiles
 
 

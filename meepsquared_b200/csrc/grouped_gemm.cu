@@ -1,19 +1,26 @@
 // The grouped product of the expert layer on sm_100a: a persistent, warp-specialised tcgen05 GEMM.
 //
 // Replaces _grouped_gemm_kernel and _launch (meepsquared/_grouped.py:121-221, 313-345). Rows are sorted by expert;
-// a work unit is (tile of 128 rows of one expert, block of 192 output columns). Per CTA (one per SM):
+// a work unit is (tile of 128 rows of one expert, block of 192 output columns). Per CTA (one per SM, 12 warps):
 //   warp 0      TMA producer: x tile (128 x 64), the stack tile (192 x 64) with the rank-16 adapter panel P_e
-//               riding along as 16 extra rows (K-major) or a 4th column chunk (MN-major), 4-stage ring;
+//               riding along as 16 extra rows (K-major) or a 4th column chunk (MN-major); a ring of 5 (K-major)
+//               or 4 (MN-major) stages; after a unit's k-steps, the adapter's up factor U_e for its columns;
 //   warp 1      TMEM owner and MMA issuer: per k-step 4 x tcgen05.mma M=128 N=208 K=16 into one of two
 //               accumulators (columns 0..191 the product, 192..207 the panel low = x P_e^T); at the end of the
 //               unit two more MMAs of depth 16 add (s low / scale_e) U_e^T into the product, the panel split
 //               into hi and lo bf16 planes so that it keeps ~16 bits;
-//   warps 4-7   epilogue: TMEM -> registers, scale, bias, (Swi)GLU, bf16, global stores; they also turn the
-//               panel into the bf16 operand of that last MMA and store `low` for the backward pass.
+//   warps 2-3   idle;
+//   warps 4-11  epilogue, two warps per TMEM lane quarter, each on half of the unit's columns: TMEM ->
+//               registers, scale, bias, SwiGLU or its backward, bf16, global stores; the first four also turn the
+//               panel into the bf16 operand of the last MMAs and store `low` for the backward pass.
 // Two accumulators (columns 0 and 256 of a 512-column TMEM allocation) let the epilogue of one unit overlap
 // the main loop of the next. Every barrier wait is bounded (common.cuh).
 #include "common.cuh"
 #include "host.hpp"
+
+#ifndef MEEP2B_KSTEP_FENCE
+#define MEEP2B_KSTEP_FENCE 1
+#endif
 
 namespace meep2b {
 namespace gemm {
@@ -22,22 +29,30 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int BN = 192;
 constexpr int RP = 16;  // rank panel width: the LoRA rank padded to 16
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;    // 16 KB
-constexpr int B_BYTES = 4 * 64 * BK * 2;  // 32 KB: room for 4 MN-major chunks (K-major uses 208 rows x 128 B)
-constexpr int U_BYTES = BN * RP * 2;    // 6 KB
+constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+constexpr int U_BYTES = BN * RP * 2;      // 6 KB
 constexpr int LOW_BYTES = 2 * BM * RP * 2;  // 8 KB: the panel as two bf16 planes, hi and lo
-constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-constexpr int OFF_U = OFF_B + STAGES * B_BYTES;
-constexpr int OFF_LOW = OFF_U + 2 * U_BYTES;
-constexpr int OFF_BAR = OFF_LOW + 2 * LOW_BYTES;
-constexpr int NUM_BARS = 2 * STAGES + 13;
-constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
-constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + slack to align the base to 1024
-constexpr int THREADS = 256;
+constexpr int THREADS = 384;
+constexpr int EPI_WARP0 = 4;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int ACC_STRIDE = 256;
+
+// Shared-memory plan per mode. K-major: the B tile is 208 rows of 128 bytes; MN-major: four 64-column chunks.
+template <bool B_MN>
+struct Plan {
+  static constexpr int STAGES = B_MN ? 4 : 5;  // the most that fit beside the adapter buffers
+  static constexpr int B_BYTES = B_MN ? 4 * 64 * BK * 2 : (BN + RP) * BK * 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_U = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_LOW = OFF_U + U_BYTES;
+  static constexpr int OFF_BAR = OFF_LOW + LOW_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 10;
+  static constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + slack to align the base to 1024
+  static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
+  static_assert(B_BYTES % 1024 == 0 && OFF_U % 1024 == 0 && OFF_LOW % 1024 == 0, "swizzle atoms need 1 KB alignment");
+};
 
 struct Params {
   int rows, K, N, nblocks, kblocks, inter;
@@ -52,31 +67,355 @@ struct Params {
   __nv_bfloat16* out;
   __nv_bfloat16* low;
   __nv_bfloat16* aux;
+  bool v8;  // out, aux and low rows 32-byte aligned: whole-sector stores
 };
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+// silu(g) = g / (1 + exp(-g)) with the fast exponential and division intrinsics; the result is rounded to bf16.
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+__device__ __forceinline__ float sigmoid_f(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
+
+__device__ __forceinline__ void store32(__nv_bfloat16* dst, const uint32_t (&w)[16], int cnt) {
+  if (cnt == 32) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) d4[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  } else {
+    for (int j = 0; j < cnt; ++j)
+      dst[j] = __ushort_as_bfloat16(static_cast<unsigned short>(w[j >> 1] >> ((j & 1) * 16)));
+  }
+}
+
+__device__ __forceinline__ void store16(__nv_bfloat16* dst, const uint32_t (&w)[8], int cnt) {
+  if (cnt == 16) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  } else {
+    for (int j = 0; j < cnt; ++j)
+      dst[j] = __ushort_as_bfloat16(static_cast<unsigned short>(w[j >> 1] >> ((j & 1) * 16)));
+  }
+}
+
+// 32 bf16 of a row as 16 packed words; elements past cnt read as zero.
+__device__ __forceinline__ void load32(const __nv_bfloat16* src, int cnt, uint32_t (&w)[16]) {
+  if (cnt == 32) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 a = s4[j];
+      w[4 * j] = a.x, w[4 * j + 1] = a.y, w[4 * j + 2] = a.z, w[4 * j + 3] = a.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t lo = 2 * j < cnt ? __bfloat16_as_ushort(src[2 * j]) : 0u;
+      const uint32_t hi = 2 * j + 1 < cnt ? __bfloat16_as_ushort(src[2 * j + 1]) : 0u;
+      w[j] = lo | (hi << 16);
+    }
+  }
+}
+
+// Arrival of an epilogue thread on a barrier of the MMA-issuing CTA: its own (one CTA per unit) or the pair
+// leader's (rank 0 of a CTA pair).
+template <bool PAIR>
+__device__ __forceinline__ void arrive_on(uint32_t bar) {
+  if (PAIR) {
+    mbar_arrive_remote(bar, 0);
+  } else {
+    mbar_arrive(bar);
+  }
+}
+
+// 16 bf16 (32 bytes, one DRAM sector) per store when the row is 32-byte aligned; 16-byte stores otherwise.
+__device__ __forceinline__ void put16(__nv_bfloat16* dst, const uint32_t* w, bool v8) {
+  if (v8) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]), "r"(w[1]),
+                 "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+  } else {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+// cnt (<= 16) bf16 of w to dst: whole sectors when cnt == 16, element stores at a ragged edge.
+__device__ __forceinline__ void put_n(__nv_bfloat16* dst, const uint32_t* w, int cnt, bool v8) {
+  if (cnt == 16) {
+    put16(dst, w, v8);
+  } else {
+    for (int j = 0; j < cnt; ++j)
+      dst[j] = __ushort_as_bfloat16(static_cast<unsigned short>(w[j >> 1] >> ((j & 1) * 16)));
+  }
+}
+
+// The 32 columns' raw accumulator words of this thread's row, issued without waiting (tcgen05.wait::ld joins).
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// tcgen05.wait::ld that also names the destination registers of the loads it completes, so that the compiler
+// reads them only after the wait.
+__device__ __forceinline__ void tmem_wait_regs16(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
+// The epilogue of one work unit for the 128 accumulator rows this CTA holds (TMEM lane quarter q, column half
+// `half`). row_shift: the offset of this CTA's rows within the tile (128 for the second CTA of a pair). All of a
+// thread's accumulator loads for the unit are issued before one wait (the dSwiGLU epilogue, which also reads the
+// pre-activations, pipelines them by two). Returns false when a bounded wait ran out.
+template <int EPI, bool LORA, bool PAIR>
+__device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, int row_shift, uint8_t* smem_low,
+                                              uint32_t tmem_base, int q, int half, int lane,
+                                              uint32_t bar_lowfull_ab, uint32_t bar_lowready,
+                                              uint32_t bar_tfull_ab, uint32_t bar_tempty_ab) {
+  const int r_in = q * 32 + lane;
+  const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+  const int t = u / p.nblocks, nb = u - t * p.nblocks;
+  const int e = p.tile_expert[t];
+  const int row = p.tile_row[t] + row_shift + r_in;
+  const bool valid = row < p.offsets[e];
+  const int ab = it & 1;
+  const uint32_t aph = (it >> 1) & 1;
+  const float sc = p.scale != nullptr ? p.scale[e] : 1.0f;
+  const uint32_t d = tmem_base + lane_base + ab * ACC_STRIDE;
+  const int64_t orow = static_cast<int64_t>(row);
+  const bool v8 = p.v8;
+  if (LORA && half == 0) {
+    if (!mbar_wait(bar_lowfull_ab, aph)) return false;
+    tc_fence_after();
+    float lv[16];
+    tmem_ld16(d + BN, lv);
+    if (p.low != nullptr && nb == 0 && valid) {
+      uint32_t lw[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) lw[i] = pack_bf16x2(lv[2 * i], lv[2 * i + 1]);
+      put16(p.low + orow * RP, lw, v8);
+    }
+    // the A operand of the last MMAs: a = s * low / scale_e (float32) split into two bf16 planes, hi = bf16(a)
+    // and lo = bf16(a - hi), K-major with the 32-byte swizzle (16-byte halves of a row swap on rows 4-7 of 8)
+    const float f = p.scaling / sc;
+    uint32_t hw[8], lo_w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a0 = lv[2 * i] * f, a1 = lv[2 * i + 1] * f;
+      hw[i] = pack_bf16x2(a0, a1);
+      lo_w[i] = pack_bf16x2(a0 - bf16_lo(hw[i]), a1 - bf16_hi(hw[i]));
+    }
+    uint8_t* low_row = smem_low + r_in * 32;
+    const int sw = (r_in >> 2) & 1;
+    *reinterpret_cast<uint4*>(low_row + (0 ^ sw) * 16) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(low_row + (1 ^ sw) * 16) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    uint8_t* lo_row = low_row + BM * RP * 2;
+    *reinterpret_cast<uint4*>(lo_row + (0 ^ sw) * 16) = make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
+    *reinterpret_cast<uint4*>(lo_row + (1 ^ sw) * 16) = make_uint4(lo_w[4], lo_w[5], lo_w[6], lo_w[7]);
+    fence_proxy_async_smem();
+    arrive_on<PAIR>(bar_lowready);
+  }
+  if (EPI == MEEP2B_EPI_SWIGLU) {
+    // gate columns 0..95 and up columns 96..191 of the accumulator; this warp takes 48 of each
+    const int n0h = nb * 96 + half * 48;
+    const int cols = min(48, p.inter - n0h);
+    uint32_t g[48], uu[48];
+    if (!mbar_wait(bar_tfull_ab, aph)) return false;
+    tc_fence_after();
+    if (cols > 0) {
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        tmem_ld16_async(d + half * 48 + 16 * c, g + 16 * c);
+        tmem_ld16_async(d + 96 + half * 48 + 16 * c, uu + 16 * c);
+      }
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        tmem_wait_regs16(g + 16 * c);
+        tmem_wait_regs16(uu + 16 * c);
+      }
+    }
+    if (valid && cols > 0) {
+      const __nv_bfloat16* bias_g = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + n0h : nullptr;
+      __nv_bfloat16* pre = p.aux + orow * p.ld_aux + n0h;
+      __nv_bfloat16* hrow = p.out + orow * p.ldo + n0h;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const int cnt = min(16, cols - 16 * c);
+        if (cnt <= 0) break;
+        uint32_t gw[8], uw[8], hw[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = 16 * c + 2 * j;
+          float g0 = __uint_as_float(g[k]) * sc, g1 = __uint_as_float(g[k + 1]) * sc;
+          float u0 = __uint_as_float(uu[k]) * sc, u1 = __uint_as_float(uu[k + 1]) * sc;
+          if (bias_g != nullptr && 2 * j + 1 < cnt) {
+            g0 += __bfloat162float(bias_g[k]);
+            g1 += __bfloat162float(bias_g[k + 1]);
+            u0 += __bfloat162float(bias_g[p.inter + k]);
+            u1 += __bfloat162float(bias_g[p.inter + k + 1]);
+          }
+          gw[j] = pack_bf16x2(g0, g1);
+          uw[j] = pack_bf16x2(u0, u1);
+          const float a0 = bf16_round(silu_f(bf16_lo(gw[j]))), a1 = bf16_round(silu_f(bf16_hi(gw[j])));
+          hw[j] = pack_bf16x2(a0 * bf16_lo(uw[j]), a1 * bf16_hi(uw[j]));
+        }
+        put_n(pre + 16 * c, gw, cnt, v8);
+        put_n(pre + p.inter + 16 * c, uw, cnt, v8);
+        put_n(hrow + 16 * c, hw, cnt, v8);
+      }
+    }
+  } else if (EPI == MEEP2B_EPI_PLAIN) {
+    const int n0 = nb * BN + half * 96;
+    const int cols = min(96, p.N - n0);
+    uint32_t v[96];
+    if (!mbar_wait(bar_tfull_ab, aph)) return false;
+    tc_fence_after();
+    if (cols > 0) {
+      tmem_ld32_async(d + half * 96, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld32_async(d + half * 96 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_ld32_async(d + half * 96 + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
+#pragma unroll
+      for (int c = 0; c < 6; ++c) tmem_wait_regs16(v + 16 * c);
+    }
+    if (valid && cols > 0) {
+      const __nv_bfloat16* bias = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + n0 : nullptr;
+      __nv_bfloat16* dst = p.out + orow * p.ldo + n0;
+#pragma unroll
+      for (int c = 0; c < 6; ++c) {
+        const int cnt = min(16, cols - 16 * c);
+        if (cnt <= 0) break;
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = 16 * c + 2 * j;
+          float a = __uint_as_float(v[k]) * sc, b = __uint_as_float(v[k + 1]) * sc;
+          if (bias != nullptr && 2 * j + 1 < cnt) {
+            a += __bfloat162float(bias[k]);
+            b += __bfloat162float(bias[k + 1]);
+          }
+          w[j] = pack_bf16x2(a, b);
+        }
+        put_n(dst + 16 * c, w, cnt, v8);
+      }
+    }
+  } else {  // MEEP2B_EPI_DSWIGLU: the product is dh; aux holds (gate, up); out receives (dgate, dup)
+    // 16 columns per step, two steps in flight: the next step's accumulator words and pre-activations are
+    // requested before this step is computed
+    const int n0 = nb * BN + half * 96;
+    const int cols = min(96, p.N - n0);
+    const __nv_bfloat16* gp = p.aux + orow * p.ld_aux + n0;
+    __nv_bfloat16* outp = p.out + orow * p.ldo + n0;
+    uint32_t gw[2][8], uw[2][8], acc[2][16];
+    auto load_pre = [&](int c, int b) {
+      const int cnt = min(16, cols - 16 * c);
+      if (cnt == 16) {
+        const uint4 a0 = reinterpret_cast<const uint4*>(gp + 16 * c)[0], a1 = reinterpret_cast<const uint4*>(gp + 16 * c)[1];
+        const uint4 b0 = reinterpret_cast<const uint4*>(gp + p.N + 16 * c)[0];
+        const uint4 b1 = reinterpret_cast<const uint4*>(gp + p.N + 16 * c)[1];
+        gw[b][0] = a0.x, gw[b][1] = a0.y, gw[b][2] = a0.z, gw[b][3] = a0.w;
+        gw[b][4] = a1.x, gw[b][5] = a1.y, gw[b][6] = a1.z, gw[b][7] = a1.w;
+        uw[b][0] = b0.x, uw[b][1] = b0.y, uw[b][2] = b0.z, uw[b][3] = b0.w;
+        uw[b][4] = b1.x, uw[b][5] = b1.y, uw[b][6] = b1.z, uw[b][7] = b1.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = 16 * c + 2 * j;
+          const uint32_t g0 = 2 * j < cnt ? __bfloat16_as_ushort(gp[k]) : 0u;
+          const uint32_t g1 = 2 * j + 1 < cnt ? __bfloat16_as_ushort(gp[k + 1]) : 0u;
+          const uint32_t u0 = 2 * j < cnt ? __bfloat16_as_ushort(gp[p.N + k]) : 0u;
+          const uint32_t u1 = 2 * j + 1 < cnt ? __bfloat16_as_ushort(gp[p.N + k + 1]) : 0u;
+          gw[b][j] = g0 | (g1 << 16);
+          uw[b][j] = u0 | (u1 << 16);
+        }
+      }
+    };
+    if (valid && cols > 0) load_pre(0, 0);
+    if (!mbar_wait(bar_tfull_ab, aph)) return false;
+    tc_fence_after();
+    if (cols > 0) {
+      tmem_ld16_async(d + half * 96, acc[0]);
+      tmem_wait_regs16(acc[0]);
+    }
+#pragma unroll
+    for (int c = 0; c < 6; ++c) {
+      const int cnt = min(16, cols - 16 * c);
+      if (cnt <= 0) break;
+      const int b = c & 1;
+      const bool more = c < 5 && cols - 16 * (c + 1) > 0;
+      if (more) {
+        tmem_ld16_async(d + half * 96 + 16 * (c + 1), acc[b ^ 1]);
+        if (valid) load_pre(c + 1, b ^ 1);
+      }
+      if (valid) {
+        uint32_t dgw[8], duw[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float dgo[2], duo[2];
+#pragma unroll
+          for (int hlf = 0; hlf < 2; ++hlf) {
+            const float gb = hlf ? bf16_hi(gw[b][j]) : bf16_lo(gw[b][j]);
+            const float ub = hlf ? bf16_hi(uw[b][j]) : bf16_lo(uw[b][j]);
+            const float dh = bf16_round(__uint_as_float(acc[b][2 * j + hlf]) * sc);
+            const float sig = sigmoid_f(gb);  // one exponential and one reciprocal per element
+            const float act = bf16_round(gb * sig);
+            const float dact = bf16_round(dh * ub);
+            duo[hlf] = dh * act;
+            dgo[hlf] = dact * sig * (1.0f + gb * (1.0f - sig));
+          }
+          dgw[j] = pack_bf16x2(dgo[0], dgo[1]);
+          duw[j] = pack_bf16x2(duo[0], duo[1]);
+        }
+        put_n(outp + 16 * c, dgw, cnt, v8);
+        put_n(outp + p.N + 16 * c, duw, cnt, v8);
+      }
+      if (more) tmem_wait_regs16(acc[b ^ 1]);
+    }
+  }
+  tc_fence_before();
+  arrive_on<PAIR>(bar_tempty_ab);
+  return true;
+}
 
 template <bool B_MN, bool LORA, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_u,
                         const Params p) {
+  using P = Plan<B_MN>;
+  constexpr int STAGES = P::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const uint32_t bar0 = sbase + OFF_BAR;
+  const uint32_t bar0 = sbase + P::OFF_BAR;
   auto bar_full = [&](int s) { return bar0 + 8u * s; };
   auto bar_empty = [&](int s) { return bar0 + 8u * (STAGES + s); };
   auto bar_tfull = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
   auto bar_tempty = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
   auto bar_lowfull = [&](int b) { return bar0 + 8u * (2 * STAGES + 4 + b); };
-  auto bar_lowready = [&](int b) { return bar0 + 8u * (2 * STAGES + 6 + b); };
-  auto bar_ufull = [&](int b) { return bar0 + 8u * (2 * STAGES + 8 + b); };
-  auto bar_uempty = [&](int b) { return bar0 + 8u * (2 * STAGES + 10 + b); };
-  const uint32_t bar_drain = bar0 + 8u * (2 * STAGES + 12);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+  const uint32_t bar_lowready = bar0 + 8u * (2 * STAGES + 6);
+  const uint32_t bar_ufull = bar0 + 8u * (2 * STAGES + 7);
+  const uint32_t bar_uempty = bar0 + 8u * (2 * STAGES + 8);
+  const uint32_t bar_drain = bar0 + 8u * (2 * STAGES + 9);  // used only on the way out of a failed run
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + P::OFF_TMEM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -85,12 +424,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_tfull(b), 1);
-      mbar_init(bar_tempty(b), 128);
+      mbar_init(bar_tempty(b), 256);
       mbar_init(bar_lowfull(b), 1);
-      mbar_init(bar_lowready(b), 128);
-      mbar_init(bar_ufull(b), 1);
-      mbar_init(bar_uempty(b), 1);
     }
+    mbar_init(bar_lowready, 128);
+    mbar_init(bar_ufull, 1);
+    mbar_init(bar_uempty, 1);
     mbar_init(bar_drain, 1);
     fence_barrier_init();
   }
@@ -104,7 +443,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int total = (*p.tiles) * p.nblocks;
-  constexpr int NW = BN;  // output columns per unit (SwiGLU: 96 gate + 96 up)
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------------------ TMA producer
@@ -115,7 +453,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_prefetch_desc(&tm_p);
         tma_prefetch_desc(&tm_u);
       }
-      constexpr uint32_t B_TX = 64 * NW * 2 + (LORA ? (B_MN ? 64 * 64 * 2 : RP * 64 * 2) : 0);
+      constexpr uint32_t B_TX = 64 * BN * 2 + (LORA ? (B_MN ? 64 * 64 * 2 : RP * 64 * 2) : 0);
       constexpr uint32_t STAGE_TX = A_BYTES + B_TX;
       int stage = 0;
       uint32_t phase = 0;
@@ -127,29 +465,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++it) {
         const int t = u / p.nblocks, nb = u - t * p.nblocks;
         const int e = p.tile_expert[t], row0 = p.tile_row[t];
-        if (LORA) {
-          const int ub = it & 1;
-          const uint32_t uph = (it >> 1) & 1;
-          if (!mbar_wait(bar_uempty(ub), uph ^ 1)) { ok = false; break; }
-          const uint32_t dst = sbase + OFF_U + ub * U_BYTES;
-          mbar_arrive_expect_tx(bar_ufull(ub), U_BYTES);
-          if (!B_MN) {
-            if (EPI == MEEP2B_EPI_SWIGLU) {
-              tma_load_3d(dst, &tm_u, bar_ufull(ub), 0, nb * 96, e);
-              tma_load_3d(dst + 96 * RP * 2, &tm_u, bar_ufull(ub), 0, p.inter + nb * 96, e);
-            } else {
-              tma_load_3d(dst, &tm_u, bar_ufull(ub), 0, nb * BN, e);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 3; ++j) tma_load_3d(dst + j * 2048, &tm_u, bar_ufull(ub), nb * BN + 64 * j, 0, e);
-          }
-        }
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait(bar_empty(stage), phase ^ 1)) { ok = false; break; }
           const uint32_t fb = bar_full(stage);
-          const uint32_t a_dst = sbase + OFF_A + stage * A_BYTES;
-          const uint32_t b_dst = sbase + OFF_B + stage * B_BYTES;
+          const uint32_t a_dst = sbase + P::OFF_A + stage * A_BYTES;
+          const uint32_t b_dst = sbase + P::OFF_B + stage * P::B_BYTES;
           mbar_arrive_expect_tx(fb, STAGE_TX);
           tma_load_2d(a_dst, &tm_x, fb, kb * BK, row0);
           if (!B_MN) {
@@ -172,6 +492,25 @@ __global__ void __launch_bounds__(THREADS, 1)
             phase ^= 1;
           }
         }
+        if (!ok) break;
+        if (LORA) {
+          // the up factor for this unit's columns, after its k-steps: the previous unit's last MMAs are done with
+          // the single U buffer well before the producer, a ring ahead of the MMAs, gets here
+          if (!mbar_wait(bar_uempty, (it & 1) ^ 1)) { ok = false; break; }
+          const uint32_t dst = sbase + P::OFF_U;
+          mbar_arrive_expect_tx(bar_ufull, U_BYTES);
+          if (!B_MN) {
+            if (EPI == MEEP2B_EPI_SWIGLU) {
+              tma_load_3d(dst, &tm_u, bar_ufull, 0, nb * 96, e);
+              tma_load_3d(dst + 96 * RP * 2, &tm_u, bar_ufull, 0, p.inter + nb * 96, e);
+            } else {
+              tma_load_3d(dst, &tm_u, bar_ufull, 0, nb * BN, e);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 3; ++j) tma_load_3d(dst + j * 2048, &tm_u, bar_ufull, nb * BN + 64 * j, 0, e);
+          }
+        }
       }
       if (!ok) {
         // a partner is gone: let this thread's copies in flight land before the CTA's shared memory goes away
@@ -188,6 +527,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       int it = 0;
+      // The adapter MMAs of a unit wait for the epilogue to turn its panel into bf16 planes. Rather than idle
+      // meanwhile, the issuer starts the next unit's main loop (in the other accumulator) and issues the pending
+      // unit's adapter MMAs as soon as the panel is ready, tested between k-steps.
+      int pend = -1;
+      auto issue_up = [&](bool block) -> bool {
+        const uint32_t par = static_cast<uint32_t>(pend) & 1;
+        if (block) {
+          if (!mbar_wait(bar_lowready, par) || !mbar_wait(bar_ufull, par)) return false;
+        } else if (!mbar_test(bar_lowready, par) || !mbar_test(bar_ufull, par)) {
+          return true;  // not yet: try again after the next k-step
+        }
+        tc_fence_after();
+        const uint32_t dp = tmem_base + (pend & 1) * ACC_STRIDE;
+        const uint32_t low_addr = sbase + P::OFF_LOW;
+        const uint32_t u_addr = sbase + P::OFF_U;
+        const uint64_t bdesc = B_MN ? smem_desc(u_addr, 2048, 1024, 2) : smem_desc(u_addr, 16, 256, 6);
+        mma_bf16(dp, smem_desc(low_addr, 16, 256, 6), bdesc, IDESC_UP, 1);             // hi plane
+        mma_bf16(dp, smem_desc(low_addr + BM * RP * 2, 16, 256, 6), bdesc, IDESC_UP, 1);  // lo plane
+        mma_commit(bar_uempty);
+        mma_commit(bar_tfull(pend & 1));
+        pend = -1;
+        return true;
+      };
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++it) {
         const int ab = it & 1;
         const uint32_t aph = (it >> 1) & 1;
@@ -196,9 +558,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t d = tmem_base + ab * ACC_STRIDE;
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait(bar_full(stage), phase)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a_addr = sbase + OFF_A + stage * A_BYTES;
-          const uint32_t b_addr = sbase + OFF_B + stage * B_BYTES;
+          if (MEEP2B_KSTEP_FENCE) tc_fence_after();
+          const uint32_t a_addr = sbase + P::OFF_A + stage * A_BYTES;
+          const uint32_t b_addr = sbase + P::OFF_B + stage * P::B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024, 2);
@@ -211,231 +573,34 @@ __global__ void __launch_bounds__(THREADS, 1)
             stage = 0;
             phase ^= 1;
           }
+          if (LORA && pend >= 0 && !issue_up(false)) { ok = false; break; }
         }
         if (!ok) break;
         if (LORA) {
-          mma_commit(bar_lowfull(ab));
-          if (!mbar_wait(bar_lowready(ab), aph)) { ok = false; break; }
-          if (!mbar_wait(bar_ufull(ab), aph)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t low_addr = sbase + OFF_LOW + ab * LOW_BYTES;
-          const uint32_t u_addr = sbase + OFF_U + ab * U_BYTES;
-          const uint64_t bdesc = B_MN ? smem_desc(u_addr, 2048, 1024, 2) : smem_desc(u_addr, 16, 256, 6);
-          mma_bf16(d, smem_desc(low_addr, 16, 256, 6), bdesc, IDESC_UP, 1);             // hi plane
-          mma_bf16(d, smem_desc(low_addr + BM * RP * 2, 16, 256, 6), bdesc, IDESC_UP, 1);  // lo plane
-          mma_commit(bar_uempty(ab));
+          if (pend >= 0 && !issue_up(true)) { ok = false; break; }
+          mma_commit(bar_lowfull(ab));  // this unit's panel is in tensor memory: the epilogue may convert it
+          pend = it;
+        } else {
+          mma_commit(bar_tfull(ab));
         }
-        mma_commit(bar_tfull(ab));
       }
+      if (ok && LORA && pend >= 0) ok = issue_up(true);
       if (!ok) {
         // let the MMAs already issued finish before tensor memory is released
         mma_commit(bar_drain);
         mbar_wait_drain(bar_drain, 0);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= EPI_WARP0) {
     // ------------------------------------------------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int r_in = q * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int q = warp & 3;                    // TMEM lane quarter this warp may read
+    const int half = (warp - EPI_WARP0) >> 2;  // which half of the unit's columns
     int it = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++it) {
-      const int t = u / p.nblocks, nb = u - t * p.nblocks;
-      const int e = p.tile_expert[t];
-      const int row = p.tile_row[t] + r_in;
-      const bool valid = row < p.offsets[e];
       const int ab = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      const float sc = p.scale != nullptr ? p.scale[e] : 1.0f;
-      const uint32_t d = tmem_base + lane_base + ab * ACC_STRIDE;
-      if (LORA) {
-        if (!mbar_wait(bar_lowfull(ab), aph)) break;
-        tc_fence_after();
-        float lv[16];
-        tmem_ld16(d + BN, lv);
-        uint32_t lw[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) lw[i] = pack_bf16x2(lv[2 * i], lv[2 * i + 1]);
-        if (p.low != nullptr && nb == 0 && valid) {
-          uint4* dst = reinterpret_cast<uint4*>(p.low + static_cast<int64_t>(row) * RP);
-          dst[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-          dst[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-        }
-        // the A operand of the last MMAs: a = s * low / scale_e (float32) split into two bf16 planes, hi = bf16(a)
-        // and lo = bf16(a - hi), so the adapter's second product keeps ~16 bits of the panel, not 8.
-        // K-major with the 32-byte swizzle.
-        const float f = p.scaling / sc;
-        uint32_t hw[8], lo_w[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a0 = lv[2 * i] * f, a1 = lv[2 * i + 1] * f;
-          hw[i] = pack_bf16x2(a0, a1);
-          lo_w[i] = pack_bf16x2(a0 - bf16_lo(hw[i]), a1 - bf16_hi(hw[i]));
-        }
-        uint8_t* low_row = smem + OFF_LOW + ab * LOW_BYTES + r_in * 32;
-        const int sw = (r_in >> 2) & 1;
-        *reinterpret_cast<uint4*>(low_row + (0 ^ sw) * 16) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(low_row + (1 ^ sw) * 16) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-        uint8_t* lo_row = low_row + BM * RP * 2;
-        *reinterpret_cast<uint4*>(lo_row + (0 ^ sw) * 16) = make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
-        *reinterpret_cast<uint4*>(lo_row + (1 ^ sw) * 16) = make_uint4(lo_w[4], lo_w[5], lo_w[6], lo_w[7]);
-        fence_proxy_async_smem();
-        mbar_arrive(bar_lowready(ab));
-      }
-      if (!mbar_wait(bar_tfull(ab), aph)) break;
-      tc_fence_after();
-      const int64_t orow = static_cast<int64_t>(row);
-      if (EPI == MEEP2B_EPI_PLAIN) {
-        const int n0 = nb * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int col = n0 + 32 * c;
-          if (col >= p.N) break;
-          float v[32];
-          tmem_ld32(d + 32 * c, v);
-          if (valid) {
-            const __nv_bfloat16* bias = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + col : nullptr;
-            __nv_bfloat16* dst = p.out + orow * p.ldo + col;
-            if (col + 32 <= p.N) {
-              uint32_t w[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                float a = v[2 * j] * sc, b = v[2 * j + 1] * sc;
-                if (bias != nullptr) {
-                  a += __bfloat162float(bias[2 * j]);
-                  b += __bfloat162float(bias[2 * j + 1]);
-                }
-                w[j] = pack_bf16x2(a, b);
-              }
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) d4[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-            } else {
-              for (int j = 0; j < p.N - col; ++j) {
-                float a = v[j] * sc;
-                if (bias != nullptr) a += __bfloat162float(bias[j]);
-                dst[j] = __float2bfloat16_rn(a);
-              }
-            }
-          }
-        }
-      } else if (EPI == MEEP2B_EPI_SWIGLU) {
-        const int n0h = nb * 96;
-#pragma unroll 1
-        for (int c = 0; c < 3; ++c) {
-          const int col = n0h + 32 * c;
-          if (col >= p.inter) break;
-          float g[32], uu[32];
-          tmem_ld32(d + 32 * c, g);
-          tmem_ld32(d + 96 + 32 * c, uu);
-          if (valid) {
-            const int cnt = min(32, p.inter - col);
-            const __nv_bfloat16* bias_g =
-                p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + col : nullptr;
-            __nv_bfloat16* pre = p.aux + orow * p.ld_aux;
-            __nv_bfloat16* h = p.out + orow * p.ldo + col;
-            uint32_t gw[16], uw[16], hw[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float g0 = g[2 * j] * sc, g1 = g[2 * j + 1] * sc;
-              float u0 = uu[2 * j] * sc, u1 = uu[2 * j + 1] * sc;
-              if (bias_g != nullptr && 2 * j + 1 < cnt) {
-                g0 += __bfloat162float(bias_g[2 * j]);
-                g1 += __bfloat162float(bias_g[2 * j + 1]);
-                u0 += __bfloat162float(bias_g[p.inter + 2 * j]);
-                u1 += __bfloat162float(bias_g[p.inter + 2 * j + 1]);
-              }
-              gw[j] = pack_bf16x2(g0, g1);
-              uw[j] = pack_bf16x2(u0, u1);
-              const float a0 = bf16_round(silu_f(bf16_lo(gw[j]))), a1 = bf16_round(silu_f(bf16_hi(gw[j])));
-              hw[j] = pack_bf16x2(a0 * bf16_lo(uw[j]), a1 * bf16_hi(uw[j]));
-            }
-            if (cnt == 32) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                reinterpret_cast<uint4*>(pre + col)[j] = make_uint4(gw[4 * j], gw[4 * j + 1], gw[4 * j + 2], gw[4 * j + 3]);
-                reinterpret_cast<uint4*>(pre + p.inter + col)[j] =
-                    make_uint4(uw[4 * j], uw[4 * j + 1], uw[4 * j + 2], uw[4 * j + 3]);
-                reinterpret_cast<uint4*>(h)[j] = make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
-              }
-            } else {
-              for (int j = 0; j < cnt; ++j) {
-                const uint32_t sh = (j & 1) * 16;
-                pre[col + j] = __ushort_as_bfloat16(static_cast<unsigned short>(gw[j >> 1] >> sh));
-                pre[p.inter + col + j] = __ushort_as_bfloat16(static_cast<unsigned short>(uw[j >> 1] >> sh));
-                h[j] = __ushort_as_bfloat16(static_cast<unsigned short>(hw[j >> 1] >> sh));
-              }
-            }
-          }
-        }
-      } else {  // MEEP2B_EPI_DSWIGLU: the product is dh; aux holds (gate, up); out receives (dgate, dup)
-        const int n0 = nb * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int col = n0 + 32 * c;
-          if (col >= p.N) break;
-          float v[32];
-          tmem_ld32(d + 32 * c, v);
-          if (valid) {
-            const int cnt = min(32, p.N - col);
-            const __nv_bfloat16* gp = p.aux + orow * p.ld_aux + col;
-            const __nv_bfloat16* up = gp + p.N;
-            __nv_bfloat16* dg = p.out + orow * p.ldo + col;
-            __nv_bfloat16* du = dg + p.N;
-            uint32_t gw[16], uw[16], dgw[16], duw[16];
-            if (cnt == 32) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 a = reinterpret_cast<const uint4*>(gp)[j], b = reinterpret_cast<const uint4*>(up)[j];
-                gw[4 * j] = a.x, gw[4 * j + 1] = a.y, gw[4 * j + 2] = a.z, gw[4 * j + 3] = a.w;
-                uw[4 * j] = b.x, uw[4 * j + 1] = b.y, uw[4 * j + 2] = b.z, uw[4 * j + 3] = b.w;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const uint32_t g0 = 2 * j < cnt ? __bfloat16_as_ushort(gp[2 * j]) : 0u;
-                const uint32_t g1 = 2 * j + 1 < cnt ? __bfloat16_as_ushort(gp[2 * j + 1]) : 0u;
-                const uint32_t u0 = 2 * j < cnt ? __bfloat16_as_ushort(up[2 * j]) : 0u;
-                const uint32_t u1 = 2 * j + 1 < cnt ? __bfloat16_as_ushort(up[2 * j + 1]) : 0u;
-                gw[j] = g0 | (g1 << 16);
-                uw[j] = u0 | (u1 << 16);
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float dgo[2], duo[2];
-#pragma unroll
-              for (int hlf = 0; hlf < 2; ++hlf) {
-                const float gb = hlf ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
-                const float ub = hlf ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
-                const float dh = bf16_round(v[2 * j + hlf] * sc);
-                const float sig = 1.0f / (1.0f + expf(-gb));
-                const float act = bf16_round(silu_f(gb));
-                const float dact = bf16_round(dh * ub);
-                duo[hlf] = dh * act;
-                dgo[hlf] = dact * sig * (1.0f + gb * (1.0f - sig));
-              }
-              dgw[j] = pack_bf16x2(dgo[0], dgo[1]);
-              duw[j] = pack_bf16x2(duo[0], duo[1]);
-            }
-            if (cnt == 32) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                reinterpret_cast<uint4*>(dg)[j] = make_uint4(dgw[4 * j], dgw[4 * j + 1], dgw[4 * j + 2], dgw[4 * j + 3]);
-                reinterpret_cast<uint4*>(du)[j] = make_uint4(duw[4 * j], duw[4 * j + 1], duw[4 * j + 2], duw[4 * j + 3]);
-              }
-            } else {
-              for (int j = 0; j < cnt; ++j) {
-                const uint32_t sh = (j & 1) * 16;
-                dg[j] = __ushort_as_bfloat16(static_cast<unsigned short>(dgw[j >> 1] >> sh));
-                du[j] = __ushort_as_bfloat16(static_cast<unsigned short>(duw[j >> 1] >> sh));
-              }
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(bar_tempty(ab));
+      if (!epilogue_unit<EPI, LORA, false>(p, u, it, 0, smem + P::OFF_LOW, tmem_base, q, half, lane, bar_lowfull(ab),
+                                           bar_lowready, bar_tfull(ab), bar_tempty(ab)))
+        break;
     }
   }
 
@@ -447,19 +612,271 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2) for stacks read K-major. A work unit is 256 rows of one expert by 192
+// columns. CTA r of the pair loads rows 128r..128r+127 of the x tile and rows 104r..104r+103 of the 208-row B tile
+// (the 192 stack rows, then the 16 panel rows), so each SM stages half of B; the pair leader issues M=256 N=208
+// MMAs that write both CTAs' tensor memory (each holds its 128 rows of the 208 columns). The epilogue is the
+// same per CTA. All loads are plain TMA tile loads into the loading CTA's own shared memory, completing on the
+// leader's barrier; there is no multicast.
+#ifndef MEEP2B_PAIR_STAGES
+#define MEEP2B_PAIR_STAGES 7
+#endif
+constexpr int PAIR_STAGES = MEEP2B_PAIR_STAGES;
+constexpr int PAIR_B_ROWS = (BN + RP) / 2;            // 104
+constexpr int PAIR_B_BYTES = PAIR_B_ROWS * BK * 2;    // 13 KB
+constexpr int PAIR_U_BYTES = (BN / 2) * RP * 2;       // 3 KB
+constexpr int PAIR_OFF_B = PAIR_STAGES * A_BYTES;
+constexpr int PAIR_OFF_U = PAIR_OFF_B + PAIR_STAGES * PAIR_B_BYTES;
+constexpr int PAIR_OFF_LOW = PAIR_OFF_U + PAIR_U_BYTES;
+constexpr int PAIR_OFF_BAR = PAIR_OFF_LOW + LOW_BYTES;
+constexpr int PAIR_NUM_BARS = 2 * PAIR_STAGES + 10;
+constexpr int PAIR_OFF_TMEM = PAIR_OFF_BAR + PAIR_NUM_BARS * 8;
+constexpr int PAIR_SMEM_BYTES = PAIR_OFF_TMEM + 16 + 1024;
+static_assert(PAIR_SMEM_BYTES <= 232448, "pair shared memory plan exceeds 227 KB");
+static_assert(PAIR_B_BYTES % 1024 == 0 && PAIR_OFF_U % 1024 == 0 && PAIR_OFF_LOW % 1024 == 0, "1 KB alignment");
+
+struct PairMaps {
+  CUtensorMap x;     // (k, rows) box 64 x 128
+  CUtensorMap w104;  // (k, n, E) box 64 x 104
+  CUtensorMap w96;   // box 64 x 96
+  CUtensorMap w88;   // box 64 x 88
+  CUtensorMap w8;    // box 64 x 8
+  CUtensorMap p16;   // panel (k, 16, E) box 64 x 16
+  CUtensorMap u96;   // up (16, n, E) box 16 x 96, 32-byte swizzle
+};
+
+template <bool LORA, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ PairMaps m, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair_id = static_cast<int>(cluster_id_x()), pairs = static_cast<int>(num_clusters_x());
+
+  const uint32_t bar0 = sbase + PAIR_OFF_BAR;
+  auto bar_full = [&](int s) { return bar0 + 8u * s; };
+  auto bar_empty = [&](int s) { return bar0 + 8u * (PAIR_STAGES + s); };
+  auto bar_tfull = [&](int b) { return bar0 + 8u * (2 * PAIR_STAGES + b); };
+  auto bar_tempty = [&](int b) { return bar0 + 8u * (2 * PAIR_STAGES + 2 + b); };
+  auto bar_lowfull = [&](int b) { return bar0 + 8u * (2 * PAIR_STAGES + 4 + b); };
+  const uint32_t bar_lowready = bar0 + 8u * (2 * PAIR_STAGES + 6);
+  const uint32_t bar_ufull = bar0 + 8u * (2 * PAIR_STAGES + 7);
+  const uint32_t bar_uempty = bar0 + 8u * (2 * PAIR_STAGES + 8);
+  const uint32_t bar_drain = bar0 + 8u * (2 * PAIR_STAGES + 9);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PAIR_OFF_TMEM);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_tfull(b), 1);
+      mbar_init(bar_tempty(b), 512);  // 256 epilogue threads of each CTA
+      mbar_init(bar_lowfull(b), 1);
+    }
+    mbar_init(bar_lowready, 256);  // 128 per CTA
+    mbar_init(bar_ufull, 1);
+    mbar_init(bar_uempty, 1);
+    mbar_init(bar_drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival or load
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total = (*p.tiles) * p.nblocks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&m.x);
+      tma_prefetch_desc(EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? &m.w96 : &m.w88) : (rank == 0 ? &m.w104 : &m.w88));
+      // with the panel the 208 B rows split 104 / 104 (the second CTA's last 16 are the panel); without it 96 / 96
+      constexpr uint32_t CTA_TX = A_BYTES + (LORA ? PAIR_B_ROWS : BN / 2) * 128;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t last_parity[PAIR_STAGES];
+      bool issued[PAIR_STAGES];
+      for (int s = 0; s < PAIR_STAGES; ++s) issued[s] = false, last_parity[s] = 0;
+      bool ok = true;
+      int it = 0;
+      for (int u = pair_id; u < total && ok; u += pairs, ++it) {
+        const int t = u / p.nblocks, nb = u - t * p.nblocks;
+        const int e = p.tile_expert[t], row0 = p.tile_row[t] + 128 * static_cast<int>(rank);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(bar_empty(stage), phase ^ 1)) { ok = false; break; }
+          const uint32_t fb = bar_full(stage);
+          const uint32_t fb_lead = map_to_rank(fb, 0);
+          const uint32_t a_dst = sbase + stage * A_BYTES;
+          const uint32_t b_dst = sbase + PAIR_OFF_B + stage * PAIR_B_BYTES;
+          if (rank == 0) mbar_arrive_expect_tx(fb, 2 * CTA_TX);
+          tma_load_2d_pair(a_dst, &m.x, fb_lead, kb * BK, row0);
+          const int k0 = kb * BK;
+          if (EPI == MEEP2B_EPI_SWIGLU) {
+            const int g0 = nb * 96;
+            if (!LORA) {  // gate rows in the first CTA, up rows in the second
+              tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, rank == 0 ? g0 : p.inter + g0, e);
+            } else if (rank == 0) {
+              tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, g0, e);                       // gate 0..95
+              tma_load_3d_pair(b_dst + 96 * 128, &m.w8, fb_lead, k0, p.inter + g0, e);   // up 0..7
+            } else {
+              tma_load_3d_pair(b_dst, &m.w88, fb_lead, k0, p.inter + g0 + 8, e);         // up 8..95
+              tma_load_3d_pair(b_dst + 88 * 128, &m.p16, fb_lead, k0, 0, e);             // the rank panel
+            }
+          } else {
+            const int n0 = nb * BN;
+            if (!LORA) {
+              tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, n0 + 96 * static_cast<int>(rank), e);
+            } else if (rank == 0) {
+              tma_load_3d_pair(b_dst, &m.w104, fb_lead, k0, n0, e);
+            } else {
+              tma_load_3d_pair(b_dst, &m.w88, fb_lead, k0, n0 + 104, e);
+              tma_load_3d_pair(b_dst + 88 * 128, &m.p16, fb_lead, k0, 0, e);             // the rank panel
+            }
+          }
+          issued[stage] = true;
+          last_parity[stage] = phase;
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        if (LORA) {
+          if (!mbar_wait(bar_uempty, (it & 1) ^ 1)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(bar_ufull, 2 * PAIR_U_BYTES);
+          const int urow = EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? nb * 96 : p.inter + nb * 96)
+                                                    : nb * BN + 96 * static_cast<int>(rank);
+          tma_load_3d_pair(sbase + PAIR_OFF_U, &m.u96, map_to_rank(bar_ufull, 0), 0, urow, e);
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < PAIR_STAGES; ++s)
+          if (issued[s] && rank == 0) mbar_wait_drain(bar_full(s), last_parity[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t IDESC_MAIN = idesc_bf16(256, LORA ? BN + RP : BN, false, false);
+      constexpr uint32_t IDESC_UP = idesc_bf16(256, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      int pend = -1;  // as in the one-CTA kernel: a unit's adapter MMAs go out during the next unit's main loop
+      auto issue_up = [&](bool block) -> bool {
+        const uint32_t par = static_cast<uint32_t>(pend) & 1;
+        if (block) {
+          if (!mbar_wait_cluster(bar_lowready, par) || !mbar_wait(bar_ufull, par)) return false;
+        } else if (!mbar_test_cluster(bar_lowready, par) || !mbar_test(bar_ufull, par)) {
+          return true;
+        }
+        tc_fence_after();
+        const uint32_t dp = tmem_base + (pend & 1) * ACC_STRIDE;
+        const uint32_t low_addr = sbase + PAIR_OFF_LOW;
+        const uint64_t bdesc = smem_desc(sbase + PAIR_OFF_U, 16, 256, 6);
+        mma_bf16_pair(dp, smem_desc(low_addr, 16, 256, 6), bdesc, IDESC_UP, 1);             // hi plane
+        mma_bf16_pair(dp, smem_desc(low_addr + BM * RP * 2, 16, 256, 6), bdesc, IDESC_UP, 1);  // lo plane
+        mma_commit_pair(bar_uempty);
+        mma_commit_pair(bar_tfull(pend & 1));
+        pend = -1;
+        return true;
+      };
+      for (int u = pair_id; u < total && ok; u += pairs, ++it) {
+        const int ab = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait_cluster(bar_tempty(ab), aph ^ 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d = tmem_base + ab * ACC_STRIDE;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(bar_full(stage), phase)) { ok = false; break; }
+          if (MEEP2B_KSTEP_FENCE) tc_fence_after();
+          const uint32_t a_addr = sbase + stage * A_BYTES;
+          const uint32_t b_addr = sbase + PAIR_OFF_B + stage * PAIR_B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_bf16_pair(d, smem_desc(a_addr + kk * 32, 16, 1024, 2), smem_desc(b_addr + kk * 32, 16, 1024, 2),
+                          IDESC_MAIN, (kb | kk) != 0);
+          mma_commit_pair(bar_empty(stage));
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (LORA && pend >= 0 && !issue_up(false)) { ok = false; break; }
+        }
+        if (!ok) break;
+        if (LORA) {
+          if (pend >= 0 && !issue_up(true)) { ok = false; break; }
+          mma_commit_pair(bar_lowfull(ab));
+          pend = it;
+        } else {
+          mma_commit_pair(bar_tfull(ab));
+        }
+      }
+      if (ok && LORA && pend >= 0) ok = issue_up(true);
+      if (!ok) {
+        mma_commit_pair(bar_drain);
+        mbar_wait_drain(bar_drain, 0);
+      }
+    }
+  } else if (warp >= EPI_WARP0) {
+    // ------------------------------------------------------------------------------------------ epilogue (each CTA)
+    const int q = warp & 3;
+    const int half = (warp - EPI_WARP0) >> 2;
+    int it = 0;
+    for (int u = pair_id; u < total; u += pairs, ++it) {
+      const int ab = it & 1;
+      if (!epilogue_unit<EPI, LORA, true>(p, u, it, 128 * static_cast<int>(rank), smem + PAIR_OFF_LOW, tmem_base, q,
+                                          half, lane, bar_lowfull(ab), bar_lowready, bar_tfull(ab), bar_tempty(ab)))
+        break;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA releases tensor memory while the pair's MMAs or the other epilogue may still use it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+template <bool LORA, int EPI>
+static int launch_pair(const PairMaps& maps, const Params& prm, int grid, cudaStream_t s) {
+  auto kern = grouped_gemm_pair_kernel<LORA, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES) != cudaSuccess) {
+      cudaGetLastError();
+      return MEEP2B_ERR_LAUNCH;
+    }
+    configured = true;
+  }
+  kern<<<grid, THREADS, PAIR_SMEM_BYTES, s>>>(maps, prm);
+  return launch_status();
+}
+
 template <bool B_MN, bool LORA, int EPI>
 static int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tu,
                   const Params& prm, int grid, cudaStream_t s) {
   auto kern = grouped_gemm_kernel<B_MN, LORA, EPI>;
   static bool configured = false;  // per instantiation; attributes are per device but idempotent
   if (!configured) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<B_MN>::SMEM_BYTES) != cudaSuccess) {
       cudaGetLastError();
       return MEEP2B_ERR_LAUNCH;
     }
     configured = true;
   }
-  kern<<<grid, THREADS, SMEM_BYTES, s>>>(tx, tw, tp, tu, prm);
+  kern<<<grid, THREADS, Plan<B_MN>::SMEM_BYTES, s>>>(tx, tw, tp, tu, prm);
   return launch_status();
 }
 
@@ -559,12 +976,54 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   prm.out = static_cast<__nv_bfloat16*>(a->out);
   prm.low = static_cast<__nv_bfloat16*>(a->low);
   prm.aux = static_cast<__nv_bfloat16*>(a->aux);
+  auto aligned32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 31u) == 0; };
+  prm.v8 = aligned32(a->out) && (a->aux == nullptr || aligned32(a->aux)) && (a->low == nullptr || aligned32(a->low)) &&
+           a->ldo % 16 == 0 && prm.ld_aux % 16 == 0;
 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (a->sm_limit > 0 && a->sm_limit < sms) sms = a->sm_limit;
   const int64_t units = a->max_tiles * prm.nblocks;
+
+  const int block_m = a->block_m == 0 ? 128 : a->block_m;
+  if (block_m != 128 && block_m != 256) return MEEP2B_ERR_UNSUPPORTED;
+  if (block_m == 256) {
+    if (a->b_mn) return MEEP2B_ERR_UNSUPPORTED;
+    PairMaps maps;
+    maps.x = tx;
+    const uint32_t heights[4] = {104, 96, 88, 8};
+    CUtensorMap* targets[4] = {&maps.w104, &maps.w96, &maps.w88, &maps.w8};
+    for (int i = 0; i < 4; ++i) {
+      const uint64_t dims[3] = {K, N, E};
+      const uint64_t strides[2] = {K * 2, N * K * 2};
+      const uint32_t box[3] = {64, heights[i], 1};
+      MEEP2B_TRY(encode_tiled(targets[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->weight, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    if (lora) {
+      maps.p16 = tp;
+      const uint64_t ud[3] = {RP, N, E};
+      const uint64_t us[2] = {RP * 2, N * RP * 2};
+      const uint32_t ubx[3] = {RP, 96, 1};
+      MEEP2B_TRY(encode_tiled(&maps.u96, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->up, ud, us, ubx,
+                              CU_TENSOR_MAP_SWIZZLE_32B));
+    } else {
+      maps.p16 = tx;
+      maps.u96 = tx;
+    }
+    const int pairs_max = sms / 2;
+    const int64_t pairs = units < pairs_max ? (units > 0 ? units : 1) : pairs_max;
+    const int grid = static_cast<int>(2 * pairs);
+    switch (epi) {
+      case MEEP2B_EPI_PLAIN:
+        return lora ? launch_pair<true, 0>(maps, prm, grid, s) : launch_pair<false, 0>(maps, prm, grid, s);
+      case MEEP2B_EPI_SWIGLU:
+        return lora ? launch_pair<true, 1>(maps, prm, grid, s) : launch_pair<false, 1>(maps, prm, grid, s);
+      default:
+        return lora ? launch_pair<true, 2>(maps, prm, grid, s) : launch_pair<false, 2>(maps, prm, grid, s);
+    }
+  }
   const int grid = static_cast<int>(units < sms ? (units > 0 ? units : 1) : sms);
 
   const bool mn = a->b_mn != 0;

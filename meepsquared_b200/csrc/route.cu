@@ -181,30 +181,34 @@ __global__ void __launch_bounds__(256) unpermute_rows(const uint4* __restrict__ 
   }
 }
 
-// grad_y[i] = bf16(grad_out[tok] * w_g[i]); grad_weights[perm[i]] = sum_h grad_out[tok][h] * y[i][h]. One CTA per
-// routed row.
+// grad_y[i] = bf16(grad_out[tok] * w_g[i]); grad_weights[perm[i]] = sum_h grad_out[tok][h] * y[i][h]. One warp per
+// routed row, eight rows per CTA, 16-byte vectors; the dot product reduced with shuffles.
 template <typename W>
 __global__ void __launch_bounds__(256) unpermute_backward_rows(const uint4* __restrict__ grad_out,
                                                                const uint4* __restrict__ y,
                                                                const int64_t* __restrict__ perm,
                                                                const W* __restrict__ weights_g,
                                                                const int32_t* __restrict__ offsets, int experts,
-                                                               int top_k, int64_t vec_per_row,
+                                                               int top_k, int64_t rows, int64_t vec_per_row,
                                                                uint4* __restrict__ grad_y,
                                                                float* __restrict__ grad_weights) {
-  __shared__ float partial[8];
-  const int64_t i = blockIdx.x;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (i >= rows) return;
   const int64_t valid = offsets[experts - 1];
   const int64_t src = perm[i];
   const bool live = i < valid;
   const float w = live ? weight_value(weights_g, i) : 0.f;
   const bool round_bf16 = sizeof(W) == 2;
   float dot = 0.f;
-  for (int64_t v = threadIdx.x; v < vec_per_row; v += blockDim.x) {
+  const uint4* g_row = grad_out + (src / top_k) * vec_per_row;
+  const uint4* y_row = y + i * vec_per_row;
+  uint4* o_row = grad_y + i * vec_per_row;
+  for (int64_t v = lane; v < vec_per_row; v += 32) {
     uint4 o = make_uint4(0, 0, 0, 0);
     if (live) {
-      const uint4 g = __ldg(grad_out + (src / top_k) * vec_per_row + v);
-      const uint4 q = __ldg(y + i * vec_per_row + v);
+      const uint4 g = __ldg(g_row + v);
+      const uint4 q = __ldcs(y_row + v);  // read once: do not keep in L2
       const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
       const uint32_t yw[4] = {q.x, q.y, q.z, q.w};
       uint32_t ow[4];
@@ -222,17 +226,11 @@ __global__ void __launch_bounds__(256) unpermute_backward_rows(const uint4* __re
       }
       o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     }
-    grad_y[i * vec_per_row + v] = o;
+    o_row[v] = o;
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = dot;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float s = 0.f;
-    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) s += partial[k];
-    grad_weights[src] = live ? s : 0.f;
-  }
+  if (lane == 0) grad_weights[src] = live ? dot : 0.f;
 }
 
 // The tile map: tiles per expert, their running sum, and for every tile index t < max_tiles the expert (by binary
@@ -359,14 +357,14 @@ int meep2b_unpermute_backward(const void* grad_out, const void* y, const int64_t
   if (assignments == 0) return MEEP2B_OK;
   const int64_t vec = hidden_dim / 8;
   if (weights_dtype == MEEP2B_BF16)
-    unpermute_backward_rows<__nv_bfloat16><<<static_cast<unsigned>(assignments), 256, 0, s>>>(
+    unpermute_backward_rows<__nv_bfloat16><<<static_cast<unsigned>((assignments + 7) / 8), 256, 0, s>>>(
         static_cast<const uint4*>(grad_out), static_cast<const uint4*>(y), perm,
-        static_cast<const __nv_bfloat16*>(weights_g), offsets, experts, top_k, vec, static_cast<uint4*>(grad_y),
-        grad_weights);
+        static_cast<const __nv_bfloat16*>(weights_g), offsets, experts, top_k, assignments, vec,
+        static_cast<uint4*>(grad_y), grad_weights);
   else
-    unpermute_backward_rows<float><<<static_cast<unsigned>(assignments), 256, 0, s>>>(
+    unpermute_backward_rows<float><<<static_cast<unsigned>((assignments + 7) / 8), 256, 0, s>>>(
         static_cast<const uint4*>(grad_out), static_cast<const uint4*>(y), perm, static_cast<const float*>(weights_g),
-        offsets, experts, top_k, vec, static_cast<uint4*>(grad_y), grad_weights);
+        offsets, experts, top_k, assignments, vec, static_cast<uint4*>(grad_y), grad_weights);
   return launch_status();
 }
 

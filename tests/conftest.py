@@ -27,3 +27,10 @@ def golden():
         return cache[name]
 
     return load
+
+
+@pytest.fixture(params=["0", "1"], ids=["one-cta", "cta-pair"])
+def pair_mode(request, monkeypatch):
+    """Runs a product test with the one-CTA kernel and with the CTA-pair kernel (tiles of 256 rows)."""
+    monkeypatch.setenv("MEEP2B_PAIR", request.param)
+    return request.param

@@ -25,7 +25,7 @@ def offsets_of(rows_per_expert, device=DEV):
     ([3], 2048, 1024),
     ([129, 0, 0, 500, 127], 2048, 1536),
 ])
-def test_the_kernel_matches_one_product_per_expert(is_transposed, rows_per_expert, K, N):
+def test_the_kernel_matches_one_product_per_expert(is_transposed, rows_per_expert, K, N, pair_mode):
     torch.manual_seed(0)
     rows, experts = sum(rows_per_expert), len(rows_per_expert)
     x = torch.randn(rows, K, device=DEV, dtype=torch.bfloat16)
@@ -86,7 +86,7 @@ def check_lora(got, x, weight, scale, offsets, is_transposed, lhs, rhs, scaling,
 
 
 @pytest.mark.parametrize("prefix,is_transposed", [("n_", False), ("t_", True)])
-def test_lora_matches_the_reference_golden_vectors(golden, prefix, is_transposed):
+def test_lora_matches_the_reference_golden_vectors(golden, prefix, is_transposed, pair_mode):
     g = golden("grouped")
     f = {k[len(prefix):]: v for k, v in g.items() if k.startswith(prefix)}
     t = {n: torch.from_numpy(quant.bf16_to_f32(f[n])).to(torch.bfloat16) for n in ("x", "weight", "lhs", "rhs", "bias", "grad")}
@@ -103,7 +103,7 @@ def test_lora_matches_the_reference_golden_vectors(golden, prefix, is_transposed
 @pytest.mark.parametrize("rank", [4, 8, 16])
 @pytest.mark.parametrize("rows_per_expert,K,N", [([37, 0, 200, 64, 1], 96, 80), ([1000, 3, 0, 700], 2048, 1536),
                                                   ([513, 256], 768, 2048)])
-def test_lora_forward_and_backward_match_float32(is_transposed, rank, rows_per_expert, K, N):
+def test_lora_forward_and_backward_match_float32(is_transposed, rank, rows_per_expert, K, N, pair_mode):
     gen = torch.Generator().manual_seed(rank + K)
     experts = len(rows_per_expert)
     offsets = torch.cumsum(torch.tensor(rows_per_expert, dtype=torch.int32), 0, dtype=torch.int32)
@@ -143,7 +143,7 @@ def test_the_product_without_adapters_gives_the_base_and_its_input_gradient():
     assert_close(x.grad, want, "grad_x")
 
 
-def test_qwen3_shaped_products_sampled_rows():
+def test_qwen3_shaped_products_sampled_rows(pair_mode):
     """Full BASELINE config-2 product sizes (131072 routed rows, 128 experts): sampled rows against float32."""
     gen = torch.Generator(device=DEV).manual_seed(11)
     experts, rows, H, I = 128, 131072, 2048, 768

@@ -57,7 +57,7 @@ def check_against(res, want, prefix="", scaled=False):
 
 
 @pytest.mark.parametrize("sentinel", [False, True])
-def test_layer_matches_the_reference_golden_vectors(golden, sentinel):
+def test_layer_matches_the_reference_golden_vectors(golden, sentinel, pair_mode):
     res, _ = run_layer(layer_inputs.layer(**layer_inputs.SMALL), sentinel)
     check_against(res, golden("layer_small"), "sentinel_" if sentinel else "")
 
@@ -84,7 +84,7 @@ def test_layer_at_config1_matches_the_oracle_and_the_reference_slices(golden):
 
 @pytest.mark.parametrize("cfg", [dict(layer_inputs.QWEN3_30B, tokens=512), dict(layer_inputs.MIXTRAL, tokens=256),
                                  dict(layer_inputs.QWEN3_235B_FP8, tokens=256)])
-def test_layer_at_baseline_shapes_matches_the_oracle(cfg):
+def test_layer_at_baseline_shapes_matches_the_oracle(cfg, pair_mode):
     inp = layer_inputs.layer(**cfg)
     res, idx = run_layer(inp)
     check_against(res, oracle_layer(inp, idx), scaled=True)
