@@ -66,6 +66,22 @@ int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts
                  int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* workspace,
                  size_t workspace_bytes, void* stream);
 
+/* meep2b_route for callers that cannot allocate device memory; it has no counterpart in the reference. Some
+ * callers own every device buffer and have no allocator to lend this library (an FFI caller outside PyTorch, a
+ * serving process that reserves its device memory up front), or must not call cudaMalloc because it would
+ * synchronise the device or break a memory budget; they cannot supply meep2b_route's workspace. This entry point
+ * keeps the bucket-count table in a fixed 256 KB array of device memory that the library declares and that every
+ * GPU loading the library holds until the process exits; it calls no cudaMalloc, cudaFree or other allocating
+ * routine. Limit: ceil(assignments / 4096) * (experts + 1) <= 65536 (for example 262,144 assignments over up to
+ * 1023 experts, or 1,048,576 over up to 255); larger requests return MEEP2B_ERR_SHAPE before any work. The first
+ * call on a device looks up the array's device address with cudaGetSymbolAddress (with that device current) and
+ * caches it, so make that first call before any stream capture. All calls share the one array: calls that overlap
+ * on the GPU (two streams, or two host threads on one device) race and must be serialised by the caller. Outputs
+ * and arguments as meep2b_route; every table entry a call reads is written earlier in the same call, so nothing
+ * from a previous call carries over. */
+int meep2b_route_noalloc(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
+                         int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* stream);
+
 /* The gather of _moe.py:80-81,87: selected[i] = hidden[perm[i] / top_k] (bf16 rows of hidden_dim), zero for the
  * sentinel rows i >= offsets[experts-1]; weights_g[i] = weights[perm[i]] (weights_dtype F32 or BF16, same type
  * out; both may be NULL). */

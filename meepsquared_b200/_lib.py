@@ -40,6 +40,7 @@ _SIGNATURES = {
     "meep2b_sm_count": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "meep2b_route_workspace_bytes": (_sz, [_i64, _i32]),
     "meep2b_route": (ctypes.c_int, [_p, _i64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
+    "meep2b_route_noalloc": (ctypes.c_int, [_p, _i64, _i32, _p, _p, _p, _p, _p]),
     "meep2b_gather": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _i32, _p, _i32, _p, _p, _p]),
     "meep2b_unpermute": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p]),
     "meep2b_unpermute_backward": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p, _p]),

@@ -5,6 +5,8 @@
 //
 // Replaces _moe._routed_forward's sort / histc / cumsum / gather / weighted sum (meepsquared/_moe.py:75-87,
 // 123-126) and _grouped.tile_map (meepsquared/_grouped.py:88-103).
+#include <mutex>
+
 #include "common.cuh"
 #include "host.hpp"
 
@@ -380,3 +382,72 @@ int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------------
+// Routing without allocation.
+//
+// meep2b_route takes its bucket-count table as a caller-provided workspace. Some callers cannot provide one: a
+// host runtime that hands this library only the input and output buffers it owns and has no device allocator to
+// lend (an FFI caller outside PyTorch, a serving process whose device memory is reserved up front), or code that
+// must not call cudaMalloc because it would synchronise the device or break a memory budget. For them,
+// meep2b_route_noalloc keeps that table in a fixed array in device memory that this library declares at file
+// scope, so the call allocates nothing. The array lives on every GPU that loads the library until the process
+// exits. Its host-side name is only a stand-in for the symbol: the device address is fetched once per device with
+// cudaGetSymbolAddress and cached.
+namespace meep2b {
+
+constexpr int64_t kNoAllocRouteWords = 65536;  // 256 KB of int32 bucket counts
+static __device__ __align__(256) int g_route_scratch[kNoAllocRouteWords];
+
+constexpr int kMaxDevices = 64;
+static int* g_route_scratch_addr[kMaxDevices] = {nullptr};
+static std::mutex g_route_scratch_mutex;
+
+// The device address of g_route_scratch on the current device, fetched on first use (with that device current).
+static int route_scratch_address(int** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return MEEP2B_ERR_LAUNCH;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return MEEP2B_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_route_scratch_mutex);
+  if (g_route_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_route_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return MEEP2B_ERR_LAUNCH;
+    }
+    g_route_scratch_addr[dev] = static_cast<int*>(p);
+  }
+  *out = g_route_scratch_addr[dev];
+  return MEEP2B_OK;
+}
+
+}  // namespace meep2b
+
+extern "C" int meep2b_route_noalloc(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
+                                    int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* stream) {
+  using namespace meep2b;
+  if (experts < 1 || experts + 1 > kMaxBuckets || assignments < 0) return MEEP2B_ERR_SHAPE;
+  const int64_t blocks = (assignments + kRouteChunk - 1) / kRouteChunk;
+  if (blocks * (experts + 1) > kNoAllocRouteWords) return MEEP2B_ERR_SHAPE;  // beyond the fixed table
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  int* counts = nullptr;
+  MEEP2B_TRY(route_scratch_address(&counts));
+  if (assignments == 0) {
+    cudaMemsetAsync(offsets, 0, sizeof(int32_t) * experts, s);
+    return launch_status();
+  }
+  // Every entry of the table this call reads is first written by route_histogram, so nothing left over from an
+  // earlier call leaks in; nothing needs clearing.
+  const size_t hist_smem = sizeof(int) * (experts + 1);
+  route_histogram<<<static_cast<int>(blocks), kRouteThreads, hist_smem, s>>>(expert_ids, assignments, experts,
+                                                                            counts);
+  route_scan<<<1, 1024, 0, s>>>(counts, static_cast<int>(blocks), experts, offsets);
+  const size_t scatter_smem = sizeof(int) * 9 * (experts + 1);
+  route_scatter<<<static_cast<int>(blocks), kRouteThreads, scatter_smem, s>>>(expert_ids, assignments, experts,
+                                                                              counts, perm, expert_ids_g, inverse);
+  return launch_status();
+}
