@@ -33,9 +33,10 @@ CONFIGS = {
     "half": dict(tokens=8192, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
 }
 METRIC = "MoE-LoRA layer fwd+bwd tokens/s"
-# DRAM bytes (read + write) of one launch of the grouped product, from the ncu capture summarised in
-# profiles/grouped_gemm_qwen3_30b.md, scaled to the full workload there; None until captured.
-GEMM_TRAFFIC_BYTES_PER_STEP = None
+# DRAM bytes (read + write) per grouped-product launch at config 2, averaged over the step's four launches: from the
+# ncu capture summarised in profiles/grouped_gemm_half_qwen3_30b.md (half the tokens), weight bytes kept and
+# activation bytes doubled to the full workload.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 1.67e9
 
 
 def flop_per_token(c):
@@ -52,7 +53,8 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """nvidia-smi sampled every 100 ms from before the warm-up; the summary keeps the samples that arrived while
+    the timed region ran (between mark_start and mark_stop)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -61,31 +63,48 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+
+        def read():
+            for ln in self.proc.stdout:
+                self.lines.append((time.monotonic(), ln.strip()))
+
+        self.reader = threading.Thread(target=read, daemon=True)
+        self.reader.start()
         return self
 
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_stop(self):
+        self.t1 = time.monotonic()
+
     def __exit__(self, *a):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for t, ln in list(self.lines):
+            if self.t0 is not None and (t < self.t0 or (self.t1 is not None and t > self.t1 + 0.1)):
+                continue
             f = [x.strip() for x in ln.split(",")]
             try:
                 sm.append(float(f[1]))
@@ -210,6 +229,7 @@ def run_meep2b(a):
             dist.barrier()
             torch.cuda.synchronize(device)
 
+    clocks = ClockSampler(local).__enter__()
     for _ in range(a.warmup):
         step(hidden_leaf, idx, w, grad)
     sync()
@@ -219,46 +239,79 @@ def run_meep2b(a):
     timer.active = True
     stream = torch.cuda.current_stream(device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        sync()
-        start.record(stream)
-        for _ in range(a.steps):
-            step(hidden_leaf, idx, w, grad)
-        stop.record(stream)
-        sync()
+    sync()
+    clocks.mark_start()
+    start.record(stream)
+    for _ in range(a.steps):
+        step(hidden_leaf, idx, w, grad)
+    stop.record(stream)
+    sync()
+    clocks.mark_stop()
+    clocks.__exit__()
     timer.active = False
     _grouped.set_launch_observer(None)
     ms = start.elapsed_time(stop)
     gemm_ms, gemm_flops, gemm_launches = timer.totals()
 
-    # end to end through the public API with host buffers: pinned host inputs copied in, results read back
+    # End to end through the public API with host buffers: every step copies its inputs in from pinned host memory
+    # and reads its results back (layer output, input gradient, LoRA gradients). As a training loop with a
+    # prefetching data loader does, the copies run on a second stream: step i+1's inputs go in and step i's results
+    # come out while step i+1 computes. The timed region covers every step's copies in both directions.
     h_host = hidden.cpu().pin_memory()
     i_host = idx.cpu().pin_memory()
     w_host = w.cpu().pin_memory()
     g_host = grad.cpu().pin_memory()
-    out_host = torch.empty(hidden.shape, dtype=torch.bfloat16).pin_memory()
-    gh_host = torch.empty(hidden.shape, dtype=torch.bfloat16).pin_memory()
-    lg_host = torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory()
+    out_host = [torch.empty(hidden.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    gh_host = [torch.empty(hidden.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    lg_host = [torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory() for _ in range(2)]
+    d_in = [(torch.empty_like(hidden), torch.empty_like(idx), torch.empty_like(w), torch.empty_like(grad))
+            for _ in range(2)]
+    lg_stage = [torch.empty_like(bucket.flat) for _ in range(2)]
+    copy = torch.cuda.Stream(device)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]  # step on this slot finished with its inputs and outputs
 
-    def e2e_step():
-        h = h_host.to(device, non_blocking=True).requires_grad_()
-        ids = i_host.to(device, non_blocking=True)
-        wts = w_host.to(device, non_blocking=True)
-        g = g_host.to(device, non_blocking=True)
-        out = step(h, ids, wts, g)
-        out_host.copy_(out.detach(), non_blocking=True)
-        gh_host.copy_(h.grad, non_blocking=True)
-        lg_host.copy_(bucket.flat, non_blocking=True)
+    def h2d(slot):
+        copy.wait_event(used[slot])
+        with torch.cuda.stream(copy):
+            for dst, src in zip(d_in[slot], (h_host, i_host, w_host, g_host)):
+                dst.copy_(src, non_blocking=True)
+            in_ready[slot].record(copy)
 
-    for _ in range(max(2, a.warmup // 2)):
-        e2e_step()
+    def e2e_run(n):
+        for slot in range(2):
+            used[slot].record(stream)
+        h2d(0)
+        for i in range(n):
+            cur = i % 2
+            stream.wait_event(in_ready[cur])
+            if i + 1 < n:
+                h2d(1 - cur)
+            hd, ids, wts, g = d_in[cur]
+            h = hd.detach().requires_grad_()
+            out = step(h, ids, wts, g)
+            lg_stage[cur].copy_(bucket.flat)
+            done = torch.cuda.Event()
+            done.record(stream)
+            copy.wait_event(done)
+            with torch.cuda.stream(copy):
+                out_host[cur].copy_(out.detach(), non_blocking=True)
+                gh_host[cur].copy_(h.grad, non_blocking=True)
+                lg_host[cur].copy_(lg_stage[cur], non_blocking=True)
+            out.record_stream(copy)
+            h.grad.record_stream(copy)
+            fin = torch.cuda.Event()
+            fin.record(copy)
+            used[cur] = fin
+        stream.wait_stream(copy)
+
+    e2e_run(max(2, a.warmup))
     sync()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_steps = max(3, a.steps // 2)
     sync()
     e_start.record(stream)
-    for _ in range(e_steps):
-        e2e_step()
+    e2e_run(e_steps)
     e_stop.record(stream)
     sync()
     e_ms = e_start.elapsed_time(e_stop)
@@ -289,7 +342,8 @@ def run_meep2b(a):
                      "unit": "TFLOP/s", "frac": round(achieved / sustained, 4) if achieved else None,
                      "peak_kind": f"bf16 sustained, {peak_kind}",
                      "launches_timed": gemm_launches, "gemm_ms_per_step": round(gemm_ms / a.steps, 4),
-                     "traffic": GEMM_TRAFFIC_BYTES_PER_STEP},
+                     "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH if a.config == "qwen3_30b" else None,
+                     "traffic_unit": "DRAM bytes per launch (ncu, profiles/grouped_gemm_half_qwen3_30b.md)"},
         "e2e": {"value": round(e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": launches_per_step * a.steps,
@@ -364,7 +418,7 @@ def run_reference(a):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="meep2b", choices=["meep2b", "reference"])
     ap.add_argument("--config", default="qwen3_30b", choices=sorted(CONFIGS))

@@ -1,0 +1,106 @@
+"""Data-parallel host logic on CPU ranks (gloo, world size 2), the way the reference tests DDP
+(tests/test_ddp.py there: gloo CPU processes): the flat LoRA-gradient bucket averages across ranks, autograd
+accumulates into it in place, and a rank that fails before the exchange makes the other rank's collective end with
+an error within the process group's timeout instead of hanging."""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from meepsquared_b200.ddp import LoraGradBucket
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s=30):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _average_worker(rank, world, port, queue):
+    _init(rank, world, port)
+    torch.manual_seed(0)
+    params = [torch.nn.Parameter(torch.zeros(3, 4, 2)), torch.nn.Parameter(torch.zeros(3, 2, 5))]
+    bucket = LoraGradBucket(params)
+    for step in range(2):
+        bucket.zero()
+        # each rank's loss differs; autograd accumulates into the bucket's views in place
+        loss = (params[0] * (rank + 1)).sum() + (params[1] * (step + 1) * (rank + 2)).sum()
+        loss.backward()
+        bucket.reduce()
+        queue.put((rank, step, params[0].grad.tolist(), params[1].grad.tolist(),
+                   bucket.flat.data_ptr() == params[0].grad.data_ptr()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _failing_worker(rank, world, port, queue):
+    _init(rank, world, port, timeout_s=5)
+    params = [torch.nn.Parameter(torch.zeros(8))]
+    bucket = LoraGradBucket(params)
+    if rank == 1:
+        queue.put((rank, "left"))
+        queue.close()
+        queue.join_thread()  # the message is out before the process goes
+        os._exit(3)  # leaves between steps, before the exchange: no collective of its own in flight
+    params[0].sum().backward()
+    try:
+        bucket.reduce()
+        queue.put((rank, "returned"))
+    except Exception as exc:  # the collective ends with an error (timeout or closed connection)
+        queue.put((rank, f"error: {type(exc).__name__}"))
+    queue.close()
+    queue.join_thread()
+    os._exit(0)
+
+
+def _run(fn, world=2):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    items = []
+    expected = {"_average_worker": 2 * world, "_failing_worker": world}[fn.__name__]
+    import queue as _queue
+    try:
+        while len(items) < expected:
+            items.append(queue.get(timeout=120))
+    except _queue.Empty:
+        pass
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank did not finish")
+    return procs, items
+
+
+def test_the_bucket_averages_lora_gradients_across_ranks():
+    procs, items = _run(_average_worker)
+    assert all(p.exitcode == 0 for p in procs)
+    assert len(items) == 4
+    for rank, step, g0, g1, shares_storage in items:
+        assert shares_storage
+        g0, g1 = torch.tensor(g0), torch.tensor(g1)
+        torch.testing.assert_close(g0, torch.full_like(g0, (1 + 2) / 2))
+        torch.testing.assert_close(g1, torch.full_like(g1, (step + 1) * (2 + 3) / 2))
+
+
+def test_a_rank_that_leaves_before_the_exchange_ends_the_other_ranks_collective_with_an_error():
+    procs, items = _run(_failing_worker)
+    outcome = dict(items)
+    assert outcome[1] == "left"
+    assert outcome[0].startswith("error"), outcome[0]
+    assert procs[0].exitcode == 0
