@@ -100,15 +100,17 @@ class TileMaps:
         return self._maps[block_m]
 
 
-def _pair_tiles(b_mn: int, rows: int, experts: int, k: int) -> bool:
-    """Whether a product runs on CTA pairs (tiles of 256 rows): stacks read K-major, enough rows per expert on
-    average that the wider tiles waste little, and a long enough contraction (k >= 1024) that the pair's
-    cross-CTA hand-offs at the end of each tile stay hidden; MEEP2B_PAIR=0 or 1 overrides."""
-    if b_mn != 0:
-        return False
+def _pair_tiles(b_mn: int, rows: int, experts: int, k: int, adapters: bool) -> bool:
+    """Whether a product runs on CTA pairs (tiles of 256 rows): enough rows per expert on average that the wider
+    tiles waste little, and a long enough contraction (k >= 1024) that the pair's cross-CTA hand-offs at the end
+    of each tile stay hidden. A stack read MN-major (the input gradient) goes to pairs only without adapters: its
+    rank panel arrives as a separate 32-column atom of which the MMA uses 8, and on B200 the one-CTA kernel is
+    measured faster for it. MEEP2B_PAIR=0 or 1 overrides."""
     forced = os.environ.get("MEEP2B_PAIR")
     if forced in ("0", "1"):
         return forced == "1"
+    if b_mn != 0 and adapters:
+        return False
     return rows >= 384 * experts and k >= 1024
 
 
@@ -233,7 +235,7 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
         return out, low
     if tiles is None:
         tiles = TileMaps(offsets, rows)
-    block_m = 256 if _pair_tiles(b_mn, rows, stack.shape[0], K) else 128
+    block_m = 256 if _pair_tiles(b_mn, rows, stack.shape[0], K, adapters is not None) else 128
     tmap = tiles.get(block_m)
     panel = up = None
     if adapters is not None:

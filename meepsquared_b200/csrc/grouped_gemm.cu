@@ -184,7 +184,9 @@ __device__ __forceinline__ void tmem_wait_regs16(uint32_t* r) {
 // `half`). row_shift: the offset of this CTA's rows within the tile (128 for the second CTA of a pair). All of a
 // thread's accumulator loads for the unit are issued before one wait (the dSwiGLU epilogue, which also reads the
 // pre-activations, pipelines them by two). Returns false when a bounded wait ran out.
-template <int EPI, bool LORA, bool PAIR>
+// SPLIT: the accumulator of an MN-major CTA pair, whose columns are [stack 0..95 | panel 0..7 | stack 96..191 |
+// panel 8..15] (each CTA's half of B is 96 stack columns then 8 panel columns); otherwise [stack 0..191 | panel].
+template <int EPI, bool LORA, bool PAIR, bool SPLIT = false>
 __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, int row_shift, uint8_t* smem_low,
                                               uint32_t tmem_base, int q, int half, int lane,
                                               uint32_t bar_lowfull_ab, uint32_t bar_lowready,
@@ -205,7 +207,15 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
     if (!mbar_wait(bar_lowfull_ab, aph)) return false;
     tc_fence_after();
     float lv[16];
-    tmem_ld16(d + BN, lv);
+    if (SPLIT) {
+      float l0[16], l1[16];
+      tmem_ld16(d + 96, l0);    // panel columns 0..7 then stack columns 96..103 of the second half
+      tmem_ld16(d + 200, l1);   // panel columns 8..15 then 8 columns past the tile
+#pragma unroll
+      for (int i = 0; i < 8; ++i) lv[i] = l0[i], lv[8 + i] = l1[i];
+    } else {
+      tmem_ld16(d + BN, lv);
+    }
     if (p.low != nullptr && nb == 0 && valid) {
       uint32_t lw[8];
 #pragma unroll
@@ -282,15 +292,16 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
       }
     }
   } else if (EPI == MEEP2B_EPI_PLAIN) {
+    constexpr int HS = SPLIT ? 104 : 96;  // accumulator column of the second half
     const int n0 = nb * BN + half * 96;
     const int cols = min(96, p.N - n0);
     uint32_t v[96];
     if (!mbar_wait(bar_tfull_ab, aph)) return false;
     tc_fence_after();
     if (cols > 0) {
-      tmem_ld32_async(d + half * 96, *reinterpret_cast<uint32_t(*)[32]>(v));
-      tmem_ld32_async(d + half * 96 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-      tmem_ld32_async(d + half * 96 + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
+      tmem_ld32_async(d + half * HS, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld32_async(d + half * HS + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_ld32_async(d + half * HS + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
 #pragma unroll
       for (int c = 0; c < 6; ++c) tmem_wait_regs16(v + 16 * c);
     }
@@ -318,6 +329,7 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
   } else {  // MEEP2B_EPI_DSWIGLU: the product is dh; aux holds (gate, up); out receives (dgate, dup)
     // 16 columns per step, two steps in flight: the next step's accumulator words and pre-activations are
     // requested before this step is computed
+    constexpr int HS = SPLIT ? 104 : 96;
     const int n0 = nb * BN + half * 96;
     const int cols = min(96, p.N - n0);
     const __nv_bfloat16* gp = p.aux + orow * p.ld_aux + n0;
@@ -350,7 +362,7 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
     if (!mbar_wait(bar_tfull_ab, aph)) return false;
     tc_fence_after();
     if (cols > 0) {
-      tmem_ld16_async(d + half * 96, acc[0]);
+      tmem_ld16_async(d + half * HS, acc[0]);
       tmem_wait_regs16(acc[0]);
     }
 #pragma unroll
@@ -360,7 +372,7 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
       const int b = c & 1;
       const bool more = c < 5 && cols - 16 * (c + 1) > 0;
       if (more) {
-        tmem_ld16_async(d + half * 96 + 16 * (c + 1), acc[b ^ 1]);
+        tmem_ld16_async(d + half * HS + 16 * (c + 1), acc[b ^ 1]);
         if (valid) load_pre(c + 1, b ^ 1);
       }
       if (valid) {
@@ -462,6 +474,27 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int s = 0; s < STAGES; ++s) issued[s] = false, last_parity[s] = 0;
       bool ok = true;
       int it = 0;
+      // The up factor of a unit (single buffer) is loaded one k-step into the next unit, so that the producer never
+      // waits for the previous unit's adapter MMAs while the ring could be refilled.
+      int pu = -1, pu_nb = 0, pu_e = 0;
+      auto load_u = [&]() -> bool {
+        if (!mbar_wait(bar_uempty, (pu & 1) ^ 1)) return false;
+        const uint32_t dst = sbase + P::OFF_U;
+        mbar_arrive_expect_tx(bar_ufull, U_BYTES);
+        if (!B_MN) {
+          if (EPI == MEEP2B_EPI_SWIGLU) {
+            tma_load_3d(dst, &tm_u, bar_ufull, 0, pu_nb * 96, pu_e);
+            tma_load_3d(dst + 96 * RP * 2, &tm_u, bar_ufull, 0, p.inter + pu_nb * 96, pu_e);
+          } else {
+            tma_load_3d(dst, &tm_u, bar_ufull, 0, pu_nb * BN, pu_e);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 3; ++j) tma_load_3d(dst + j * 2048, &tm_u, bar_ufull, pu_nb * BN + 64 * j, 0, pu_e);
+        }
+        pu = -1;
+        return true;
+      };
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++it) {
         const int t = u / p.nblocks, nb = u - t * p.nblocks;
         const int e = p.tile_expert[t], row0 = p.tile_row[t];
@@ -491,27 +524,15 @@ __global__ void __launch_bounds__(THREADS, 1)
             stage = 0;
             phase ^= 1;
           }
+          if (LORA && kb == 0 && pu >= 0 && !load_u()) { ok = false; break; }
         }
         if (!ok) break;
         if (LORA) {
-          // the up factor for this unit's columns, after its k-steps: the previous unit's last MMAs are done with
-          // the single U buffer well before the producer, a ring ahead of the MMAs, gets here
-          if (!mbar_wait(bar_uempty, (it & 1) ^ 1)) { ok = false; break; }
-          const uint32_t dst = sbase + P::OFF_U;
-          mbar_arrive_expect_tx(bar_ufull, U_BYTES);
-          if (!B_MN) {
-            if (EPI == MEEP2B_EPI_SWIGLU) {
-              tma_load_3d(dst, &tm_u, bar_ufull, 0, nb * 96, e);
-              tma_load_3d(dst + 96 * RP * 2, &tm_u, bar_ufull, 0, p.inter + nb * 96, e);
-            } else {
-              tma_load_3d(dst, &tm_u, bar_ufull, 0, nb * BN, e);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 3; ++j) tma_load_3d(dst + j * 2048, &tm_u, bar_ufull, nb * BN + 64 * j, 0, e);
-          }
+          if (pu >= 0 && !load_u()) { ok = false; break; }
+          pu = it, pu_nb = nb, pu_e = e;
         }
       }
+      if (ok && LORA && pu >= 0) ok = load_u();
       if (!ok) {
         // a partner is gone: let this thread's copies in flight land before the CTA's shared memory goes away
         for (int s = 0; s < STAGES; ++s)
@@ -623,18 +644,29 @@ __global__ void __launch_bounds__(THREADS, 1)
 #define MEEP2B_PAIR_STAGES 7
 #endif
 constexpr int PAIR_STAGES = MEEP2B_PAIR_STAGES;
-constexpr int PAIR_B_ROWS = (BN + RP) / 2;            // 104
-constexpr int PAIR_B_BYTES = PAIR_B_ROWS * BK * 2;    // 13 KB
-constexpr int PAIR_U_BYTES = (BN / 2) * RP * 2;       // 3 KB
-constexpr int PAIR_OFF_B = PAIR_STAGES * A_BYTES;
-constexpr int PAIR_OFF_U = PAIR_OFF_B + PAIR_STAGES * PAIR_B_BYTES;
-constexpr int PAIR_OFF_LOW = PAIR_OFF_U + PAIR_U_BYTES;
-constexpr int PAIR_OFF_BAR = PAIR_OFF_LOW + LOW_BYTES;
-constexpr int PAIR_NUM_BARS = 2 * PAIR_STAGES + 10;
-constexpr int PAIR_OFF_TMEM = PAIR_OFF_BAR + PAIR_NUM_BARS * 8;
-constexpr int PAIR_SMEM_BYTES = PAIR_OFF_TMEM + 16 + 1024;
-static_assert(PAIR_SMEM_BYTES <= 232448, "pair shared memory plan exceeds 227 KB");
-static_assert(PAIR_B_BYTES % 1024 == 0 && PAIR_OFF_U % 1024 == 0 && PAIR_OFF_LOW % 1024 == 0, "1 KB alignment");
+constexpr int PAIR_B_ROWS = (BN + RP) / 2;  // 104: each CTA's share of the 208 K-major B rows
+
+// Shared memory of a CTA of a pair. K-major: per stage the x tile and 104 B rows (7 stages). MN-major: the x tile,
+// then this CTA's 96 stack columns as three 32-column atoms with the 64-byte swizzle (64 rows x 64 B each) and,
+// right after them, a fourth atom whose first 8 columns are its 8 panel columns: the 104 columns the pair's N = 208
+// MMA reads from it (6 stages).
+template <bool B_MN>
+struct PairPlan {
+  static constexpr int STAGES = B_MN ? 6 : PAIR_STAGES;
+  static constexpr int B_BYTES = B_MN ? 4 * 64 * 64 : PAIR_B_ROWS * BK * 2;  // 16 KB : 13 KB
+  static constexpr int PANEL_OFF = 3 * 64 * 64;                            // MN-major panel atom
+  static constexpr int U_TX = B_MN ? 4 * RP * 64 : (BN / 2) * RP * 2;      // bytes of U each CTA loads
+  static constexpr int U_BYTES = 4096;
+  static constexpr int OFF_B = STAGES * A_BYTES;
+  static constexpr int OFF_U = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_LOW = OFF_U + U_BYTES;
+  static constexpr int OFF_BAR = OFF_LOW + LOW_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 10;
+  static constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "pair shared memory plan exceeds 227 KB");
+  static_assert(B_BYTES % 1024 == 0 && OFF_U % 1024 == 0 && OFF_LOW % 1024 == 0, "1 KB alignment");
+};
 
 struct PairMaps {
   CUtensorMap x;     // (k, rows) box 64 x 128
@@ -644,11 +676,15 @@ struct PairMaps {
   CUtensorMap w8;    // box 64 x 8
   CUtensorMap p16;   // panel (k, 16, E) box 64 x 16
   CUtensorMap u96;   // up (16, n, E) box 16 x 96, 32-byte swizzle
+  CUtensorMap w_mn;  // MN-major stack (n, k, E) box 32 x 64, 64-byte swizzle
+  CUtensorMap p_mn;  // MN-major panel (E, k, 64) box 32 x 64 from column 8 * rank, 64-byte swizzle
+  CUtensorMap u_mn;  // MN-major up factor (n, 16, E) box 32 x 16, 64-byte swizzle
 };
 
-template <bool LORA, int EPI>
+template <bool B_MN, bool LORA, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ PairMaps m, const Params p) {
+  using PP = PairPlan<B_MN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -656,20 +692,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_rank();
   const int pair_id = static_cast<int>(cluster_id_x()), pairs = static_cast<int>(num_clusters_x());
 
-  const uint32_t bar0 = sbase + PAIR_OFF_BAR;
+  const uint32_t bar0 = sbase + PP::OFF_BAR;
   auto bar_full = [&](int s) { return bar0 + 8u * s; };
-  auto bar_empty = [&](int s) { return bar0 + 8u * (PAIR_STAGES + s); };
-  auto bar_tfull = [&](int b) { return bar0 + 8u * (2 * PAIR_STAGES + b); };
-  auto bar_tempty = [&](int b) { return bar0 + 8u * (2 * PAIR_STAGES + 2 + b); };
-  auto bar_lowfull = [&](int b) { return bar0 + 8u * (2 * PAIR_STAGES + 4 + b); };
-  const uint32_t bar_lowready = bar0 + 8u * (2 * PAIR_STAGES + 6);
-  const uint32_t bar_ufull = bar0 + 8u * (2 * PAIR_STAGES + 7);
-  const uint32_t bar_uempty = bar0 + 8u * (2 * PAIR_STAGES + 8);
-  const uint32_t bar_drain = bar0 + 8u * (2 * PAIR_STAGES + 9);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PAIR_OFF_TMEM);
+  auto bar_empty = [&](int s) { return bar0 + 8u * (PP::STAGES + s); };
+  auto bar_tfull = [&](int b) { return bar0 + 8u * (2 * PP::STAGES + b); };
+  auto bar_tempty = [&](int b) { return bar0 + 8u * (2 * PP::STAGES + 2 + b); };
+  auto bar_lowfull = [&](int b) { return bar0 + 8u * (2 * PP::STAGES + 4 + b); };
+  const uint32_t bar_lowready = bar0 + 8u * (2 * PP::STAGES + 6);
+  const uint32_t bar_ufull = bar0 + 8u * (2 * PP::STAGES + 7);
+  const uint32_t bar_uempty = bar0 + 8u * (2 * PP::STAGES + 8);
+  const uint32_t bar_drain = bar0 + 8u * (2 * PP::STAGES + 9);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PP::OFF_TMEM);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < PAIR_STAGES; ++s) {
+    for (int s = 0; s < PP::STAGES; ++s) {
       mbar_init(bar_full(s), 1);
       mbar_init(bar_empty(s), 1);
     }
@@ -698,16 +734,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&m.x);
-      tma_prefetch_desc(EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? &m.w96 : &m.w88) : (rank == 0 ? &m.w104 : &m.w88));
-      // with the panel the 208 B rows split 104 / 104 (the second CTA's last 16 are the panel); without it 96 / 96
-      constexpr uint32_t CTA_TX = A_BYTES + (LORA ? PAIR_B_ROWS : BN / 2) * 128;
+      // K-major: with the panel the 208 B rows split 104 / 104 (the second CTA's last 16 are the panel), without it
+      // 96 / 96. MN-major: 96 stack columns per CTA, plus 8 panel columns (one 16-column atom) with the adapters.
+      constexpr uint32_t CTA_TX =
+          B_MN ? A_BYTES + 3 * 64 * 64 + (LORA ? 64 * 64 : 0) : A_BYTES + (LORA ? PAIR_B_ROWS : BN / 2) * 128;
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t last_parity[PAIR_STAGES];
-      bool issued[PAIR_STAGES];
-      for (int s = 0; s < PAIR_STAGES; ++s) issued[s] = false, last_parity[s] = 0;
+      uint32_t last_parity[PP::STAGES];
+      bool issued[PP::STAGES];
+      for (int s = 0; s < PP::STAGES; ++s) issued[s] = false, last_parity[s] = 0;
       bool ok = true;
       int it = 0;
+      int pu = -1, pu_nb = 0, pu_e = 0;  // as in the one-CTA kernel: a unit's up factor goes out one k-step later
+      auto load_u = [&]() -> bool {
+        if (!mbar_wait(bar_uempty, (pu & 1) ^ 1)) return false;
+        if (rank == 0) mbar_arrive_expect_tx(bar_ufull, 2 * PP::U_TX);
+        const int urow = EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? pu_nb * 96 : p.inter + pu_nb * 96)
+                                                  : pu_nb * BN + 96 * static_cast<int>(rank);
+        if (B_MN) {  // 96 columns and 8 more: the fourth atom lands on panel columns of the accumulator, read already
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_3d_pair(sbase + PP::OFF_U + j * 1024, &m.u_mn, map_to_rank(bar_ufull, 0), urow + 32 * j, 0, pu_e);
+        } else {
+          tma_load_3d_pair(sbase + PP::OFF_U, &m.u96, map_to_rank(bar_ufull, 0), 0, urow, pu_e);
+        }
+        pu = -1;
+        return true;
+      };
       for (int u = pair_id; u < total && ok; u += pairs, ++it) {
         const int t = u / p.nblocks, nb = u - t * p.nblocks;
         const int e = p.tile_expert[t], row0 = p.tile_row[t] + 128 * static_cast<int>(rank);
@@ -716,11 +769,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const uint32_t fb = bar_full(stage);
           const uint32_t fb_lead = map_to_rank(fb, 0);
           const uint32_t a_dst = sbase + stage * A_BYTES;
-          const uint32_t b_dst = sbase + PAIR_OFF_B + stage * PAIR_B_BYTES;
+          const uint32_t b_dst = sbase + PP::OFF_B + stage * PP::B_BYTES;
           if (rank == 0) mbar_arrive_expect_tx(fb, 2 * CTA_TX);
           tma_load_2d_pair(a_dst, &m.x, fb_lead, kb * BK, row0);
           const int k0 = kb * BK;
-          if (EPI == MEEP2B_EPI_SWIGLU) {
+          if (B_MN) {
+            const int c0 = nb * BN + 96 * static_cast<int>(rank);
+#pragma unroll
+            for (int j = 0; j < 3; ++j) tma_load_3d_pair(b_dst + j * 4096, &m.w_mn, fb_lead, c0 + 32 * j, k0, e);
+            if (LORA) tma_load_3d_pair(b_dst + PP::PANEL_OFF, &m.p_mn, fb_lead, 8 * static_cast<int>(rank), k0, e);
+          } else if (EPI == MEEP2B_EPI_SWIGLU) {
             const int g0 = nb * 96;
             if (!LORA) {  // gate rows in the first CTA, up rows in the second
               tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, rank == 0 ? g0 : p.inter + g0, e);
@@ -744,30 +802,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
           issued[stage] = true;
           last_parity[stage] = phase;
-          if (++stage == PAIR_STAGES) {
+          if (++stage == PP::STAGES) {
             stage = 0;
             phase ^= 1;
           }
+          if (LORA && kb == 0 && pu >= 0 && !load_u()) { ok = false; break; }
         }
         if (!ok) break;
         if (LORA) {
-          if (!mbar_wait(bar_uempty, (it & 1) ^ 1)) { ok = false; break; }
-          if (rank == 0) mbar_arrive_expect_tx(bar_ufull, 2 * PAIR_U_BYTES);
-          const int urow = EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? nb * 96 : p.inter + nb * 96)
-                                                    : nb * BN + 96 * static_cast<int>(rank);
-          tma_load_3d_pair(sbase + PAIR_OFF_U, &m.u96, map_to_rank(bar_ufull, 0), 0, urow, e);
+          if (pu >= 0 && !load_u()) { ok = false; break; }
+          pu = it, pu_nb = nb, pu_e = e;
         }
       }
+      if (ok && LORA && pu >= 0) ok = load_u();
       if (!ok) {
-        for (int s = 0; s < PAIR_STAGES; ++s)
+        for (int s = 0; s < PP::STAGES; ++s)
           if (issued[s] && rank == 0) mbar_wait_drain(bar_full(s), last_parity[s]);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t IDESC_MAIN = idesc_bf16(256, LORA ? BN + RP : BN, false, false);
-      constexpr uint32_t IDESC_UP = idesc_bf16(256, BN, false, false);
+      // one MMA of N = 208 with the adapters (the panel rides along in the B tile), 192 without; the MN-major
+      // adapter MMA also spans 208 columns so that its two halves land on the split accumulator's stack columns
+      constexpr uint32_t IDESC_MAIN = idesc_bf16(256, LORA ? BN + RP : BN, false, B_MN);
+      constexpr uint32_t IDESC_UP = idesc_bf16(256, B_MN ? BN + RP : BN, false, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -782,8 +841,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t dp = tmem_base + (pend & 1) * ACC_STRIDE;
-        const uint32_t low_addr = sbase + PAIR_OFF_LOW;
-        const uint64_t bdesc = smem_desc(sbase + PAIR_OFF_U, 16, 256, 6);
+        const uint32_t low_addr = sbase + PP::OFF_LOW;
+        const uint64_t bdesc =
+            B_MN ? smem_desc(sbase + PP::OFF_U, 1024, 512, 4) : smem_desc(sbase + PP::OFF_U, 16, 256, 6);
         mma_bf16_pair(dp, smem_desc(low_addr, 16, 256, 6), bdesc, IDESC_UP, 1);             // hi plane
         mma_bf16_pair(dp, smem_desc(low_addr + BM * RP * 2, 16, 256, 6), bdesc, IDESC_UP, 1);  // lo plane
         mma_commit_pair(bar_uempty);
@@ -801,13 +861,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (!mbar_wait(bar_full(stage), phase)) { ok = false; break; }
           if (MEEP2B_KSTEP_FENCE) tc_fence_after();
           const uint32_t a_addr = sbase + stage * A_BYTES;
-          const uint32_t b_addr = sbase + PAIR_OFF_B + stage * PAIR_B_BYTES;
+          const uint32_t b_addr = sbase + PP::OFF_B + stage * PP::B_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            mma_bf16_pair(d, smem_desc(a_addr + kk * 32, 16, 1024, 2), smem_desc(b_addr + kk * 32, 16, 1024, 2),
-                          IDESC_MAIN, (kb | kk) != 0);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024, 2);
+            if (B_MN) {
+              mma_bf16_pair(d, adesc, smem_desc(b_addr + kk * 1024, 4096, 512, 4), IDESC_MAIN, (kb | kk) != 0);
+            } else {
+              mma_bf16_pair(d, adesc, smem_desc(b_addr + kk * 32, 16, 1024, 2), IDESC_MAIN, (kb | kk) != 0);
+            }
+          }
           mma_commit_pair(bar_empty(stage));
-          if (++stage == PAIR_STAGES) {
+          if (++stage == PP::STAGES) {
             stage = 0;
             phase ^= 1;
           }
@@ -835,7 +900,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int it = 0;
     for (int u = pair_id; u < total; u += pairs, ++it) {
       const int ab = it & 1;
-      if (!epilogue_unit<EPI, LORA, true>(p, u, it, 128 * static_cast<int>(rank), smem + PAIR_OFF_LOW, tmem_base, q,
+      if (!epilogue_unit<EPI, LORA, true, B_MN && LORA>(p, u, it, 128 * static_cast<int>(rank), smem + PP::OFF_LOW, tmem_base, q,
                                           half, lane, bar_lowfull(ab), bar_lowready, bar_tfull(ab), bar_tempty(ab)))
         break;
     }
@@ -849,18 +914,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   }
 }
 
-template <bool LORA, int EPI>
+template <bool B_MN, bool LORA, int EPI>
 static int launch_pair(const PairMaps& maps, const Params& prm, int grid, cudaStream_t s) {
-  auto kern = grouped_gemm_pair_kernel<LORA, EPI>;
+  auto kern = grouped_gemm_pair_kernel<B_MN, LORA, EPI>;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES) != cudaSuccess) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairPlan<B_MN>::SMEM_BYTES) != cudaSuccess) {
       cudaGetLastError();
       return MEEP2B_ERR_LAUNCH;
     }
     configured = true;
   }
-  kern<<<grid, THREADS, PAIR_SMEM_BYTES, s>>>(maps, prm);
+  kern<<<grid, THREADS, PairPlan<B_MN>::SMEM_BYTES, s>>>(maps, prm);
   return launch_status();
 }
 
@@ -989,39 +1054,62 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   const int block_m = a->block_m == 0 ? 128 : a->block_m;
   if (block_m != 128 && block_m != 256) return MEEP2B_ERR_UNSUPPORTED;
   if (block_m == 256) {
-    if (a->b_mn) return MEEP2B_ERR_UNSUPPORTED;
     PairMaps maps;
     maps.x = tx;
-    const uint32_t heights[4] = {104, 96, 88, 8};
-    CUtensorMap* targets[4] = {&maps.w104, &maps.w96, &maps.w88, &maps.w8};
-    for (int i = 0; i < 4; ++i) {
-      const uint64_t dims[3] = {K, N, E};
-      const uint64_t strides[2] = {K * 2, N * K * 2};
-      const uint32_t box[3] = {64, heights[i], 1};
-      MEEP2B_TRY(encode_tiled(targets[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->weight, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_128B));
-    }
-    if (lora) {
-      maps.p16 = tp;
-      const uint64_t ud[3] = {RP, N, E};
-      const uint64_t us[2] = {RP * 2, N * RP * 2};
-      const uint32_t ubx[3] = {RP, 96, 1};
-      MEEP2B_TRY(encode_tiled(&maps.u96, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->up, ud, us, ubx,
-                              CU_TENSOR_MAP_SWIZZLE_32B));
+    maps.w104 = maps.w96 = maps.w88 = maps.w8 = maps.p16 = maps.u96 = maps.w_mn = maps.p_mn = maps.u_mn = tx;
+    if (!a->b_mn) {
+      const uint32_t heights[4] = {104, 96, 88, 8};
+      CUtensorMap* targets[4] = {&maps.w104, &maps.w96, &maps.w88, &maps.w8};
+      for (int i = 0; i < 4; ++i) {
+        const uint64_t dims[3] = {K, N, E};
+        const uint64_t strides[2] = {K * 2, N * K * 2};
+        const uint32_t box[3] = {64, heights[i], 1};
+        MEEP2B_TRY(encode_tiled(targets[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->weight, dims, strides, box,
+                                CU_TENSOR_MAP_SWIZZLE_128B));
+      }
+      if (lora) {
+        maps.p16 = tp;
+        const uint64_t ud[3] = {RP, N, E};
+        const uint64_t us[2] = {RP * 2, N * RP * 2};
+        const uint32_t ubx[3] = {RP, 96, 1};
+        MEEP2B_TRY(encode_tiled(&maps.u96, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->up, ud, us, ubx,
+                                CU_TENSOR_MAP_SWIZZLE_32B));
+      }
     } else {
-      maps.p16 = tx;
-      maps.u96 = tx;
+      if (epi == MEEP2B_EPI_SWIGLU) return MEEP2B_ERR_UNSUPPORTED;
+      const uint64_t wd[3] = {N, K, E};
+      const uint64_t ws[2] = {N * 2, K * N * 2};
+      const uint32_t wb[3] = {32, 64, 1};
+      MEEP2B_TRY(encode_tiled(&maps.w_mn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->weight, wd, ws, wb,
+                              CU_TENSOR_MAP_SWIZZLE_64B));
+      if (lora) {
+        const uint64_t pd[3] = {64, K, E};  // the (E, k, 64) panel, 32 columns from column 8 * rank
+        const uint64_t ps[2] = {128, K * 128};
+        const uint32_t pb[3] = {32, 64, 1};
+        MEEP2B_TRY(encode_tiled(&maps.p_mn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->panel, pd, ps, pb,
+                                CU_TENSOR_MAP_SWIZZLE_64B));
+        const uint64_t ud[3] = {N, RP, E};
+        const uint64_t us[2] = {N * 2, RP * N * 2};
+        const uint32_t ub[3] = {32, RP, 1};
+        MEEP2B_TRY(encode_tiled(&maps.u_mn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->up, ud, us, ub,
+                                CU_TENSOR_MAP_SWIZZLE_64B));
+      }
     }
     const int pairs_max = sms / 2;
     const int64_t pairs = units < pairs_max ? (units > 0 ? units : 1) : pairs_max;
     const int grid = static_cast<int>(2 * pairs);
+    if (a->b_mn) {
+      if (epi == MEEP2B_EPI_PLAIN)
+        return lora ? launch_pair<true, true, 0>(maps, prm, grid, s) : launch_pair<true, false, 0>(maps, prm, grid, s);
+      return lora ? launch_pair<true, true, 2>(maps, prm, grid, s) : launch_pair<true, false, 2>(maps, prm, grid, s);
+    }
     switch (epi) {
       case MEEP2B_EPI_PLAIN:
-        return lora ? launch_pair<true, 0>(maps, prm, grid, s) : launch_pair<false, 0>(maps, prm, grid, s);
+        return lora ? launch_pair<false, true, 0>(maps, prm, grid, s) : launch_pair<false, false, 0>(maps, prm, grid, s);
       case MEEP2B_EPI_SWIGLU:
-        return lora ? launch_pair<true, 1>(maps, prm, grid, s) : launch_pair<false, 1>(maps, prm, grid, s);
+        return lora ? launch_pair<false, true, 1>(maps, prm, grid, s) : launch_pair<false, false, 1>(maps, prm, grid, s);
       default:
-        return lora ? launch_pair<true, 2>(maps, prm, grid, s) : launch_pair<false, 2>(maps, prm, grid, s);
+        return lora ? launch_pair<false, true, 2>(maps, prm, grid, s) : launch_pair<false, false, 2>(maps, prm, grid, s);
     }
   }
   const int grid = static_cast<int>(units < sms ? (units > 0 ? units : 1) : sms);
