@@ -255,8 +255,9 @@ def run_meep2b(a):
 
     # End to end through the public API with host buffers: every step copies its inputs in from pinned host memory
     # and reads its results back (layer output, input gradient, LoRA gradients). As a training loop with a
-    # prefetching data loader does, the copies run on a second stream: step i+1's inputs go in and step i's results
-    # come out while step i+1 computes. The timed region covers every step's copies in both directions.
+    # prefetching data loader does, the copies run beside the compute: step i+1's inputs go in on one stream and
+    # step i's results come out on another (PCIe carries both directions at once) while step i+1 computes. The timed
+    # region covers every step's copies in both directions.
     h_host = hidden.cpu().pin_memory()
     i_host = idx.cpu().pin_memory()
     w_host = w.cpu().pin_memory()
@@ -267,20 +268,22 @@ def run_meep2b(a):
     d_in = [(torch.empty_like(hidden), torch.empty_like(idx), torch.empty_like(w), torch.empty_like(grad))
             for _ in range(2)]
     lg_stage = [torch.empty_like(bucket.flat) for _ in range(2)]
-    copy = torch.cuda.Stream(device)
+    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     in_ready = [torch.cuda.Event() for _ in range(2)]
-    used = [torch.cuda.Event() for _ in range(2)]  # step on this slot finished with its inputs and outputs
+    inputs_free = [None, None]   # the step that last read this input slot has finished
+    outputs_free = [None, None]  # the read-back of this slot's staged LoRA gradients has finished
 
     def h2d(slot):
-        copy.wait_event(used[slot])
-        with torch.cuda.stream(copy):
+        if inputs_free[slot] is not None:
+            copy_in.wait_event(inputs_free[slot])
+        with torch.cuda.stream(copy_in):
             for dst, src in zip(d_in[slot], (h_host, i_host, w_host, g_host)):
                 dst.copy_(src, non_blocking=True)
-            in_ready[slot].record(copy)
+            in_ready[slot].record(copy_in)
 
     def e2e_run(n):
-        for slot in range(2):
-            used[slot].record(stream)
+        inputs_free[:] = [None, None]
+        outputs_free[:] = [None, None]
         h2d(0)
         for i in range(n):
             cur = i % 2
@@ -290,20 +293,24 @@ def run_meep2b(a):
             hd, ids, wts, g = d_in[cur]
             h = hd.detach().requires_grad_()
             out = step(h, ids, wts, g)
+            if outputs_free[cur] is not None:
+                stream.wait_event(outputs_free[cur])
             lg_stage[cur].copy_(bucket.flat)
             done = torch.cuda.Event()
             done.record(stream)
-            copy.wait_event(done)
-            with torch.cuda.stream(copy):
+            inputs_free[cur] = done
+            copy_out.wait_event(done)
+            with torch.cuda.stream(copy_out):
                 out_host[cur].copy_(out.detach(), non_blocking=True)
                 gh_host[cur].copy_(h.grad, non_blocking=True)
                 lg_host[cur].copy_(lg_stage[cur], non_blocking=True)
-            out.record_stream(copy)
-            h.grad.record_stream(copy)
+            out.record_stream(copy_out)
+            h.grad.record_stream(copy_out)
             fin = torch.cuda.Event()
-            fin.record(copy)
-            used[cur] = fin
-        stream.wait_stream(copy)
+            fin.record(copy_out)
+            outputs_free[cur] = fin
+        stream.wait_stream(copy_in)
+        stream.wait_stream(copy_out)
 
     e2e_run(max(2, a.warmup))
     sync()
