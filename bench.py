@@ -28,7 +28,9 @@ sys.path.insert(0, ROOT)
 CONFIGS = {
     "qwen3_30b": dict(tokens=16384, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
     "mixtral": dict(tokens=8192, hidden=4096, inter=14336, experts=8, top_k=2, rank=16, alpha=32),
-    "qwen3_235b_fp8": dict(tokens=32768, hidden=4096, inter=1536, experts=128, top_k=8, rank=16, alpha=32, zipf=1.1),
+    "qwen3_30b_nf4": dict(tokens=16384, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32, quant="nf4"),
+    "qwen3_235b_fp8": dict(tokens=32768, hidden=4096, inter=1536, experts=128, top_k=8, rank=16, alpha=32, zipf=1.1,
+                           quant="fp8_block128"),
     "small": dict(tokens=2048, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
     "half": dict(tokens=8192, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
 }
@@ -184,8 +186,14 @@ def make_layer(c, device, seed):
 
     ex = Experts()
     ex.num_experts, ex.has_gate, ex.has_bias, ex.is_transposed = E, True, False, False
-    ex.gate_up_proj = (torch.randn(E, 2 * I, H, device=device, generator=g) * 0.02).to(torch.bfloat16)
-    ex.down_proj = (torch.randn(E, H, I, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    ex.gate_up_proj = torch.nn.Parameter((torch.randn(E, 2 * I, H, device=device, generator=g) * 0.02).to(torch.bfloat16),
+                                         requires_grad=False)
+    ex.down_proj = torch.nn.Parameter((torch.randn(E, H, I, device=device, generator=g) * 0.02).to(torch.bfloat16),
+                                      requires_grad=False)
+    if c.get("quant") == "nf4":  # QLoRA: NF4 blocks of 64, absmax double-quantised (blocks of 256)
+        mb._nf4.convert_stacks(ex)
+    elif c.get("quant") == "fp8_block128":  # e4m3 with a 128 x 128 grid of scales per expert matrix
+        mb._fp8.convert_stacks(ex, block=128)
     bound1, bound2 = 1.0 / H ** 0.5, 1.0 / I ** 0.5
     lora = {
         "lhs1": (torch.randn(E, 2 * I, r, device=device, generator=g) * 0.01).to(torch.bfloat16),
@@ -373,7 +381,7 @@ def cpu_baseline(c, tokens):
     import layer_inputs
     from oracle import layer as olayer
 
-    cfg = {k: v for k, v in c.items()}
+    cfg = {k: v for k, v in c.items() if k != "quant"}  # a quantised config's CPU leg runs the weights dequantised
     cfg["tokens"] = tokens
     inp = layer_inputs.layer(**cfg)
     fac = {"gate_up_proj": (inp["gate_up_lhs"].numpy(), inp["gate_up_rhs"].numpy(), inp["scaling"]),
@@ -385,24 +393,23 @@ def cpu_baseline(c, tokens):
         out, saved = olayer.forward(*args)
         olayer.backward(inp["grad"].numpy(), saved, inp["gate_up"].numpy(), inp["down"].numpy(), fac)
 
-    once()
-    reps = []
-    t_end = time.perf_counter() + 10.0
-    while len(reps) < 3 or (time.perf_counter() < t_end and len(reps) < 20):
-        t0 = time.perf_counter()
-        once()
-        reps.append(time.perf_counter() - t0)
-    sec = statistics.median(reps)
-    try:
-        from threadpoolctl import threadpool_info
+    # all host cores: a launcher (torchrun) sets OMP_NUM_THREADS=1 for its ranks, so the BLAS pool is raised here
+    from threadpoolctl import threadpool_info, threadpool_limits
 
+    with threadpool_limits(limits=os.cpu_count()):
+        once()
+        reps = []
+        t_end = time.perf_counter() + 10.0
+        while len(reps) < 3 or (time.perf_counter() < t_end and len(reps) < 20):
+            t0 = time.perf_counter()
+            once()
+            reps.append(time.perf_counter() - t0)
         cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
-    except Exception:
-        cores = os.cpu_count()
+    sec = statistics.median(reps)
     del np
     return {"value": round(tokens / sec, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{tokens} tokens of the workload (all {c['experts']} experts), fwd+bwd, float32 numpy, "
-                      f"median of {len(reps)}"}
+                      f"median of {len(reps)}" + (", stacks already dequantised" if c.get("quant") else "")}
 
 
 def run_reference(a):

@@ -29,7 +29,10 @@ enum meep2b_status {
   MEEP2B_ERR_DEVICE = 7       /* no compute capability 10.0 GPU: RuntimeError */
 };
 
-enum meep2b_dtype { MEEP2B_F32 = 0, MEEP2B_BF16 = 1, MEEP2B_E4M3 = 2 };
+/* F32, BF16: plain types. Weight formats of meep2b_product.weight_dtype: BF16; E4M3 (codes converted exactly,
+ * the per-expert `scale` applied in the epilogue); NF4 (packed codes with their block absmax); E4M3_BLOCKS (codes
+ * with a grid of block scales). The last two take per-group multipliers (meep2b_quant_multipliers) in `wscale`. */
+enum meep2b_dtype { MEEP2B_F32 = 0, MEEP2B_BF16 = 1, MEEP2B_E4M3 = 2, MEEP2B_NF4 = 3, MEEP2B_E4M3_BLOCKS = 4 };
 
 enum meep2b_epilogue {
   MEEP2B_EPI_PLAIN = 0,   /* out = scale_e * (x W^T) + s (x A^T) B^T + bias_e                                   */
@@ -124,12 +127,18 @@ int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32
  * expert are contiguous, offsets[e] is the end of expert e's rows (int32, inclusive cumsum). tile_expert /
  * tile_row / tiles come from meep2b_tile_map with the product's block_m: 128 (one CTA per tile) or 256 (a CTA
  * pair per tile, tcgen05 cta_group::2, for b_mn == 0 only; each SM then stages half of the stack tile).
- * low (rows, 16) receives bf16(x P_e^T) when not NULL (kept for the backward pass, _grouped.py:212-214). */
+ * low (rows, 16) receives bf16(x P_e^T) when not NULL (kept for the backward pass, _grouped.py:212-214).
+ * Quantised stacks (weight_dtype NF4, E4M3, E4M3_BLOCKS; block_m 128; k and n multiples of 64) are dequantised in
+ * shared memory between the TMA load and the MMA, exactly as the reference dequantises them (_grouped.py:200-201
+ * for E4M3; axolotl quantize.py:85-96 for NF4 and :131-157 for the block scales). weight then holds the codes of
+ * the stored (experts, rows, cols) stack, cols contiguous (NF4: two codes a byte, the first in the high nibble);
+ * wscale (NF4, E4M3_BLOCKS): the multiplier of each group of 64 consecutive weights, (experts, cols/64, rows)
+ * float32, as meep2b_quant_multipliers prepares it once per frozen stack. */
 typedef struct meep2b_product {
   const void* x;
   int64_t rows, k, ldx;
   const void* weight;
-  int32_t weight_dtype; /* MEEP2B_BF16 */
+  int32_t weight_dtype; /* MEEP2B_BF16, MEEP2B_E4M3, MEEP2B_NF4 or MEEP2B_E4M3_BLOCKS */
   int32_t experts;
   int64_t n;
   int32_t b_mn;
@@ -149,7 +158,8 @@ typedef struct meep2b_product {
   int32_t epilogue;     /* enum meep2b_epilogue */
   void* aux;            /* SWIGLU: pre-activation out (rows, n); DSWIGLU: pre-activation in (rows, 2n) */
   int32_t sm_limit;     /* 0: one CTA per SM */
-  int32_t block_m;      /* rows per tile: 128, or 256 for the CTA-pair kernel (b_mn == 0); 0 means 128 */
+  int32_t block_m;      /* rows per tile: 128, or 256 for the CTA-pair kernel (bf16 stacks); 0 means 128 */
+  const float* wscale;  /* NF4, E4M3_BLOCKS: per-group multipliers (experts, cols/64, rows); else NULL */
 } meep2b_product;
 
 int meep2b_grouped_product(const meep2b_product* p, void* stream);
@@ -178,6 +188,21 @@ int meep2b_fp8_block_dequantize(const uint8_t* codes, int64_t matrices, int64_t 
  * scale = max(amax_block, 1e-12) / 448, codes = e4m3(clamp(w / scale, +-448)); w bf16 or f32. */
 int meep2b_fp8_block_quantize(const void* w, int32_t dtype, int64_t matrices, int64_t rows, int64_t cols,
                               int32_t sr, int32_t sc, uint8_t* codes, float* scale_inv, void* stream);
+/* The first stage of the NF4 dequantisation (axolotl quantize.py:74-83, bitsandbytes'
+ * cdequantize_blockwise_fp32 then `+= offset`): absmax_out[i] = code2[absmax[i]] * absmax2[i / blocksize2] +
+ * offset[0], two float32 roundings; count = number of 64-weight blocks. Its output is the `wscale` of an NF4
+ * product (computed once per frozen stack). */
+int meep2b_nf4_absmax(const uint8_t* absmax, const float* absmax2, const float* code2, const float* offset,
+                      int32_t blocksize2, int64_t count, float* absmax_out, void* stream);
+/* The multipliers of a quantised stack for meep2b_grouped_product, out (experts, cols/64, rows) float32, one per
+ * group of 64 consecutive weights of each stored (rows, cols) matrix (cols a multiple of 64):
+ *   MEEP2B_NF4:         src = the float32 absmax per 64-weight block in storage order (meep2b_nf4_absmax's output):
+ *                       out[e][g][r] = src[(e * rows + r) * (cols / 64) + g];
+ *   MEEP2B_E4M3_BLOCKS: src = the (experts, sr, sc) scales of dequantize_fp8 (quantize.py:131-157):
+ *                       out[e][g][r] = bf16(src[e][r / br][64 g / bc]), br = ceil(rows/sr), bc = ceil(cols/sc)
+ *                       (bc a multiple of 64: one scale per group). */
+int meep2b_quant_multipliers(int32_t weight_dtype, const float* src, int32_t experts, int64_t rows, int64_t cols,
+                             int32_t sr, int32_t sc, float* out, void* stream);
 /* The NF4 double dequantisation of axolotl quantize._ctypes_nf4_dequant (quantize.py:52-101), which calls
  * bitsandbytes' cdequantize_blockwise_fp32 then `+= offset` then cdequantize_blockwise_bf16_nf4:
  * absmax_out[i] = code2[absmax[i]] * absmax2[i / blocksize2] + offset[0] (two float32 roundings);

@@ -82,6 +82,16 @@ def quantize_blocks(weight: torch.Tensor, grid=None, block: int = 128) -> tuple[
     return codes, scale
 
 
+def dequantize(weight8: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """An FP8 stack in bf16 by the form of its scale: (E,) one per expert, (E, sr, sc) a grid of blocks."""
+    if scale.dim() == 1:
+        return dequantize_stack(weight8, scale, torch.bfloat16)
+    if scale.dim() == weight8.dim():
+        return dequantize_blocks(weight8, scale)
+    raise ValueError(f"an FP8 stack of shape {tuple(weight8.shape)} takes a scale of (experts,) or "
+                     f"(experts, rows/block, cols/block); got {tuple(scale.shape)}")
+
+
 def dequantize_blocks(codes: torch.Tensor, scale_inv: torch.Tensor) -> torch.Tensor:
     """bf16(bf16(w8) * bf16(scale)) per block, the reference's dequantize_fp8 with dtype bf16."""
     _cuda(codes, "dequantize_blocks")
@@ -96,8 +106,12 @@ def dequantize_blocks(codes: torch.Tensor, scale_inv: torch.Tensor) -> torch.Ten
     return out
 
 
-def convert_stacks(experts) -> int:
-    """Every frozen stack of an experts module held as FP8, its scale as <name>_scale_inv; returns how many."""
+def convert_stacks(experts, block: int | None = None) -> int:
+    """Every frozen stack of an experts module held as FP8, its scale as <name>_scale_inv; returns how many.
+
+    block=None: one scale per expert, (E,) (meepsquared/_fp8.py:170-186). block=128: a grid of 128 x 128 blocks per
+    expert matrix, scale_inv (E, ceil(out/128), ceil(in/128)), as an FP8 checkpoint of block-scaled weights holds.
+    """
     converted = 0
     for name, parameter in list(experts.named_parameters(recurse=False)):
         if parameter.dim() != 3 or parameter.requires_grad or not parameter.is_floating_point():
@@ -105,7 +119,10 @@ def convert_stacks(experts) -> int:
         if parameter.dtype == torch.float8_e4m3fn and hasattr(experts, name + STACK_SCALE):
             converted += 1
             continue
-        weight8, scale = quantize_stack(parameter.detach())
+        if block is None:
+            weight8, scale = quantize_stack(parameter.detach())
+        else:
+            weight8, scale = quantize_blocks(parameter.detach(), block=block)
         setattr(experts, name, nn.Parameter(weight8, requires_grad=False))
         experts.register_buffer(name + STACK_SCALE, scale)
         converted += 1

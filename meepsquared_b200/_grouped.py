@@ -205,6 +205,61 @@ class _Adapters:
         return self._cache[key]
 
 
+class QuantStack:
+    """A frozen stack held quantised, read by the product as it is and dequantised in shared memory.
+
+    codes: the stored (experts, rows, cols) stack, cols contiguous: e4m3 codes (uint8 or float8_e4m3fn), or NF4
+    codes packed two a byte (experts, rows, cols / 2). kind: _lib.E4M3 (the per-expert scale goes to the product
+    as `scale`), _lib.NF4 or _lib.E4M3_BLOCKS; for the last two `mult` holds the multiplier of each group of 64
+    consecutive weights, (experts, cols/64, rows) float32 (meep2b_quant_multipliers): the block absmax (NF4), or
+    the bf16 value of the block scale, blocks of ceil(rows/sr) x ceil(cols/sc) as the reference's dequantize_fp8
+    sizes them for an (sr, sc) grid.
+    """
+
+    def __init__(self, codes: torch.Tensor, kind: int, shape, mult=None, grid=(0, 0)):
+        self.codes, self.kind, self.shape, self.mult, self.grid = codes, kind, tuple(shape), mult, tuple(grid)
+        self.device = codes.device
+
+    @staticmethod
+    def fits(shape) -> bool:
+        """Whether the fused product takes the stack: whole 64-weight blocks along both matrix dimensions."""
+        return shape[1] % 64 == 0 and shape[2] % 64 == 0
+
+    @staticmethod
+    def multipliers(kind, src, shape, grid=(0, 0)) -> torch.Tensor:
+        e, rows, cols = shape
+        out = torch.empty((e, cols // 64, rows), device=src.device, dtype=torch.float32)
+        _lib.check(_lib.load().meep2b_quant_multipliers(kind, _lib.ptr(src.float().contiguous()), e, rows, cols,
+                                                        grid[0], grid[1], _lib.ptr(out), _lib.stream_of(src)),
+                   "meep2b_quant_multipliers")
+        return out
+
+    @classmethod
+    def from_fp8(cls, weight8: torch.Tensor, scale: torch.Tensor):
+        """An FP8 stack with one scale per expert (E4M3) or a grid of block scales (E4M3_BLOCKS) whose column
+        blocks are whole 64-column groups; None if the product does not take it fused."""
+        if not cls.fits(weight8.shape) or not weight8.is_contiguous():
+            return None
+        e, rows, cols = weight8.shape
+        if scale.dim() == 1:
+            return cls(weight8, _lib.E4M3, weight8.shape)
+        if scale.dim() == 3 and scale.shape[0] == e and 0 < scale.shape[1] <= rows and 0 < scale.shape[2] <= cols:
+            grid = (int(scale.shape[1]), int(scale.shape[2]))
+            if (-(-cols // grid[1])) % 64 == 0:
+                if not weight8.is_cuda:
+                    return cls(weight8, _lib.E4M3_BLOCKS, weight8.shape, None, grid)
+                mult = cls.multipliers(_lib.E4M3_BLOCKS, scale, weight8.shape, grid)
+                return cls(weight8, _lib.E4M3_BLOCKS, weight8.shape, mult, grid)
+        return None
+
+    @classmethod
+    def from_nf4(cls, state):
+        """An NF4 stack (blocks of 64 along its rows); None if not fused."""
+        if len(state.shape) != 3 or not cls.fits(state.shape) or state.blocksize != 64:
+            return None
+        return cls(state.packed, _lib.NF4, state.shape, state.multipliers())
+
+
 def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward=False,
             tiles=None, epilogue=_lib.EPI_PLAIN, aux=None, out=None):
     """One launch of the grouped product; returns (out, low). The reference's _launch (_grouped.py:313-345).
@@ -212,12 +267,21 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
     k_contiguous_layout: whether the stack is logically (experts, n, k) for this product.
     """
     rows, K = x.shape
-    stack, b_mn = _stack_memory(weight, k_contiguous_layout)
-    N = stack.shape[1] if b_mn == 0 else stack.shape[2]
-    if weight.dtype == torch.float8_e4m3fn:
-        raise NotImplementedError("an FP8 stack is dequantized by the caller (meepsquared_b200._fp8)")
-    if weight.dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
-        raise TypeError(f"the grouped kernel computes in bf16: x {x.dtype}, stack {weight.dtype}")
+    quant = isinstance(weight, QuantStack)
+    if quant:  # stored (E, rows, cols) as it is: K-major when the product contracts over its columns
+        stack, b_mn = weight.codes, 0 if k_contiguous_layout else 1
+        experts, N = weight.shape[0], weight.shape[1] if b_mn == 0 else weight.shape[2]
+        if weight.shape[2 if b_mn == 0 else 1] != K:
+            raise ValueError(f"a quantised stack {weight.shape} does not take x with {K} columns")
+    else:
+        stack, b_mn = _stack_memory(weight, k_contiguous_layout)
+        experts, N = stack.shape[0], stack.shape[1] if b_mn == 0 else stack.shape[2]
+        if weight.dtype == torch.float8_e4m3fn:
+            raise NotImplementedError("an FP8 stack goes to the product as a QuantStack or dequantized")
+        if weight.dtype != torch.bfloat16:
+            raise TypeError(f"the grouped kernel computes in bf16: stack {weight.dtype}")
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"the grouped kernel computes in bf16: x {x.dtype}")
     if x.stride(1) != 1 or x.stride(0) % 8:
         x = x.contiguous()
     if epilogue == _lib.EPI_SWIGLU:
@@ -235,14 +299,16 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
         return out, low
     if tiles is None:
         tiles = TileMaps(offsets, rows)
-    block_m = 256 if _pair_tiles(b_mn, rows, stack.shape[0], K, adapters is not None) else 128
+    block_m = 256 if not quant and _pair_tiles(b_mn, rows, experts, K, adapters is not None) else 128
     tmap = tiles.get(block_m)
     panel = up = None
     if adapters is not None:
         panel, up = adapters.operands(b_mn, backward)
     p = _lib.Product()
     p.x, p.rows, p.k, p.ldx = x.data_ptr(), rows, K, x.stride(0)
-    p.weight, p.weight_dtype, p.experts, p.n, p.b_mn = stack.data_ptr(), _lib.BF16, stack.shape[0], N, b_mn
+    p.weight, p.experts, p.n, p.b_mn = stack.data_ptr(), experts, N, b_mn
+    p.weight_dtype = weight.kind if quant else _lib.BF16
+    p.wscale = weight.mult.data_ptr() if quant and weight.mult is not None else None
     p.scale = scale.data_ptr() if scale is not None else None
     p.panel = panel.data_ptr() if panel is not None else None
     p.up = up.data_ptr() if up is not None else None
@@ -312,13 +378,15 @@ class _LoraGroupedProduct(torch.autograd.Function):
         adapters = _Adapters(lhs.detach(), rhs.detach(), is_transposed) if lhs is not None else None
         tiles = TileMaps(offsets, x.shape[0])
         out, low = _launch(x, weight, scale, offsets, not is_transposed, adapters, scaling, bias, True, tiles=tiles)
-        ctx.save_for_backward(x, weight, offsets, *((low,) if low is not None else ()))
+        ctx.save_for_backward(x, offsets, *((low,) if low is not None else ()))
+        ctx.weight = weight  # the frozen stack (a tensor or a QuantStack), read again by the backward product
         ctx.adapters, ctx.scale, ctx.is_transposed, ctx.scaling, ctx.tiles = adapters, scale, is_transposed, scaling, tiles
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        x, weight, offsets, *rest = ctx.saved_tensors
+        x, offsets, *rest = ctx.saved_tensors
+        weight = ctx.weight
         adapters = ctx.adapters
         grad_out = grad_out.contiguous()
         if adapters is None:
@@ -342,12 +410,17 @@ def _check_fp8_products(weight, products_fp8, device):
 
 
 def _dequantized(weight, scale):
-    """An FP8 stack as bf16 for one product: (bf16 stack, the scale left for the kernel to apply)."""
+    """An FP8 stack for the products: (stack, the scale left for the kernel to apply). The codes go to the kernel
+    as they are (converted exactly in shared memory, as the reference's kernel converts its FP8 tile) when the stack
+    has whole 64-blocks; otherwise they are converted to bf16 here, exactly, without the scale."""
     if weight.dtype != torch.float8_e4m3fn:
         return weight, scale
+    ones = torch.ones(weight.shape[0], device=weight.device, dtype=torch.float32)
+    fused = QuantStack.from_fp8(weight, ones)
+    if fused is not None:
+        return fused, scale
     from . import _fp8
 
-    ones = torch.ones(weight.shape[0], device=weight.device, dtype=torch.float32)
     return _fp8.dequantize_stack(weight, ones, torch.bfloat16), scale
 
 

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libmeep2b.so")
 
 OK, ERR_SHAPE, ERR_DTYPE, ERR_LAUNCH, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_ALIGN, ERR_DEVICE = range(8)
-F32, BF16, E4M3 = 0, 1, 2
+F32, BF16, E4M3, NF4, E4M3_BLOCKS = 0, 1, 2, 3, 4  # enum meep2b_dtype
 EPI_PLAIN, EPI_SWIGLU, EPI_DSWIGLU = 0, 1, 2
 
 _p, _i64, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_size_t
@@ -28,7 +28,7 @@ class Product(ctypes.Structure):
         ("scale", _p), ("panel", _p), ("up", _p), ("scaling", _f32), ("bias", _p),
         ("offsets", _p), ("tile_expert", _p), ("tile_row", _p), ("tiles", _p), ("max_tiles", _i64),
         ("out", _p), ("ldo", _i64), ("low", _p), ("epilogue", _i32), ("aux", _p), ("sm_limit", _i32),
-        ("block_m", _i32),
+        ("block_m", _i32), ("wscale", _p),
     ]
 
 
@@ -51,6 +51,8 @@ _SIGNATURES = {
     "meep2b_fp8_stack_dequantize": (ctypes.c_int, [_p, _p, _i32, _i64, _p, _p]),
     "meep2b_fp8_block_dequantize": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i32, _i32, _p, _p]),
     "meep2b_fp8_block_quantize": (ctypes.c_int, [_p, _i32, _i64, _i64, _i64, _i32, _i32, _p, _p, _p]),
+    "meep2b_nf4_absmax": (ctypes.c_int, [_p, _p, _p, _p, _i32, _i64, _p, _p]),
+    "meep2b_quant_multipliers": (ctypes.c_int, [_i32, _p, _i32, _i64, _i64, _i32, _i32, _p, _p]),
     "meep2b_nf4_dequantize": (ctypes.c_int, [_p, _p, _p, _p, _p, _i32, _i32, _i64, _p, _p, _p]),
 }
 

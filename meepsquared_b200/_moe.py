@@ -139,7 +139,10 @@ class _RoutedExperts(torch.autograd.Function):
         t = st.is_transposed
         ad1 = _grouped._Adapters(lhs1.detach(), rhs1.detach(), t) if lhs1 is not None else None
         ad2 = _grouped._Adapters(lhs2.detach(), rhs2.detach(), t) if lhs2 is not None else None
-        _, b_mn = _grouped._stack_memory(st.gate_up, not t)
+        if isinstance(st.gate_up, _grouped.QuantStack):
+            b_mn = 1 if t else 0
+        else:
+            _, b_mn = _grouped._stack_memory(st.gate_up, not t)
         if b_mn != 0:
             raise NotImplementedError("SwiGLU is fused for a gate/up stack stored (experts, 2I, hidden), k contiguous")
         two_i = st.gate_up.shape[2] if t else st.gate_up.shape[1]
@@ -182,36 +185,55 @@ class _RoutedExperts(torch.autograd.Function):
         return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None)
 
 
-def _bf16_stack(weight, scale):
-    """A stack for the kernels: bf16 as it is, or an FP8 stack dequantized for this call (its scale applied)."""
-    if weight.dtype == torch.float8_e4m3fn:
-        from . import _fp8
+def _kernel_stack(experts, name):
+    """(stack, scale) for the kernels. A bf16 stack as it is. A quantised one goes to the products as a QuantStack,
+    dequantised in shared memory between the TMA load and the MMA: FP8 (e4m3) with its `<name>_scale_inv` (one
+    scale per expert, applied in the epilogue, or a 128 x 128 grid of blocks) or NF4 (an NF4State in the
+    attribute's place). A quantised stack without whole 64-weight blocks is dequantised for this call instead."""
+    from . import _fp8, _nf4
 
-        return _fp8.dequantize_stack(weight, scale, torch.bfloat16)
+    weight = getattr(experts, name)
+    if isinstance(weight, _nf4.NF4State):
+        fused = _grouped.QuantStack.from_nf4(weight)
+        return (fused if fused is not None else _nf4.dequantize(weight)), None
+    if weight.dtype == torch.float8_e4m3fn:
+        scale = getattr(experts, name + _fp8.STACK_SCALE)
+        # the multipliers of a block-scaled stack are prepared once and kept while the stack and scale are unchanged
+        cache = experts.__dict__.setdefault("_meep2b_quant_stacks", {})
+        key = (weight.data_ptr(), weight._version, scale.data_ptr(), scale._version)
+        hit = cache.get(name)
+        if hit is not None and hit[0] == key:
+            fused = hit[1]
+        else:
+            fused = _grouped.QuantStack.from_fp8(weight.detach(), scale)
+            cache[name] = (key, fused)
+        if fused is None:
+            return _fp8.dequantize(weight.detach(), scale), None
+        return fused, (scale.float().contiguous() if fused.kind == _lib.E4M3 else None)
     if weight.dtype != torch.bfloat16:
-        raise TypeError(f"expert stacks in bf16 or FP8 (e4m3); got {weight.dtype}")
-    return weight
+        raise TypeError(f"expert stacks in bf16, FP8 (e4m3) or NF4; got {weight.dtype}")
+    return weight.detach(), None
 
 
 def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
     """The routed layer of a gated experts module with its adapters: _moe._routed_forward's contract.
 
     experts: a Transformers experts module (num_experts, has_gate, has_bias, is_transposed, gate_up_proj,
-    down_proj; FP8 stacks with ``<name>_scale_inv``). factors: {stack name: (lhs, rhs, scaling)} in PEFT's layout.
+    down_proj; FP8 stacks with ``<name>_scale_inv`` of one scale per expert or a 128 x 128 block grid; NF4 stacks
+    as an ``_nf4.NF4State`` in the stack's place). factors: {stack name: (lhs, rhs, scaling)} in PEFT's layout.
     """
     if not experts.has_gate:
         raise NotImplementedError("the fused layer needs a gated experts module (gate_up_proj)")
     if not hidden_states.is_cuda:
         raise RuntimeError("the routed layer runs on a CUDA GPU (compute capability 10.0)")
-    gate_up, down = experts.gate_up_proj, experts.down_proj
-    scale1 = getattr(experts, "gate_up_proj_scale_inv", None) if gate_up.dtype == torch.float8_e4m3fn else None
-    scale2 = getattr(experts, "down_proj_scale_inv", None) if down.dtype == torch.float8_e4m3fn else None
     bias1 = experts.gate_up_proj_bias if experts.has_bias else None
     bias2 = experts.down_proj_bias if experts.has_bias else None
     lhs1, rhs1, s1 = factors.get("gate_up_proj", (None, None, 1.0))
     lhs2, rhs2, s2 = factors.get("down_proj", (None, None, 1.0))
     cast = lambda f: f.to(torch.bfloat16) if f is not None and f.dtype != torch.bfloat16 else f  # noqa: E731
-    st = _Stacks(_bf16_stack(gate_up.detach(), scale1), _bf16_stack(down.detach(), scale2), None, None,
+    gate_up, scale1 = _kernel_stack(experts, "gate_up_proj")
+    down, scale2 = _kernel_stack(experts, "down_proj")
+    st = _Stacks(gate_up, down, scale1, scale2,
                  bias1.detach().to(torch.bfloat16).contiguous() if bias1 is not None else None,
                  bias2.detach().to(torch.bfloat16).contiguous() if bias2 is not None else None,
                  bool(experts.is_transposed), int(experts.num_experts), float(s1), float(s2))

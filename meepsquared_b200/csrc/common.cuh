@@ -21,6 +21,25 @@ namespace meep2b {
 // read back, and cleared, by meep2b_device_error(). (The library is one translation unit, libmeep2b.cu.)
 __device__ int g_device_error = 0;
 
+// The 16 NormalFloat-4 levels (QLoRA, Dettmers et al. 2023, appendix E), as float32: the NF4 code book of the
+// dequantisation kernel and of the grouped product's in-shared-memory converter.
+__constant__ float kNF4Levels[16] = {-1.0f,
+                                     -0.6961928009986877f,
+                                     -0.5250730514526367f,
+                                     -0.39491748809814453f,
+                                     -0.28444138169288635f,
+                                     -0.18477343022823334f,
+                                     -0.09105003625154495f,
+                                     0.0f,
+                                     0.07958029955625534f,
+                                     0.16093020141124725f,
+                                     0.24611230194568634f,
+                                     0.33791524171829224f,
+                                     0.44070982933044434f,
+                                     0.5626170039176941f,
+                                     0.7229568362236023f,
+                                     1.0f};
+
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_device_error, 0, code); }
 __device__ __forceinline__ bool error_seen() { return *(volatile int*)&g_device_error != 0; }
 

@@ -945,6 +945,8 @@ static int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMa
   return launch_status();
 }
 
+#include "grouped_gemm_q.cuh"
+
 }  // namespace gemm
 }  // namespace meep2b
 
@@ -953,7 +955,10 @@ using namespace meep2b::gemm;
 
 extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   if (a == nullptr) return MEEP2B_ERR_SHAPE;
-  if (a->weight_dtype != MEEP2B_BF16) return MEEP2B_ERR_UNSUPPORTED;
+  const bool quantised = a->weight_dtype == MEEP2B_NF4 || a->weight_dtype == MEEP2B_E4M3 ||
+                         a->weight_dtype == MEEP2B_E4M3_BLOCKS;
+  if (a->weight_dtype != MEEP2B_BF16 && !quantised) return MEEP2B_ERR_UNSUPPORTED;
+  if (quantised && a->block_m == 256) return MEEP2B_ERR_UNSUPPORTED;
   if (a->rows < 0 || a->k < 1 || a->n < 1 || a->experts < 1) return MEEP2B_ERR_SHAPE;
   if (a->k % 8 || a->n % 8 || a->ldx % 8 || a->ldo % 8 || a->ldx < a->k) return MEEP2B_ERR_ALIGN;
   if (a->rows > INT32_MAX || a->k > INT32_MAX || a->n > INT32_MAX) return MEEP2B_ERR_SHAPE;
@@ -980,7 +985,9 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
                             CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const uint32_t rows_per_load = (epi == MEEP2B_EPI_SWIGLU) ? 96 : BN;
-  if (!a->b_mn) {
+  if (quantised) {
+    tw = tx;  // the codes get their own map (launch_quantized)
+  } else if (!a->b_mn) {
     const uint64_t dims[3] = {K, N, E};
     const uint64_t strides[2] = {K * 2, N * K * 2};
     const uint32_t box[3] = {64, rows_per_load, 1};
@@ -1113,6 +1120,7 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
     }
   }
   const int grid = static_cast<int>(units < sms ? (units > 0 ? units : 1) : sms);
+  if (quantised) return launch_quantized(a, tx, tp, tu, prm, grid, s);
 
   const bool mn = a->b_mn != 0;
   switch (epi) {

@@ -121,24 +121,6 @@ __global__ void block_quant(const T* __restrict__ w, int64_t rows, int64_t cols,
   }
 }
 
-// The 16 NormalFloat levels (QLoRA, Dettmers et al. 2023), as float32.
-__constant__ float kNF4[16] = {-1.0f,
-                               -0.6961928009986877f,
-                               -0.5250730514526367f,
-                               -0.39491748809814453f,
-                               -0.28444138169288635f,
-                               -0.18477343022823334f,
-                               -0.09105003625154495f,
-                               0.0f,
-                               0.07958029955625534f,
-                               0.16093020141124725f,
-                               0.24611230194568634f,
-                               0.33791524171829224f,
-                               0.44070982933044434f,
-                               0.5626170039176941f,
-                               0.7229568362236023f,
-                               1.0f};
-
 __global__ void nf4_absmax(const uint8_t* __restrict__ absmax, const float* __restrict__ absmax2,
                            const float* __restrict__ code2, const float* __restrict__ offset, int blocksize2,
                            int64_t count, float* __restrict__ out) {
@@ -163,8 +145,8 @@ __global__ void nf4_dequant(const uint2* __restrict__ packed, const float* __res
       for (int b = 0; b < 4; ++b) {
         const uint32_t byte = (words[w] >> (8 * b)) & 0xFF;
         const int64_t j = first + 8 * w + 2 * b;
-        const float hi = __fmul_rn(kNF4[byte >> 4], absmax[j / blocksize]);
-        const float lo = __fmul_rn(kNF4[byte & 0xF], absmax[(j + 1) / blocksize]);
+        const float hi = __fmul_rn(kNF4Levels[byte >> 4], absmax[j / blocksize]);
+        const float lo = __fmul_rn(kNF4Levels[byte & 0xF], absmax[(j + 1) / blocksize]);
         res[4 * w + b] = pack_bf16x2(hi, lo);
       }
     }
@@ -178,8 +160,22 @@ __global__ void nf4_dequant_tail(const uint8_t* __restrict__ packed, const float
   const int64_t b = first_byte + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (b >= bytes) return;
   const uint8_t v = packed[b];
-  out[2 * b] = __float2bfloat16_rn(__fmul_rn(kNF4[v >> 4], absmax[(2 * b) / blocksize]));
-  out[2 * b + 1] = __float2bfloat16_rn(__fmul_rn(kNF4[v & 0xF], absmax[(2 * b + 1) / blocksize]));
+  out[2 * b] = __float2bfloat16_rn(__fmul_rn(kNF4Levels[v >> 4], absmax[(2 * b) / blocksize]));
+  out[2 * b + 1] = __float2bfloat16_rn(__fmul_rn(kNF4Levels[v & 0xF], absmax[(2 * b + 1) / blocksize]));
+}
+
+// out[e][g][r] (experts, cols/64, rows): NF4 the absmax of block (e, r, g) (storage order), else the bf16 value of
+// the block scale covering group g of row r.
+__global__ void quant_multipliers(int nf4, const float* __restrict__ src, int64_t rows, int64_t groups, int sr, int sc,
+                                  int64_t br, int64_t bc, int64_t total, float* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t per = groups * rows;
+    const int64_t e = i / per, rem = i - e * per;
+    const int64_t g = rem / rows, r = rem - g * rows;
+    out[i] = nf4 ? src[(e * rows + r) * groups + g]
+                 : bf16_round(src[(e * sr + r / br) * sc + (64 * g) / bc]);
+  }
 }
 
 inline unsigned grid_for(int64_t n, int threads = 256) {
@@ -253,6 +249,34 @@ int meep2b_fp8_block_quantize(const void* w, int32_t dtype, int64_t matrices, in
   else
     block_quant<float><<<grid, 256, 0, s>>>(static_cast<const float*>(w), rows, cols, sr, sc, br, bc, codes,
                                             scale_inv);
+  return launch_status();
+}
+
+int meep2b_quant_multipliers(int32_t weight_dtype, const float* src, int32_t experts, int64_t rows, int64_t cols,
+                             int32_t sr, int32_t sc, float* out, void* stream) {
+  if (experts < 1 || rows < 1 || cols < 64 || cols % 64) return MEEP2B_ERR_SHAPE;
+  if (weight_dtype != MEEP2B_NF4 && weight_dtype != MEEP2B_E4M3_BLOCKS) return MEEP2B_ERR_DTYPE;
+  int64_t br = 1, bc = 64;
+  if (weight_dtype == MEEP2B_E4M3_BLOCKS) {
+    if (sr < 1 || sc < 1 || sr > rows || sc > cols) return MEEP2B_ERR_SHAPE;
+    br = (rows + sr - 1) / sr;
+    bc = (cols + sc - 1) / sc;
+    if (bc % 64) return MEEP2B_ERR_UNSUPPORTED;
+  }
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  const int64_t total = static_cast<int64_t>(experts) * rows * (cols / 64);
+  quant_multipliers<<<grid_for(total), 256, 0, s>>>(weight_dtype == MEEP2B_NF4, src, rows, cols / 64, sr, sc, br, bc,
+                                                     total, out);
+  return launch_status();
+}
+
+int meep2b_nf4_absmax(const uint8_t* absmax, const float* absmax2, const float* code2, const float* offset,
+                      int32_t blocksize2, int64_t count, float* absmax_out, void* stream) {
+  if (count < 1 || blocksize2 < 1) return MEEP2B_ERR_SHAPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  nf4_absmax<<<grid_for(count), 256, 0, s>>>(absmax, absmax2, code2, offset, blocksize2, count, absmax_out);
   return launch_status();
 }
 

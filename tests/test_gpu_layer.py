@@ -98,3 +98,42 @@ def test_full_size_layer_step_is_finite_and_deterministic():
     for k in a:
         assert torch.isfinite(a[k].float()).all(), k
         assert torch.equal(a[k], b[k]), k
+
+
+def _dequantised(ex, name):
+    from meepsquared_b200 import _fp8, _nf4
+
+    w = getattr(ex, name)
+    if isinstance(w, _nf4.NF4State):
+        return _nf4.dequantize(w).float().cpu()
+    return _fp8.dequantize(w, getattr(ex, name + "_scale_inv")).float().cpu()
+
+
+@pytest.mark.parametrize("kind", ["nf4", "fp8_expert", "fp8_block128"])
+def test_layer_with_quantised_stacks_matches_the_oracle_on_the_dequantised_weights(kind):
+    """QLoRA (NF4) and FP8 stacks (one scale per expert, or 128 x 128 blocks) in the routed layer: the layer equals
+    the float32 computation with the stacks dequantised as the reference dequantises them."""
+    from meepsquared_b200 import _fp8, _nf4
+
+    inp = layer_inputs.layer(**dict(layer_inputs.QWEN3_30B, tokens=256, experts=16))
+    idx = inp["top_k_index"]
+    bf = lambda n: inp[n].to(DEV, torch.bfloat16)  # noqa: E731
+    experts = Experts(bf("gate_up"), bf("down"))
+    if kind == "nf4":
+        assert _nf4.convert_stacks(experts) == 2
+        assert isinstance(experts.gate_up_proj, _nf4.NF4State)
+    else:
+        assert _fp8.convert_stacks(experts, block=128 if kind == "fp8_block128" else None) == 2
+        assert experts.gate_up_proj.dtype == torch.float8_e4m3fn
+    hidden = bf("hidden").requires_grad_()
+    weights = inp["top_k_weights"].to(DEV).requires_grad_()
+    leaves = {n: bf(n).requires_grad_() for n in ("gate_up_lhs", "gate_up_rhs", "down_lhs", "down_rhs")}
+    factors = {"gate_up_proj": (leaves["gate_up_lhs"], leaves["gate_up_rhs"], inp["scaling"]),
+               "down_proj": (leaves["down_lhs"], leaves["down_rhs"], inp["scaling"])}
+    out = mb.routed_forward(experts, hidden, idx.to(DEV), weights, factors)
+    out.backward(inp["grad"].to(DEV, torch.bfloat16))
+    res = {"out": out.detach(), "grad_hidden": hidden.grad, "grad_weights": weights.grad}
+    for n, t in leaves.items():
+        res[f"grad_{n}"] = t.grad
+    ref_inp = dict(inp, gate_up=_dequantised(experts, "gate_up_proj"), down=_dequantised(experts, "down_proj"))
+    check_against(res, oracle_layer(ref_inp, idx), scaled=True)

@@ -63,3 +63,38 @@ def test_nf4_dequantisation_is_bit_exact_with_the_oracle(shape):
                           torch.from_numpy(st["absmax2"]), torch.from_numpy(st["code2"]),
                           torch.tensor([st["offset"]], dtype=torch.float32), tuple(shape)).to(DEV)
     np.testing.assert_array_equal(bits(_nf4.dequantize(state)), quant.dequantize_nf4(st))
+
+
+def _state_np(state):
+    return {"packed": state.packed.cpu().numpy(), "absmax": state.absmax.cpu().numpy(),
+            "absmax2": state.absmax2.cpu().numpy(), "code2": state.code2.cpu().numpy(),
+            "offset": np.float32(state.offset.item()), "blocksize": state.blocksize,
+            "blocksize2": state.blocksize2, "shape": state.shape}
+
+
+@pytest.mark.parametrize("shape", [(4, 96, 128), (2, 1536, 2048)])
+def test_nf4_quantisation_on_the_gpu_matches_the_oracle(shape):
+    """The load-time quantiser: the same codes and absmax state as the oracle's bitsandbytes restatement, and its
+    state dequantises bit-exactly as the oracle dequantises it."""
+    rng = np.random.default_rng(7 + sum(shape))
+    w = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+    state = _nf4.quantize(torch.from_numpy(w).to(DEV))
+    want = quant.quantize_nf4(w)
+    np.testing.assert_array_equal(state.code2.cpu().numpy(), want["code2"])
+    np.testing.assert_array_equal(state.packed.cpu().numpy(), want["packed"])
+    np.testing.assert_allclose(state.offset.item(), want["offset"], rtol=1e-6)
+    # the offset is a mean (its last bit depends on the summation order); the codes of the centred absmax agree
+    # wherever no value sits on a rounding boundary
+    assert (state.absmax.cpu().numpy() == want["absmax"]).mean() > 0.999
+    np.testing.assert_array_equal(bits(_nf4.dequantize(state)), quant.dequantize_nf4(_state_np(state)))
+
+
+def test_fp8_dequantize_takes_either_form_of_scale():
+    w = torch.randn(3, 256, 384, device=DEV) * 0.05
+    c1, s1 = _fp8.quantize_stack(w)
+    c2, s2 = _fp8.quantize_blocks(w)
+    assert s2.shape == (3, 2, 3)
+    assert torch.equal(_fp8.dequantize(c1, s1), _fp8.dequantize_stack(c1, s1, torch.bfloat16))
+    assert torch.equal(_fp8.dequantize(c2, s2), _fp8.dequantize_blocks(c2, s2))
+    with pytest.raises(ValueError):
+        _fp8.dequantize(c2, s2[0])
