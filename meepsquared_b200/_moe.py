@@ -17,6 +17,7 @@ reductions and the gather's gradient. The routing is computed once per layer cal
 four grouped products.
 """
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -189,15 +190,20 @@ def _kernel_stack(experts, name):
     """(stack, scale) for the kernels. A bf16 stack as it is. A quantised one goes to the products as a QuantStack,
     dequantised in shared memory between the TMA load and the MMA: FP8 (e4m3) with its `<name>_scale_inv` (one
     scale per expert, applied in the epilogue, or a 128 x 128 grid of blocks) or NF4 (an NF4State in the
-    attribute's place). A quantised stack without whole 64-weight blocks is dequantised for this call instead."""
+    attribute's place). A quantised stack without whole 64-weight blocks is dequantised for this call instead, and
+    so is every quantised stack with MEEP2B_DEQUANT=call (a bf16 copy held for the layer call: more memory, the
+    bf16 products' speed)."""
     from . import _fp8, _nf4
 
     weight = getattr(experts, name)
+    per_call = os.environ.get("MEEP2B_DEQUANT", "fused") == "call"
     if isinstance(weight, _nf4.NF4State):
-        fused = _grouped.QuantStack.from_nf4(weight)
+        fused = None if per_call else _grouped.QuantStack.from_nf4(weight)
         return (fused if fused is not None else _nf4.dequantize(weight)), None
     if weight.dtype == torch.float8_e4m3fn:
         scale = getattr(experts, name + _fp8.STACK_SCALE)
+        if per_call:
+            return _fp8.dequantize(weight.detach(), scale), None
         # the multipliers of a block-scaled stack are prepared once and kept while the stack and scale are unchanged
         cache = experts.__dict__.setdefault("_meep2b_quant_stacks", {})
         key = (weight.data_ptr(), weight._version, scale.data_ptr(), scale._version)
