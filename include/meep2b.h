@@ -85,6 +85,12 @@ int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts
 int meep2b_route_noalloc(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
                          int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* stream);
 
+/* What the routed products need of the permutation without a gathered copy of the rows: per routed row i, the
+ * token it reads, token_rows[i] = perm[i] / top_k (int32), and its routing weight weights_g[i] = weights[perm[i]]
+ * as float32 (weights F32 or BF16; weights or weights_g may be NULL). */
+int meep2b_routed_rows(const int64_t* perm, int64_t assignments, int32_t top_k, const void* weights,
+                       int32_t weights_dtype, int32_t* token_rows, float* weights_g, void* stream);
+
 /* The gather of _moe.py:80-81,87: selected[i] = hidden[perm[i] / top_k] (bf16 rows of hidden_dim), zero for the
  * sentinel rows i >= offsets[experts-1]; weights_g[i] = weights[perm[i]] (weights_dtype F32 or BF16, same type
  * out; both may be NULL). */
@@ -160,6 +166,19 @@ typedef struct meep2b_product {
   int32_t sm_limit;     /* 0: one CTA per SM */
   int32_t block_m;      /* rows per tile: 128, or 256 for the CTA-pair kernel (bf16 stacks); 0 means 128 */
   const float* wscale;  /* NF4, E4M3_BLOCKS: per-group multipliers (experts, cols/64, rows); else NULL */
+  /* The routed layer's fusions (bf16 stacks). x_rows: NULL, or row i of the product's input is row x_rows[i] of the
+   * ldx-strided x, which has x_src_rows rows (the routed rows read from the token-major tensor: no gathered copy;
+   * SWIGLU with b_mn == 0, and DSWIGLU with b_mn == 1). row_scale: NULL, or product row i is scaled by
+   * row_scale[i] (the routing weight: the un-permute's backward folded into the down stack's input gradient), and
+   * so is its stored panel. w_grad (DSWIGLU): NULL, or w_grad[i * w_ld + b] = sum over the columns j of block b of
+   * 96 columns of dh[i, j] * h[i, j], the row's unscaled product dh and h = bf16(bf16(silu(gate)) * up), for rows i
+   * of the experts' ranges (b < ceil(n / 96)): summed over b, the routing weight's gradient <g, y> (the caller sums
+   * in a fixed order, so the result does not depend on the schedule). */
+  const int32_t* x_rows;
+  int64_t x_src_rows;
+  const float* row_scale;
+  float* w_grad;
+  int64_t w_ld;
 } meep2b_product;
 
 int meep2b_grouped_product(const meep2b_product* p, void* stream);
@@ -169,6 +188,15 @@ int meep2b_grouped_product(const meep2b_product* p, void* stream);
  * with row stride ldg, low (rows, 16) bf16, out (experts, n, 16) bf16. */
 int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int64_t ldg, const void* low,
                           const int32_t* offsets, int32_t experts, float scaling, void* out, void* stream);
+
+/* The same reduction over rows gathered from a token-major tensor and weighted: out[e, j, r] = bf16(scaling * sum
+ * over expert e's rows i of g[g_rows[i], j] * bf16(row_scale[i] * low[i, r])) (row_scale NULL: weight 1). Used
+ * for the adapters of the gate/up stack (g = hidden, g_rows = the token of each routed row: no sorted copy) and of
+ * the down stack (g = the layer's upstream gradient, row_scale = the routing weights: the un-permute's backward,
+ * _moe.py:123-126, folded in). rows: the routed rows; g has ldg-strided rows indexed by g_rows. */
+int meep2b_grouped_reduce_rows(const void* g, const int32_t* g_rows, const float* row_scale, int64_t rows,
+                               int64_t n, int64_t ldg, const void* low, const int32_t* offsets, int32_t experts,
+                               float scaling, void* out, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- quantised stacks */
 

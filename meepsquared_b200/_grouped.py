@@ -261,12 +261,15 @@ class QuantStack:
 
 
 def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward=False,
-            tiles=None, epilogue=_lib.EPI_PLAIN, aux=None, out=None):
+            tiles=None, epilogue=_lib.EPI_PLAIN, aux=None, out=None, x_rows=None, row_scale=None, w_grad=None):
     """One launch of the grouped product; returns (out, low). The reference's _launch (_grouped.py:313-345).
 
-    k_contiguous_layout: whether the stack is logically (experts, n, k) for this product.
+    k_contiguous_layout: whether the stack is logically (experts, n, k) for this product. x_rows (int32): the
+    product's row i is row x_rows[i] of x (the routed rows read from the token-major tensor); row_scale (float32):
+    product row i scaled by row_scale[i]; w_grad (dSwiGLU, float32 (rows, ceil(N/96))): <dh_i, h_i> per 96 columns.
     """
-    rows, K = x.shape
+    K = x.shape[1]
+    rows = x_rows.numel() if x_rows is not None else x.shape[0]
     quant = isinstance(weight, QuantStack)
     if quant:  # stored (E, rows, cols) as it is: K-major when the product contracts over its columns
         stack, b_mn = weight.codes, 0 if k_contiguous_layout else 1
@@ -299,7 +302,8 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
         return out, low
     if tiles is None:
         tiles = TileMaps(offsets, rows)
-    block_m = 256 if not quant and _pair_tiles(b_mn, rows, experts, K, adapters is not None) else 128
+    pair_ok = not quant and (x_rows is None or b_mn == 0)
+    block_m = 256 if pair_ok and _pair_tiles(b_mn, rows, experts, K, adapters is not None) else 128
     tmap = tiles.get(block_m)
     panel = up = None
     if adapters is not None:
@@ -309,6 +313,11 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
     p.weight, p.experts, p.n, p.b_mn = stack.data_ptr(), experts, N, b_mn
     p.weight_dtype = weight.kind if quant else _lib.BF16
     p.wscale = weight.mult.data_ptr() if quant and weight.mult is not None else None
+    if x_rows is not None:
+        p.x_rows, p.x_src_rows = x_rows.data_ptr(), x.shape[0]
+    p.row_scale = row_scale.data_ptr() if row_scale is not None else None
+    if w_grad is not None:
+        p.w_grad, p.w_ld = w_grad.data_ptr(), w_grad.stride(0)
     p.scale = scale.data_ptr() if scale is not None else None
     p.panel = panel.data_ptr() if panel is not None else None
     p.up = up.data_ptr() if up is not None else None
@@ -343,18 +352,33 @@ def set_launch_observer(observer):
     _launch_observer = observer
 
 
-def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: float) -> torch.Tensor:
-    """(experts, N, 16) bf16: scaling * sum over each expert's rows of g^T @ low (_grouped.py:362-370)."""
+def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: float, g_rows=None,
+            row_scale=None) -> torch.Tensor:
+    """(experts, N, 16) bf16: scaling * sum over each expert's rows of g^T @ low (_grouped.py:362-370).
+
+    g_rows (int32): row i is row g_rows[i] of g (the routed rows read where they are); row_scale (float32): row i
+    weighted by row_scale[i].
+    """
     experts = offsets.numel()
-    rows, N = g.shape
+    N = g.shape[1]
+    rows = g_rows.numel() if g_rows is not None else g.shape[0]
     if g.stride(1) != 1 or g.stride(0) % 8:
         g = g.contiguous()
     out = torch.empty((experts, N, RANK_MULTIPLE), device=g.device, dtype=torch.bfloat16)
     if rows == 0:
         return out.zero_()
-    _lib.check(_lib.load().meep2b_grouped_reduce(_lib.ptr(g), rows, N, g.stride(0), _lib.ptr(low.contiguous()),
-                                                 _lib.ptr(offsets), experts, float(scaling), _lib.ptr(out),
-                                                 _lib.stream_of(g)), "meep2b_grouped_reduce")
+    lib = _lib.load()
+    if g_rows is None and row_scale is None:
+        _lib.check(lib.meep2b_grouped_reduce(_lib.ptr(g), rows, N, g.stride(0), _lib.ptr(low.contiguous()),
+                                             _lib.ptr(offsets), experts, float(scaling), _lib.ptr(out),
+                                             _lib.stream_of(g)), "meep2b_grouped_reduce")
+    else:
+        if g_rows is None:
+            raise ValueError("a weighted reduction reads its rows through g_rows")
+        _lib.check(lib.meep2b_grouped_reduce_rows(_lib.ptr(g), _lib.ptr(g_rows), _lib.ptr(row_scale), rows, N,
+                                                  g.stride(0), _lib.ptr(low.contiguous()), _lib.ptr(offsets),
+                                                  experts, float(scaling), _lib.ptr(out), _lib.stream_of(g)),
+                   "meep2b_grouped_reduce_rows")
     return out
 
 

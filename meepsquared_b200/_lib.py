@@ -29,6 +29,7 @@ class Product(ctypes.Structure):
         ("offsets", _p), ("tile_expert", _p), ("tile_row", _p), ("tiles", _p), ("max_tiles", _i64),
         ("out", _p), ("ldo", _i64), ("low", _p), ("epilogue", _i32), ("aux", _p), ("sm_limit", _i32),
         ("block_m", _i32), ("wscale", _p),
+        ("x_rows", _p), ("x_src_rows", _i64), ("row_scale", _p), ("w_grad", _p), ("w_ld", _i64),
     ]
 
 
@@ -41,12 +42,14 @@ _SIGNATURES = {
     "meep2b_route_workspace_bytes": (_sz, [_i64, _i32]),
     "meep2b_route": (ctypes.c_int, [_p, _i64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
     "meep2b_route_noalloc": (ctypes.c_int, [_p, _i64, _i32, _p, _p, _p, _p, _p]),
+    "meep2b_routed_rows": (ctypes.c_int, [_p, _i64, _i32, _p, _i32, _p, _p, _p]),
     "meep2b_gather": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _i32, _p, _i32, _p, _p, _p]),
     "meep2b_unpermute": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p]),
     "meep2b_unpermute_backward": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p, _p]),
     "meep2b_tile_map": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _p, _p]),
     "meep2b_grouped_product": (ctypes.c_int, [ctypes.POINTER(Product), _p]),
     "meep2b_grouped_reduce": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _p]),
+    "meep2b_grouped_reduce_rows": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _p]),
     "meep2b_fp8_stack_quantize": (ctypes.c_int, [_p, _i32, _i32, _i64, _p, _p, _p, _p]),
     "meep2b_fp8_stack_dequantize": (ctypes.c_int, [_p, _p, _i32, _i64, _p, _p]),
     "meep2b_fp8_block_dequantize": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i32, _i32, _p, _p]),

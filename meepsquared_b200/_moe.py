@@ -128,15 +128,44 @@ class _Stacks:
     scaling2: float
 
 
+def routed_rows(routing: Routing, top_k_weights):
+    """(token of each routed row (S,) int32, routing weight of each routed row (S,) float32): what the fused
+    products read instead of gathered copies of the rows."""
+    n = routing.perm.numel()
+    dev = routing.perm.device
+    token_rows = torch.empty(n, dtype=torch.int32, device=dev)
+    w32 = torch.empty(n, dtype=torch.float32, device=dev)
+    w = top_k_weights.contiguous() if top_k_weights is not None else None
+    wd = _WEIGHT_DTYPES[w.dtype] if w is not None else _lib.F32
+    _lib.check(_lib.load().meep2b_routed_rows(_lib.ptr(routing.perm), n, routing.top_k, _lib.ptr(w), wd,
+                                              _lib.ptr(token_rows), _lib.ptr(w32 if w is not None else None),
+                                              _lib.stream_of(routing.perm)), "meep2b_routed_rows")
+    return token_rows, w32
+
+
 class _RoutedExperts(torch.autograd.Function):
-    """The whole routed layer: gradients for the hidden states, the routing weights and the four LoRA factors."""
+    """The whole routed layer: gradients for the hidden states, the routing weights and the four LoRA factors.
+
+    MEEP2B_ROUTED_ROWS selects how the layer meets the routing (bf16 stacks without an expert bias; others always
+    take "copy"):
+      fold (default)  the forward gathers the hidden rows into expert order for the gate/up product; the backward
+                      gathers the upstream gradient's rows (unweighted), and the down stack's input-gradient product
+                      applies the routing weights and yields their gradient <dh, h> = <g, y> from its dSwiGLU
+                      epilogue (the un-permute's backward, _moe.py:123-126, folded in: y is not kept); the adapter
+                      reductions read the hidden and upstream-gradient rows where they are;
+      gather          as fold, and the products read their x rows from the token-major tensors themselves (no
+                      gathered copies; slower on B200: the rows arrive by cp.async, not TMA);
+      copy            gathered copies, the un-permute's backward as its own kernel.
+    """
 
     @staticmethod
     def forward(ctx, hidden, top_k_weights, lhs1, rhs1, lhs2, rhs2, top_k_index, st: _Stacks):
         routing = route(top_k_index, top_k_weights, st.num_experts)
-        sel = gather(hidden, routing, top_k_weights)
+        mode = os.environ.get("MEEP2B_ROUTED_ROWS", "fold")
+        if (isinstance(st.gate_up, _grouped.QuantStack) or isinstance(st.down, _grouped.QuantStack)
+                or st.down_bias is not None or mode not in ("fold", "gather")):
+            mode = "copy"
         tiles = routing.tile_map()
-        rows = sel.shape[0]
         t = st.is_transposed
         ad1 = _grouped._Adapters(lhs1.detach(), rhs1.detach(), t) if lhs1 is not None else None
         ad2 = _grouped._Adapters(lhs2.detach(), rhs2.detach(), t) if lhs2 is not None else None
@@ -147,42 +176,86 @@ class _RoutedExperts(torch.autograd.Function):
         if b_mn != 0:
             raise NotImplementedError("SwiGLU is fused for a gate/up stack stored (experts, 2I, hidden), k contiguous")
         two_i = st.gate_up.shape[2] if t else st.gate_up.shape[1]
-        gu = torch.empty((rows, two_i), dtype=torch.bfloat16, device=sel.device)
-        h, low1 = _grouped._launch(sel, st.gate_up, st.gate_up_scale, routing.offsets, not t, ad1, st.scaling1,
-                                   st.gate_up_bias, True, tiles=tiles, epilogue=_lib.EPI_SWIGLU, aux=gu)
+        rows = routing.perm.numel()
+        gu = torch.empty((rows, two_i), dtype=torch.bfloat16, device=hidden.device)
+        token_rows = w32 = None
+        if mode == "copy":
+            x, x_rows, weights_g = gather(hidden, routing, top_k_weights), None, routing.weights_g
+        else:
+            token_rows, w32 = routed_rows(routing, top_k_weights)
+            weights_g = w32
+            if mode == "gather":
+                x, x_rows = hidden, token_rows
+            else:
+                x, x_rows = gather(hidden, routing, None), None
+        h, low1 = _grouped._launch(x, st.gate_up, st.gate_up_scale, routing.offsets, not t, ad1, st.scaling1,
+                                   st.gate_up_bias, True, tiles=tiles, epilogue=_lib.EPI_SWIGLU, aux=gu,
+                                   x_rows=x_rows)
         y, low2 = _grouped._launch(h, st.down, st.down_scale, routing.offsets, not t, ad2, st.scaling2,
                                    st.down_bias, True, tiles=tiles)
-        out = unpermute(y, routing, routing.weights_g)
-        ctx.save_for_backward(sel, gu, h, y, *(v for v in (low1, low2) if v is not None))
-        ctx.routing, ctx.st, ctx.ad1, ctx.ad2 = routing, st, ad1, ad2
+        out = unpermute(y, routing, weights_g)
+        kept = (x, gu, h, y) if mode == "copy" else (hidden, gu, h, token_rows, w32)
+        ctx.save_for_backward(*kept, *(v for v in (low1, low2) if v is not None))
+        ctx.routing, ctx.st, ctx.ad1, ctx.ad2, ctx.mode = routing, st, ad1, ad2, mode
         ctx.has_low = (low1 is not None, low2 is not None)
         ctx.weights_dtype = top_k_weights.dtype
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        sel, gu, h, y, *lows = ctx.saved_tensors
+        routing, st, ad1, ad2, mode = ctx.routing, ctx.st, ctx.ad1, ctx.ad2, ctx.mode
+        saved = list(ctx.saved_tensors)
+        if mode == "copy":
+            sel, gu, h, y = saved[:4]
+            lows = saved[4:]
+        else:
+            hidden, gu, h, token_rows, w32 = saved[:5]
+            lows = saved[5:]
         low1 = lows.pop(0) if ctx.has_low[0] else None
         low2 = lows.pop(0) if ctx.has_low[1] else None
-        routing, st, ad1, ad2 = ctx.routing, ctx.st, ctx.ad1, ctx.ad2
         tiles = routing.tile_map()
         t = st.is_transposed
-        grad_y, grad_w = unpermute_backward(grad_out, y, routing)
-        # down projection: dh = grad_y @ W_down (read the other way), SwiGLU's backward in the epilogue -> d(gate, up)
-        dgu, low2b = _grouped._launch(grad_y, st.down, st.down_scale, routing.offsets, t, ad2, st.scaling2, None,
-                                      True, backward=True, tiles=tiles, epilogue=_lib.EPI_DSWIGLU, aux=gu)
+        grad_out = grad_out.contiguous()
+        if grad_out.dtype != torch.bfloat16:
+            grad_out = grad_out.to(torch.bfloat16)
+        if mode == "copy":
+            grad_y, grad_w = unpermute_backward(grad_out, y, routing)
+            dgu, low2b = _grouped._launch(grad_y, st.down, st.down_scale, routing.offsets, t, ad2, st.scaling2, None,
+                                          True, backward=True, tiles=tiles, epilogue=_lib.EPI_DSWIGLU, aux=gu)
+        else:
+            # the down stack's input gradient over the upstream gradient's rows, each weighted by its routing weight,
+            # SwiGLU's backward in the epilogue, and <dh, h> per row and 96 columns for the routing weights' gradient
+            inter = gu.shape[1] // 2
+            parts = torch.zeros((routing.perm.numel(), -(-inter // 96)), dtype=torch.float32, device=grad_out.device)
+            if mode == "gather":
+                g, g_rows = grad_out, token_rows
+            else:
+                g, g_rows = gather(grad_out, routing, None), None
+            dgu, low2b = _grouped._launch(g, st.down, st.down_scale, routing.offsets, t, ad2, st.scaling2, None,
+                                          True, backward=True, tiles=tiles, epilogue=_lib.EPI_DSWIGLU, aux=gu,
+                                          x_rows=g_rows, row_scale=w32, w_grad=parts)
+            grad_w = torch.empty(routing.perm.numel(), dtype=torch.float32, device=grad_out.device)
+            grad_w[routing.perm] = parts.sum(dim=1)  # a fixed order: the same bits on every run
         dsel, low1b = _grouped._launch(dgu, st.gate_up, st.gate_up_scale, routing.offsets, t, ad1, st.scaling1, None,
                                        True, backward=True, tiles=tiles)
         grads = [None, None, None, None]
         if ad1 is not None:
-            g_first = _grouped._reduce(sel, low1b, routing.offsets, st.scaling1)
+            if mode == "copy":
+                g_first = _grouped._reduce(sel, low1b, routing.offsets, st.scaling1)
+            else:
+                g_first = _grouped._reduce(hidden, low1b, routing.offsets, st.scaling1, g_rows=token_rows)
             g_second = _grouped._reduce(dgu, low1, routing.offsets, st.scaling1)
             grads[0], grads[1] = _grouped._to_lhs_rhs(g_first, g_second, ad1)
         if ad2 is not None:
             g_first = _grouped._reduce(h, low2b, routing.offsets, st.scaling2)
-            g_second = _grouped._reduce(grad_y, low2, routing.offsets, st.scaling2)
+            if mode == "copy":
+                g_second = _grouped._reduce(grad_y, low2, routing.offsets, st.scaling2)
+            else:
+                g_second = _grouped._reduce(grad_out, low2, routing.offsets, st.scaling2, g_rows=token_rows,
+                                            row_scale=w32)
             grads[2], grads[3] = _grouped._to_lhs_rhs(g_first, g_second, ad2)
         grad_hidden = unpermute(dsel, routing, None)
+        grad_w = grad_w.view(routing.num_tokens, routing.top_k)
         return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None)
 
 

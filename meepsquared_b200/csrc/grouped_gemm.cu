@@ -68,6 +68,15 @@ struct Params {
   __nv_bfloat16* low;
   __nv_bfloat16* aux;
   bool v8;  // out, aux and low rows 32-byte aligned: whole-sector stores
+  // gathered x (GATHER kernels): tile row i reads row a_rows[i] of a_src (row stride lda)
+  const int32_t* a_rows;
+  const __nv_bfloat16* a_src;
+  int64_t lda;
+  // dSwiGLU with the un-permute's backward folded in: the product is scaled by row_scale[row] (the routing weight)
+  // and, when w_grad is set, w_grad[row * w_ld + block] = <unscaled product, h> over each 96-column block
+  const float* row_scale;
+  float* w_grad;
+  int64_t w_ld;
 };
 
 // silu(g) = g / (1 + exp(-g)) with the fast exponential and division intrinsics; the result is rounded to bf16.
@@ -200,6 +209,9 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
   const int ab = it & 1;
   const uint32_t aph = (it >> 1) & 1;
   const float sc = p.scale != nullptr ? p.scale[e] : 1.0f;
+  // the row's weight (the routing weight, when the un-permute's backward is folded in): scales the product row
+  // and its stored rank panel; the adapter MMA's planes stay unscaled (the whole row is scaled at the end)
+  const float rw = p.row_scale != nullptr && valid ? p.row_scale[row] : 1.0f;
   const uint32_t d = tmem_base + lane_base + ab * ACC_STRIDE;
   const int64_t orow = static_cast<int64_t>(row);
   const bool v8 = p.v8;
@@ -219,7 +231,7 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
     if (p.low != nullptr && nb == 0 && valid) {
       uint32_t lw[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) lw[i] = pack_bf16x2(lv[2 * i], lv[2 * i + 1]);
+      for (int i = 0; i < 8; ++i) lw[i] = pack_bf16x2(lv[2 * i] * rw, lv[2 * i + 1] * rw);
       put16(p.low + orow * RP, lw, v8);
     }
     // the A operand of the last MMAs: a = s * low / scale_e (float32) split into two bf16 planes, hi = bf16(a)
@@ -273,8 +285,8 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int k = 16 * c + 2 * j;
-          float g0 = __uint_as_float(g[k]) * sc, g1 = __uint_as_float(g[k + 1]) * sc;
-          float u0 = __uint_as_float(uu[k]) * sc, u1 = __uint_as_float(uu[k + 1]) * sc;
+          float g0 = __uint_as_float(g[k]) * sc * rw, g1 = __uint_as_float(g[k + 1]) * sc * rw;
+          float u0 = __uint_as_float(uu[k]) * sc * rw, u1 = __uint_as_float(uu[k + 1]) * sc * rw;
           if (bias_g != nullptr && 2 * j + 1 < cnt) {
             g0 += __bfloat162float(bias_g[k]);
             g1 += __bfloat162float(bias_g[k + 1]);
@@ -316,7 +328,7 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int k = 16 * c + 2 * j;
-          float a = __uint_as_float(v[k]) * sc, b = __uint_as_float(v[k + 1]) * sc;
+          float a = __uint_as_float(v[k]) * sc * rw, b = __uint_as_float(v[k + 1]) * sc * rw;
           if (bias != nullptr && 2 * j + 1 < cnt) {
             a += __bfloat162float(bias[k]);
             b += __bfloat162float(bias[k + 1]);
@@ -358,6 +370,7 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
         }
       }
     };
+    float wpart = 0.0f;  // <unscaled dh, h> over this thread's columns: the routing weight's gradient
     if (valid && cols > 0) load_pre(0, 0);
     if (!mbar_wait(bar_tfull_ab, aph)) return false;
     tc_fence_after();
@@ -384,9 +397,11 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
           for (int hlf = 0; hlf < 2; ++hlf) {
             const float gb = hlf ? bf16_hi(gw[b][j]) : bf16_lo(gw[b][j]);
             const float ub = hlf ? bf16_hi(uw[b][j]) : bf16_lo(uw[b][j]);
-            const float dh = bf16_round(__uint_as_float(acc[b][2 * j + hlf]) * sc);
+            const float dh_u = __uint_as_float(acc[b][2 * j + hlf]) * sc;
+            const float dh = bf16_round(dh_u * rw);
             const float sig = sigmoid_f(gb);  // one exponential and one reciprocal per element
             const float act = bf16_round(gb * sig);
+            if (p.w_grad != nullptr && 2 * j + hlf < cnt) wpart += dh_u * bf16_round(act * ub);  // h = bf16(act u)
             const float dact = bf16_round(dh * ub);
             duo[hlf] = dh * act;
             dgo[hlf] = dact * sig * (1.0f + gb * (1.0f - sig));
@@ -399,13 +414,107 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
       }
       if (more) tmem_wait_regs16(acc[b ^ 1]);
     }
+    if (p.w_grad != nullptr && valid && cols > 0) p.w_grad[orow * p.w_ld + n0 / 96] = wpart;
   }
   tc_fence_before();
   arrive_on<PAIR>(bar_tempty_ab);
   return true;
 }
 
-template <bool B_MN, bool LORA, int EPI>
+// The x tile of a gathered product (x row i of the tile = row src of a token-major tensor: the routed rows read
+// where they are, without an expert-sorted copy), copied by two warps, warp gw taking rows 64 gw .. 64 gw + 63:
+// 64 columns from k0 as 16-byte cp.async copies into the 128-byte-swizzled layout a TMA load of the tile gives
+// (columns past K read zero). Eight lanes cover one row's 128 bytes, so each instruction moves four whole rows
+// (coalesced line requests): lane l copies chunk l % 8 of rows 64 gw + 4 i + l / 8, i = 0..15, sources in src[i].
+constexpr int GATHER_WARP0 = 2;  // warps 2 and 3 (idle otherwise)
+__device__ __forceinline__ void gather_x_stage(uint32_t a_dst, const __nv_bfloat16* src_base, int64_t ld, int K,
+                                               int k0, const int (&src)[16], int gw, int lane) {
+  const int c = lane & 7, rg = lane >> 3;
+  const int k = k0 + 8 * c;
+  const bool ok = k < K;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int r = 64 * gw + 4 * i + rg;
+    const __nv_bfloat16* row = src_base + static_cast<int64_t>(src[i]) * ld;
+    const uint32_t dst = a_dst + r * 128 + ((static_cast<uint32_t>(c) ^ static_cast<uint32_t>(r & 7)) << 4);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(ok ? row + k : src_base),
+                 "r"(ok ? 16 : 0)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// The source rows of the tile rows this lane copies; rows past the product's end read row 0 (the epilogue drops
+// them).
+__device__ __forceinline__ void gather_rows_of_tile(const int32_t* a_rows, int rows, int row0, int gw, int lane,
+                                                    int (&src)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int r = row0 + 64 * gw + 4 * i + (lane >> 3);
+    src[i] = r < rows ? __ldg(a_rows + r) : 0;
+  }
+}
+
+// After this lane's copies of the oldest stage in flight (all but the PENDING newest groups) have landed: make the
+// warp's writes visible to the tensor cores (async proxy) and arrive once, for the warp, on that stage's barrier.
+template <int PENDING>
+__device__ __forceinline__ void gather_signal(uint32_t bar, int lane, bool to_leader) {
+  asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory");
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (to_leader) {
+      mbar_arrive_remote(bar, 0);
+    } else {
+      mbar_arrive(bar);
+    }
+  }
+}
+
+// Warps 2-3 of a gathered product: the x rows of every k-step, in the producer's stage order, into the x ring at
+// a_ring (stage s at a_ring + s * A_BYTES). The stage's full barrier (the pair leader's, to_leader) gets one arrival
+// per warp once the warp's copies have landed; a ring slot is refilled after its empty barrier completes.
+template <int STAGES>
+__device__ __forceinline__ void gather_role(const Params& p, int first_unit, int unit_stride, int total, int row_shift,
+                                            uint32_t a_ring, uint32_t bar0, int gw, int lane, bool to_leader) {
+  int stage = 0, sig_stage = 0, in_flight = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int u = first_unit; u < total && ok; u += unit_stride) {
+    const int t = u / p.nblocks;
+    int src[16];
+    gather_rows_of_tile(p.a_rows, p.rows, p.tile_row[t] + row_shift, gw, lane, src);
+    for (int kb = 0; kb < p.kblocks; ++kb) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar0 + 8u * (STAGES + stage), phase ^ 1));
+      if (!ok) break;
+      gather_x_stage(a_ring + stage * A_BYTES, p.a_src, p.lda, p.K, kb * BK, src, gw, lane);
+      if (++in_flight > STAGES - 1) {
+        gather_signal<STAGES - 1>(bar0 + 8u * sig_stage, lane, to_leader);
+        sig_stage = sig_stage + 1 == STAGES ? 0 : sig_stage + 1;
+        --in_flight;
+      }
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+  if (in_flight > 0) {  // the last stages (also on the way out of a failed run: the copies land before exit)
+    gather_signal<0>(bar0 + 8u * sig_stage, lane, to_leader);
+    for (int i = 1; i < in_flight; ++i) {
+      sig_stage = sig_stage + 1 == STAGES ? 0 : sig_stage + 1;
+      if (lane == 0) {
+        if (to_leader) {
+          mbar_arrive_remote(bar0 + 8u * sig_stage, 0);
+        } else {
+          mbar_arrive(bar0 + 8u * sig_stage);
+        }
+      }
+    }
+  }
+}
+
+template <bool B_MN, bool LORA, int EPI, bool GATHER = false>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_u,
@@ -431,7 +540,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full(s), 1);
+      mbar_init(bar_full(s), GATHER ? 3 : 1);  // gathered: the stack's TMA bytes, then the two gather warps
       mbar_init(bar_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -458,15 +567,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------------------ TMA producer
+    // (gathered x: warps 2-3 copy the x rows; this thread loads the stack and the adapters)
     if (lane == 0) {
-      tma_prefetch_desc(&tm_x);
+      const bool lead = true;
+      if (!GATHER) tma_prefetch_desc(&tm_x);
       tma_prefetch_desc(&tm_w);
       if (LORA) {
         tma_prefetch_desc(&tm_p);
         tma_prefetch_desc(&tm_u);
       }
       constexpr uint32_t B_TX = 64 * BN * 2 + (LORA ? (B_MN ? 64 * 64 * 2 : RP * 64 * 2) : 0);
-      constexpr uint32_t STAGE_TX = A_BYTES + B_TX;
+      constexpr uint32_t STAGE_TX = (GATHER ? 0 : A_BYTES) + B_TX;
+      auto wait = [&](uint32_t bar, uint32_t parity) -> bool { return mbar_wait(bar, parity); };
       int stage = 0;
       uint32_t phase = 0;
       uint32_t last_parity[STAGES];
@@ -478,19 +590,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       // waits for the previous unit's adapter MMAs while the ring could be refilled.
       int pu = -1, pu_nb = 0, pu_e = 0;
       auto load_u = [&]() -> bool {
-        if (!mbar_wait(bar_uempty, (pu & 1) ^ 1)) return false;
+        if (!wait(bar_uempty, (pu & 1) ^ 1)) return false;
         const uint32_t dst = sbase + P::OFF_U;
-        mbar_arrive_expect_tx(bar_ufull, U_BYTES);
-        if (!B_MN) {
-          if (EPI == MEEP2B_EPI_SWIGLU) {
-            tma_load_3d(dst, &tm_u, bar_ufull, 0, pu_nb * 96, pu_e);
-            tma_load_3d(dst + 96 * RP * 2, &tm_u, bar_ufull, 0, p.inter + pu_nb * 96, pu_e);
+        if (lead) {
+          mbar_arrive_expect_tx(bar_ufull, U_BYTES);
+          if (!B_MN) {
+            if (EPI == MEEP2B_EPI_SWIGLU) {
+              tma_load_3d(dst, &tm_u, bar_ufull, 0, pu_nb * 96, pu_e);
+              tma_load_3d(dst + 96 * RP * 2, &tm_u, bar_ufull, 0, p.inter + pu_nb * 96, pu_e);
+            } else {
+              tma_load_3d(dst, &tm_u, bar_ufull, 0, pu_nb * BN, pu_e);
+            }
           } else {
-            tma_load_3d(dst, &tm_u, bar_ufull, 0, pu_nb * BN, pu_e);
-          }
-        } else {
 #pragma unroll
-          for (int j = 0; j < 3; ++j) tma_load_3d(dst + j * 2048, &tm_u, bar_ufull, pu_nb * BN + 64 * j, 0, pu_e);
+            for (int j = 0; j < 3; ++j) tma_load_3d(dst + j * 2048, &tm_u, bar_ufull, pu_nb * BN + 64 * j, 0, pu_e);
+          }
         }
         pu = -1;
         return true;
@@ -499,24 +613,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int t = u / p.nblocks, nb = u - t * p.nblocks;
         const int e = p.tile_expert[t], row0 = p.tile_row[t];
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(bar_empty(stage), phase ^ 1)) { ok = false; break; }
+          if (!wait(bar_empty(stage), phase ^ 1)) { ok = false; break; }
           const uint32_t fb = bar_full(stage);
           const uint32_t a_dst = sbase + P::OFF_A + stage * A_BYTES;
           const uint32_t b_dst = sbase + P::OFF_B + stage * P::B_BYTES;
-          mbar_arrive_expect_tx(fb, STAGE_TX);
-          tma_load_2d(a_dst, &tm_x, fb, kb * BK, row0);
-          if (!B_MN) {
-            if (EPI == MEEP2B_EPI_SWIGLU) {
-              tma_load_3d(b_dst, &tm_w, fb, kb * BK, nb * 96, e);
-              tma_load_3d(b_dst + 96 * 128, &tm_w, fb, kb * BK, p.inter + nb * 96, e);
+          if (lead) {
+            mbar_arrive_expect_tx(fb, STAGE_TX);
+            if (!GATHER) tma_load_2d(a_dst, &tm_x, fb, kb * BK, row0);
+            if (!B_MN) {
+              if (EPI == MEEP2B_EPI_SWIGLU) {
+                tma_load_3d(b_dst, &tm_w, fb, kb * BK, nb * 96, e);
+                tma_load_3d(b_dst + 96 * 128, &tm_w, fb, kb * BK, p.inter + nb * 96, e);
+              } else {
+                tma_load_3d(b_dst, &tm_w, fb, kb * BK, nb * BN, e);
+              }
+              if (LORA) tma_load_3d(b_dst + BN * 128, &tm_p, fb, kb * BK, 0, e);
             } else {
-              tma_load_3d(b_dst, &tm_w, fb, kb * BK, nb * BN, e);
-            }
-            if (LORA) tma_load_3d(b_dst + BN * 128, &tm_p, fb, kb * BK, 0, e);
-          } else {
 #pragma unroll
-            for (int j = 0; j < 3; ++j) tma_load_3d(b_dst + j * 8192, &tm_w, fb, nb * BN + 64 * j, kb * BK, e);
-            if (LORA) tma_load_3d(b_dst + 3 * 8192, &tm_p, fb, 0, kb * BK, e);
+              for (int j = 0; j < 3; ++j) tma_load_3d(b_dst + j * 8192, &tm_w, fb, nb * BN + 64 * j, kb * BK, e);
+              if (LORA) tma_load_3d(b_dst + 3 * 8192, &tm_p, fb, 0, kb * BK, e);
+            }
           }
           issued[stage] = true;
           last_parity[stage] = phase;
@@ -533,12 +649,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (ok && LORA && pu >= 0) ok = load_u();
-      if (!ok) {
+      if (!ok && lead) {
         // a partner is gone: let this thread's copies in flight land before the CTA's shared memory goes away
         for (int s = 0; s < STAGES; ++s)
           if (issued[s]) mbar_wait_drain(bar_full(s), last_parity[s]);
       }
     }
+  } else if (GATHER && (warp == GATHER_WARP0 || warp == GATHER_WARP0 + 1)) {
+    // ------------------------------------------------------------------------------------------ x-row gather
+    gather_role<STAGES>(p, blockIdx.x, gridDim.x, total, 0, sbase + P::OFF_A, bar0, warp - GATHER_WARP0, lane, false);
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -681,7 +800,7 @@ struct PairMaps {
   CUtensorMap u_mn;  // MN-major up factor (n, 16, E) box 32 x 16, 64-byte swizzle
 };
 
-template <bool B_MN, bool LORA, int EPI>
+template <bool B_MN, bool LORA, int EPI, bool GATHER = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ PairMaps m, const Params p) {
   using PP = PairPlan<B_MN>;
@@ -706,7 +825,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PP::STAGES; ++s) {
-      mbar_init(bar_full(s), 1);
+      mbar_init(bar_full(s), GATHER ? 5 : 1);  // gathered: the TMA bytes, then the two gather warps of each CTA
       mbar_init(bar_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -733,11 +852,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      tma_prefetch_desc(&m.x);
+      const bool lead = true;
+      if (!GATHER) tma_prefetch_desc(&m.x);
       // K-major: with the panel the 208 B rows split 104 / 104 (the second CTA's last 16 are the panel), without it
       // 96 / 96. MN-major: 96 stack columns per CTA, plus 8 panel columns (one 16-column atom) with the adapters.
       constexpr uint32_t CTA_TX =
-          B_MN ? A_BYTES + 3 * 64 * 64 + (LORA ? 64 * 64 : 0) : A_BYTES + (LORA ? PAIR_B_ROWS : BN / 2) * 128;
+          (GATHER ? 0 : A_BYTES) + (B_MN ? 3 * 64 * 64 + (LORA ? 64 * 64 : 0) : (LORA ? PAIR_B_ROWS : BN / 2) * 128);
+      auto wait = [&](uint32_t bar, uint32_t parity) -> bool { return mbar_wait(bar, parity); };
       int stage = 0;
       uint32_t phase = 0;
       uint32_t last_parity[PP::STAGES];
@@ -747,16 +868,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int it = 0;
       int pu = -1, pu_nb = 0, pu_e = 0;  // as in the one-CTA kernel: a unit's up factor goes out one k-step later
       auto load_u = [&]() -> bool {
-        if (!mbar_wait(bar_uempty, (pu & 1) ^ 1)) return false;
-        if (rank == 0) mbar_arrive_expect_tx(bar_ufull, 2 * PP::U_TX);
-        const int urow = EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? pu_nb * 96 : p.inter + pu_nb * 96)
-                                                  : pu_nb * BN + 96 * static_cast<int>(rank);
-        if (B_MN) {  // 96 columns and 8 more: the fourth atom lands on panel columns of the accumulator, read already
+        if (!wait(bar_uempty, (pu & 1) ^ 1)) return false;
+        if (lead) {
+          if (rank == 0) mbar_arrive_expect_tx(bar_ufull, 2 * PP::U_TX);
+          const int urow = EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? pu_nb * 96 : p.inter + pu_nb * 96)
+                                                    : pu_nb * BN + 96 * static_cast<int>(rank);
+          if (B_MN) {  // 96 columns and 8 more: the fourth atom lands on panel columns of the accumulator, read already
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tma_load_3d_pair(sbase + PP::OFF_U + j * 1024, &m.u_mn, map_to_rank(bar_ufull, 0), urow + 32 * j, 0, pu_e);
-        } else {
-          tma_load_3d_pair(sbase + PP::OFF_U, &m.u96, map_to_rank(bar_ufull, 0), 0, urow, pu_e);
+            for (int j = 0; j < 4; ++j)
+              tma_load_3d_pair(sbase + PP::OFF_U + j * 1024, &m.u_mn, map_to_rank(bar_ufull, 0), urow + 32 * j, 0, pu_e);
+          } else {
+            tma_load_3d_pair(sbase + PP::OFF_U, &m.u96, map_to_rank(bar_ufull, 0), 0, urow, pu_e);
+          }
         }
         pu = -1;
         return true;
@@ -765,39 +888,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const int t = u / p.nblocks, nb = u - t * p.nblocks;
         const int e = p.tile_expert[t], row0 = p.tile_row[t] + 128 * static_cast<int>(rank);
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(bar_empty(stage), phase ^ 1)) { ok = false; break; }
+          if (!wait(bar_empty(stage), phase ^ 1)) { ok = false; break; }
           const uint32_t fb = bar_full(stage);
           const uint32_t fb_lead = map_to_rank(fb, 0);
           const uint32_t a_dst = sbase + stage * A_BYTES;
           const uint32_t b_dst = sbase + PP::OFF_B + stage * PP::B_BYTES;
-          if (rank == 0) mbar_arrive_expect_tx(fb, 2 * CTA_TX);
-          tma_load_2d_pair(a_dst, &m.x, fb_lead, kb * BK, row0);
           const int k0 = kb * BK;
-          if (B_MN) {
-            const int c0 = nb * BN + 96 * static_cast<int>(rank);
+          if (lead) {
+            if (rank == 0) mbar_arrive_expect_tx(fb, 2 * CTA_TX);
+            if (!GATHER) tma_load_2d_pair(a_dst, &m.x, fb_lead, kb * BK, row0);
+            if (B_MN) {
+              const int c0 = nb * BN + 96 * static_cast<int>(rank);
 #pragma unroll
-            for (int j = 0; j < 3; ++j) tma_load_3d_pair(b_dst + j * 4096, &m.w_mn, fb_lead, c0 + 32 * j, k0, e);
-            if (LORA) tma_load_3d_pair(b_dst + PP::PANEL_OFF, &m.p_mn, fb_lead, 8 * static_cast<int>(rank), k0, e);
-          } else if (EPI == MEEP2B_EPI_SWIGLU) {
-            const int g0 = nb * 96;
-            if (!LORA) {  // gate rows in the first CTA, up rows in the second
-              tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, rank == 0 ? g0 : p.inter + g0, e);
-            } else if (rank == 0) {
-              tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, g0, e);                       // gate 0..95
-              tma_load_3d_pair(b_dst + 96 * 128, &m.w8, fb_lead, k0, p.inter + g0, e);   // up 0..7
+              for (int j = 0; j < 3; ++j) tma_load_3d_pair(b_dst + j * 4096, &m.w_mn, fb_lead, c0 + 32 * j, k0, e);
+              if (LORA) tma_load_3d_pair(b_dst + PP::PANEL_OFF, &m.p_mn, fb_lead, 8 * static_cast<int>(rank), k0, e);
+            } else if (EPI == MEEP2B_EPI_SWIGLU) {
+              const int g0 = nb * 96;
+              if (!LORA) {  // gate rows in the first CTA, up rows in the second
+                tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, rank == 0 ? g0 : p.inter + g0, e);
+              } else if (rank == 0) {
+                tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, g0, e);                       // gate 0..95
+                tma_load_3d_pair(b_dst + 96 * 128, &m.w8, fb_lead, k0, p.inter + g0, e);   // up 0..7
+              } else {
+                tma_load_3d_pair(b_dst, &m.w88, fb_lead, k0, p.inter + g0 + 8, e);         // up 8..95
+                tma_load_3d_pair(b_dst + 88 * 128, &m.p16, fb_lead, k0, 0, e);             // the rank panel
+              }
             } else {
-              tma_load_3d_pair(b_dst, &m.w88, fb_lead, k0, p.inter + g0 + 8, e);         // up 8..95
-              tma_load_3d_pair(b_dst + 88 * 128, &m.p16, fb_lead, k0, 0, e);             // the rank panel
-            }
-          } else {
-            const int n0 = nb * BN;
-            if (!LORA) {
-              tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, n0 + 96 * static_cast<int>(rank), e);
-            } else if (rank == 0) {
-              tma_load_3d_pair(b_dst, &m.w104, fb_lead, k0, n0, e);
-            } else {
-              tma_load_3d_pair(b_dst, &m.w88, fb_lead, k0, n0 + 104, e);
-              tma_load_3d_pair(b_dst + 88 * 128, &m.p16, fb_lead, k0, 0, e);             // the rank panel
+              const int n0 = nb * BN;
+              if (!LORA) {
+                tma_load_3d_pair(b_dst, &m.w96, fb_lead, k0, n0 + 96 * static_cast<int>(rank), e);
+              } else if (rank == 0) {
+                tma_load_3d_pair(b_dst, &m.w104, fb_lead, k0, n0, e);
+              } else {
+                tma_load_3d_pair(b_dst, &m.w88, fb_lead, k0, n0 + 104, e);
+                tma_load_3d_pair(b_dst + 88 * 128, &m.p16, fb_lead, k0, 0, e);             // the rank panel
+              }
             }
           }
           issued[stage] = true;
@@ -815,11 +940,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
       }
       if (ok && LORA && pu >= 0) ok = load_u();
-      if (!ok) {
+      if (!ok && lead) {
         for (int s = 0; s < PP::STAGES; ++s)
           if (issued[s] && rank == 0) mbar_wait_drain(bar_full(s), last_parity[s]);
       }
     }
+  } else if (GATHER && (warp == GATHER_WARP0 || warp == GATHER_WARP0 + 1)) {
+    // ------------------------------------------------------------------------------------------ x-row gather
+    gather_role<PP::STAGES>(p, pair_id, pairs, total, 128 * static_cast<int>(rank), sbase, bar0,
+                            warp - GATHER_WARP0, lane, rank != 0);
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && rank == 0) {
@@ -858,7 +987,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + ab * ACC_STRIDE;
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(bar_full(stage), phase)) { ok = false; break; }
+          // gathered x: the second CTA's rows are generic-proxy writes released at cluster scope
+          if (!(GATHER ? mbar_wait_cluster(bar_full(stage), phase) : mbar_wait(bar_full(stage), phase))) {
+            ok = false;
+            break;
+          }
           if (MEEP2B_KSTEP_FENCE) tc_fence_after();
           const uint32_t a_addr = sbase + stage * A_BYTES;
           const uint32_t b_addr = sbase + PP::OFF_B + stage * PP::B_BYTES;
@@ -914,9 +1047,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   }
 }
 
-template <bool B_MN, bool LORA, int EPI>
+template <bool B_MN, bool LORA, int EPI, bool GATHER = false>
 static int launch_pair(const PairMaps& maps, const Params& prm, int grid, cudaStream_t s) {
-  auto kern = grouped_gemm_pair_kernel<B_MN, LORA, EPI>;
+  auto kern = grouped_gemm_pair_kernel<B_MN, LORA, EPI, GATHER>;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairPlan<B_MN>::SMEM_BYTES) != cudaSuccess) {
@@ -929,10 +1062,10 @@ static int launch_pair(const PairMaps& maps, const Params& prm, int grid, cudaSt
   return launch_status();
 }
 
-template <bool B_MN, bool LORA, int EPI>
+template <bool B_MN, bool LORA, int EPI, bool GATHER = false>
 static int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tu,
                   const Params& prm, int grid, cudaStream_t s) {
-  auto kern = grouped_gemm_kernel<B_MN, LORA, EPI>;
+  auto kern = grouped_gemm_kernel<B_MN, LORA, EPI, GATHER>;
   static bool configured = false;  // per instantiation; attributes are per device but idempotent
   if (!configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<B_MN>::SMEM_BYTES) != cudaSuccess) {
@@ -971,14 +1104,20 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   if (!aligned16(a->x) || !aligned16(a->weight) || !aligned16(a->out) || (a->low && !aligned16(a->low)) ||
       (a->aux && !aligned16(a->aux)) || (lora && (!aligned16(a->panel) || !aligned16(a->up))))
     return MEEP2B_ERR_ALIGN;
+  const bool gather = a->x_rows != nullptr;
+  if (gather && (quantised || a->x_src_rows < 1 ||
+                 !((epi == MEEP2B_EPI_SWIGLU && !a->b_mn) || (epi == MEEP2B_EPI_DSWIGLU && a->b_mn))))
+    return MEEP2B_ERR_UNSUPPORTED;
+  if (a->w_grad != nullptr && (epi != MEEP2B_EPI_DSWIGLU || a->w_ld < (a->n + 95) / 96)) return MEEP2B_ERR_SHAPE;
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
   if (a->rows == 0) return MEEP2B_OK;
 
   const uint64_t K = a->k, N = a->n, E = a->experts, rows = a->rows;
+  const uint64_t x_rows_in_map = gather ? static_cast<uint64_t>(a->x_src_rows) : rows;
   CUtensorMap tx, tw, tp, tu;
   {
-    const uint64_t dims[2] = {K, rows};
+    const uint64_t dims[2] = {K, x_rows_in_map};
     const uint64_t strides[1] = {static_cast<uint64_t>(a->ldx) * 2};
     const uint32_t box[2] = {64, 128};
     MEEP2B_TRY(encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->x, dims, strides, box,
@@ -1049,6 +1188,12 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   prm.low = static_cast<__nv_bfloat16*>(a->low);
   prm.aux = static_cast<__nv_bfloat16*>(a->aux);
   auto aligned32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 31u) == 0; };
+  prm.a_rows = a->x_rows;
+  prm.a_src = static_cast<const __nv_bfloat16*>(a->x);
+  prm.lda = a->ldx;
+  prm.row_scale = a->row_scale;
+  prm.w_grad = a->w_grad;
+  prm.w_ld = a->w_ld;
   prm.v8 = aligned32(a->out) && (a->aux == nullptr || aligned32(a->aux)) && (a->low == nullptr || aligned32(a->low)) &&
            a->ldo % 16 == 0 && prm.ld_aux % 16 == 0;
 
@@ -1105,6 +1250,11 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
     const int pairs_max = sms / 2;
     const int64_t pairs = units < pairs_max ? (units > 0 ? units : 1) : pairs_max;
     const int grid = static_cast<int>(2 * pairs);
+    if (gather) {  // pairs gather the x rows of the K-major SwiGLU product only
+      if (a->b_mn || epi != MEEP2B_EPI_SWIGLU) return MEEP2B_ERR_UNSUPPORTED;
+      return lora ? launch_pair<false, true, 1, true>(maps, prm, grid, s)
+                  : launch_pair<false, false, 1, true>(maps, prm, grid, s);
+    }
     if (a->b_mn) {
       if (epi == MEEP2B_EPI_PLAIN)
         return lora ? launch_pair<true, true, 0>(maps, prm, grid, s) : launch_pair<true, false, 0>(maps, prm, grid, s);
@@ -1123,6 +1273,13 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   if (quantised) return launch_quantized(a, tx, tp, tu, prm, grid, s);
 
   const bool mn = a->b_mn != 0;
+  if (gather) {
+    if (epi == MEEP2B_EPI_SWIGLU)
+      return lora ? launch<false, true, 1, true>(tx, tw, tp, tu, prm, grid, s)
+                  : launch<false, false, 1, true>(tx, tw, tp, tu, prm, grid, s);
+    return lora ? launch<true, true, 2, true>(tx, tw, tp, tu, prm, grid, s)
+                : launch<true, false, 2, true>(tx, tw, tp, tu, prm, grid, s);
+  }
   switch (epi) {
     case MEEP2B_EPI_PLAIN:
       if (mn) return lora ? launch<true, true, 0>(tx, tw, tp, tu, prm, grid, s) : launch<true, false, 0>(tx, tw, tp, tu, prm, grid, s);

@@ -8,6 +8,9 @@
 // ring of 64-row chunks.
 //
 // Grid: (ceil(n / 128), experts); 8 warps, warp w owns columns [16 w, 16 w + 16) of the CTA's 128.
+// The gathered form reads row i of g as g[g_rows[i]] (the routed rows straight from the token-major tensor, no
+// expert-sorted copy) and weights it by row_scale[i]; the weight is applied to the rank panel's row
+// (bf16(row_scale * low), 16 values) rather than to the n values of g.
 #include "common.cuh"
 #include "host.hpp"
 
@@ -46,7 +49,9 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bfloat16* __restrict__ g, int64_t n,
                                                                  int64_t ldg, const __nv_bfloat16* __restrict__ low,
                                                                  const int32_t* __restrict__ offsets, float scaling,
-                                                                 __nv_bfloat16* __restrict__ out) {
+                                                                 __nv_bfloat16* __restrict__ out,
+                                                                 const int32_t* __restrict__ g_rows,
+                                                                 const float* __restrict__ row_scale) {
   __shared__ __align__(16) __nv_bfloat16 gs[2][ROWS][G_PITCH];
   __shared__ __align__(16) __nv_bfloat16 ls[2][ROWS][L_PITCH];
   const int e = blockIdx.y;
@@ -67,14 +72,29 @@ __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bflo
       const int r = piece >> 4, c = (piece & 15) * 8;
       const int64_t row = r0 + r, col = c0 + c;
       const bool ok = row < end && col < n;
-      cp_async16(&gs[buf][r][c], ok ? g + row * ldg + col : g, ok);
+      const int64_t src = ok && g_rows != nullptr ? static_cast<int64_t>(g_rows[row]) : row;
+      cp_async16(&gs[buf][r][c], ok ? g + src * ldg + col : g, ok);
     }
     // low: 64 rows x 16 = 128 pieces
     if (threadIdx.x < 128) {
       const int r = threadIdx.x >> 1, c = (threadIdx.x & 1) * 8;
       const int64_t row = r0 + r;
       const bool ok = row < end;
-      cp_async16(&ls[buf][r][c], ok ? low + row * 16 + c : low, ok);
+      if (row_scale == nullptr) {
+        cp_async16(&ls[buf][r][c], ok ? low + row * 16 + c : low, ok);
+      } else {  // bf16(w * low): a plain load, scaled and stored (the ring's barrier also covers these stores)
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (ok) {
+          const uint4 l = *reinterpret_cast<const uint4*>(low + row * 16 + c);
+          const float w = row_scale[row];
+          const uint32_t in[4] = {l.x, l.y, l.z, l.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = pack_bf16x2(bf16_lo(in[j]) * w, bf16_hi(in[j]) * w);
+          v = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        *reinterpret_cast<uint4*>(&ls[buf][r][c]) = v;
+      }
     }
     cp_async_commit();
   };
@@ -132,9 +152,9 @@ __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bflo
 }  // namespace reduce
 }  // namespace meep2b
 
-extern "C" int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int64_t ldg, const void* low,
-                                     const int32_t* offsets, int32_t experts, float scaling, void* out,
-                                     void* stream) {
+static int grouped_reduce_launch(const void* g, const int32_t* g_rows, const float* row_scale, int64_t rows,
+                                 int64_t n, int64_t ldg, const void* low, const int32_t* offsets, int32_t experts,
+                                 float scaling, void* out, void* stream) {
   using namespace meep2b;
   if (rows < 0 || n < 1 || experts < 1 || ldg < n) return MEEP2B_ERR_SHAPE;
   if (n % 8 || ldg % 8) return MEEP2B_ERR_ALIGN;
@@ -144,6 +164,20 @@ extern "C" int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int
   dim3 grid(static_cast<unsigned>((n + reduce::COLS - 1) / reduce::COLS), static_cast<unsigned>(experts));
   reduce::grouped_reduce_kernel<<<grid, reduce::THREADS, 0, s>>>(
       static_cast<const __nv_bfloat16*>(g), n, ldg, static_cast<const __nv_bfloat16*>(low), offsets, scaling,
-      static_cast<__nv_bfloat16*>(out));
+      static_cast<__nv_bfloat16*>(out), g_rows, row_scale);
   return launch_status();
+}
+
+extern "C" int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int64_t ldg, const void* low,
+                                     const int32_t* offsets, int32_t experts, float scaling, void* out,
+                                     void* stream) {
+  return grouped_reduce_launch(g, nullptr, nullptr, rows, n, ldg, low, offsets, experts, scaling, out, stream);
+}
+
+extern "C" int meep2b_grouped_reduce_rows(const void* g, const int32_t* g_rows, const float* row_scale,
+                                          int64_t rows, int64_t n, int64_t ldg, const void* low,
+                                          const int32_t* offsets, int32_t experts, float scaling, void* out,
+                                          void* stream) {
+  if (g_rows == nullptr) return MEEP2B_ERR_SHAPE;
+  return grouped_reduce_launch(g, g_rows, row_scale, rows, n, ldg, low, offsets, experts, scaling, out, stream);
 }

@@ -273,6 +273,20 @@ __global__ void __launch_bounds__(1024) tile_map_kernel(const int32_t* __restric
 
 using namespace meep2b;
 
+namespace meep2b {
+// Per routed row i (expert order): the token it reads (perm[i] / top_k) and its routing weight as float32.
+__global__ void routed_rows(const int64_t* __restrict__ perm, int64_t n, int top_k, const void* __restrict__ weights,
+                            bool bf16, int32_t* __restrict__ token_rows, float* __restrict__ weights_g) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int64_t a = perm[i];
+  token_rows[i] = static_cast<int32_t>(a / top_k);
+  if (weights != nullptr && weights_g != nullptr)
+    weights_g[i] = bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(weights)[a])
+                        : static_cast<const float*>(weights)[a];
+}
+}  // namespace meep2b
+
 extern "C" {
 
 size_t meep2b_route_workspace_bytes(int64_t assignments, int32_t experts) {
@@ -299,6 +313,20 @@ int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts
   const size_t scatter_smem = sizeof(int) * 9 * (experts + 1);
   route_scatter<<<blocks, kRouteThreads, scatter_smem, s>>>(expert_ids, assignments, experts, counts, perm,
                                                             expert_ids_g, inverse);
+  return launch_status();
+}
+
+int meep2b_routed_rows(const int64_t* perm, int64_t assignments, int32_t top_k, const void* weights,
+                       int32_t weights_dtype, int32_t* token_rows, float* weights_g, void* stream) {
+  if (top_k < 1 || assignments < 0) return MEEP2B_ERR_SHAPE;
+  if (weights != nullptr && weights_dtype != MEEP2B_F32 && weights_dtype != MEEP2B_BF16) return MEEP2B_ERR_DTYPE;
+  if (assignments / top_k > INT32_MAX) return MEEP2B_ERR_SHAPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  if (assignments == 0) return MEEP2B_OK;
+  const unsigned grid = static_cast<unsigned>((assignments + 255) / 256);
+  routed_rows<<<grid, 256, 0, s>>>(perm, assignments, top_k, weights, weights_dtype == MEEP2B_BF16, token_rows,
+                                   weights_g);
   return launch_status();
 }
 

@@ -56,8 +56,16 @@ def check_against(res, want, prefix="", scaled=False):
         assert_close(res[f"grad_{n}"], want[f"{prefix}grad_{n}"], f"grad_{n}", scaled=True)
 
 
+@pytest.fixture(params=["fold", "gather", "copy"])
+def routed_rows_mode(request, monkeypatch):
+    """How the layer meets the routing: the un-permute's backward folded into the down stack's input gradient, the
+    products also reading their rows from the token-major tensors, or gathered copies throughout."""
+    monkeypatch.setenv("MEEP2B_ROUTED_ROWS", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("sentinel", [False, True])
-def test_layer_matches_the_reference_golden_vectors(golden, sentinel, pair_mode):
+def test_layer_matches_the_reference_golden_vectors(golden, sentinel, pair_mode, routed_rows_mode):
     res, _ = run_layer(layer_inputs.layer(**layer_inputs.SMALL), sentinel)
     check_against(res, golden("layer_small"), "sentinel_" if sentinel else "")
 
@@ -84,7 +92,7 @@ def test_layer_at_config1_matches_the_oracle_and_the_reference_slices(golden):
 
 @pytest.mark.parametrize("cfg", [dict(layer_inputs.QWEN3_30B, tokens=512), dict(layer_inputs.MIXTRAL, tokens=256),
                                  dict(layer_inputs.QWEN3_235B_FP8, tokens=256)])
-def test_layer_at_baseline_shapes_matches_the_oracle(cfg, pair_mode):
+def test_layer_at_baseline_shapes_matches_the_oracle(cfg, pair_mode, routed_rows_mode):
     inp = layer_inputs.layer(**cfg)
     res, idx = run_layer(inp)
     check_against(res, oracle_layer(inp, idx), scaled=True)
