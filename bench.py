@@ -32,6 +32,9 @@ CONFIGS = {
     "qwen3_235b_fp8": dict(tokens=32768, hidden=4096, inter=1536, experts=128, top_k=8, rank=16, alpha=32, zipf=1.1,
                            quant="fp8_block128"),
     "small": dict(tokens=2048, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
+    "small_fp8": dict(tokens=2048, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32,
+                      quant="fp8_block128"),
+    "small_nf4": dict(tokens=2048, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32, quant="nf4"),
     "half": dict(tokens=8192, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
 }
 METRIC = "MoE-LoRA layer fwd+bwd tokens/s"

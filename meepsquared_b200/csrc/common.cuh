@@ -369,6 +369,18 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return l | (h << 16);
 }
 
+// Two e4m3 codes of w (sel 0x1404: bytes 0-1, 0x3424: bytes 2-3) as a bf16 pair, exactly: each code s.eeee.mmm is
+// placed as the bf16
+// s.0000eeee.mmm0000 (sign bit kept, magnitude shifted right by 4 within its half) and the pair is multiplied by
+// 2^120, which moves the exponent bias from 7 to 127 (subnormal codes land on bf16 subnormals and come out normal).
+// Integer operations and one bf16x2 multiply: the float conversion instructions run at a fraction of the ALU rate.
+__device__ __forceinline__ __nv_bfloat162 e4m3x2_to_bf16x2(uint32_t w, uint32_t sel) {
+  const uint32_t v = __byte_perm(w, 0u, sel);  // code bytes at bits 8-15 and 24-31, zeros below
+  const uint32_t bits = (v & 0x80008000u) | ((v >> 4) & 0x07F007F0u);
+  const __nv_bfloat162 two120 = __halves2bfloat162(__ushort_as_bfloat16(0x7B80), __ushort_as_bfloat16(0x7B80));
+  return __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bits), two120);
+}
+
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 

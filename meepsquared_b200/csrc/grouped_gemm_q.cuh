@@ -82,16 +82,6 @@ __device__ __forceinline__ uint4 nf4_chunk(uint32_t w, float m, const float* lv)
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Two e4m3 codes in bytes i, i+1 of w as a bf16 pair, exactly: each code s.eeee.mmm is placed as the bf16
-// s.0000eeee.mmm0000 (sign bit kept, magnitude shifted right by 4 within its half) and the pair is multiplied by
-// 2^120, which moves the exponent bias from 7 to 127 (subnormal codes land on bf16 subnormals and come out normal).
-__device__ __forceinline__ __nv_bfloat162 e4m3x2_to_bf16x2(uint32_t w, uint32_t sel) {
-  const uint32_t v = __byte_perm(w, 0u, sel);  // code bytes at bits 8-15 and 24-31, zeros below
-  const uint32_t bits = (v & 0x80008000u) | ((v >> 4) & 0x07F007F0u);
-  const __nv_bfloat162 two120 = __halves2bfloat162(__ushort_as_bfloat16(0x7B80), __ushort_as_bfloat16(0x7B80));
-  return __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bits), two120);
-}
-
 // 8 bf16 from 8 e4m3 codes: exactly (E4M3), or times the bf16 multiplier m2 and rounded once (E4M3_BLOCKS: the
 // product of a 4-bit and an 8-bit significand is exact in float32, so the bf16 multiply rounds as
 // bf16(float32(w8) * bf16(s)) does).

@@ -178,6 +178,81 @@ __global__ void quant_multipliers(int nf4, const float* __restrict__ src, int64_
   }
 }
 
+// Vector forms of the three dequantisations: 16 weights per thread step (16 code bytes or 8 NF4 bytes in, 32 bytes
+// out), one scale or absmax look-up and one index computation per 16 weights. They apply when every group of 16
+// lies in one expert / block / 64-weight NF4 block (the launchers check), otherwise the element kernels above run.
+
+// bf16(f32(w8) * scale[e]) for 16 codes of expert e (per_expert a multiple of 16).
+__global__ void stack_dequant16(const uint4* __restrict__ codes, const float* __restrict__ scale, int64_t per16,
+                                int64_t groups, uint4* __restrict__ out) {
+  for (int64_t gi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; gi < groups;
+       gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 c = codes[gi];
+    const float s = scale[gi / per16];
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __nv_bfloat162 v = e4m3x2_to_bf16x2(w[j >> 1], (j & 1) ? 0x3424u : 0x1404u);  // exact
+      const uint32_t b = *reinterpret_cast<const uint32_t*>(&v);
+      o[j] = pack_bf16x2(__fmul_rn(bf16_lo(b), s), __fmul_rn(bf16_hi(b), s));
+    }
+    out[2 * gi] = make_uint4(o[0], o[1], o[2], o[3]);
+    out[2 * gi + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// bf16(bf16(w8) * bf16(s)) for 16 codes of one row within one block (cols and the block width multiples of 16):
+// the product of the exact bf16 code and the bf16 scale is exact before its one rounding, so a bf16x2 multiply gives
+// the same bits as the float32 multiply and conversion.
+__global__ void block_dequant16(const uint4* __restrict__ codes, int64_t rows, int64_t cols16,
+                                const float* __restrict__ scale_inv, int sr, int sc, int64_t br, int64_t bc,
+                                int64_t groups, uint4* __restrict__ out) {
+  for (int64_t gi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; gi < groups;
+       gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t rowi = gi / cols16, c = (gi - rowi * cols16) * 16;
+    const int64_t m = rowi / rows, r = rowi - m * rows;
+    const float s = bf16_round(scale_inv[(m * sr + r / br) * sc + c / bc]);
+    const __nv_bfloat162 s2 = __float2bfloat162_rn(s);
+    const uint4 cw = codes[gi];
+    const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __nv_bfloat162 v = __hmul2(e4m3x2_to_bf16x2(w[j >> 1], (j & 1) ? 0x3424u : 0x1404u), s2);
+      o[j] = *reinterpret_cast<const uint32_t*>(&v);
+    }
+    out[2 * gi] = make_uint4(o[0], o[1], o[2], o[3]);
+    out[2 * gi + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// NF4, 16 weights (8 bytes) per step within one block of `blocksize` (a multiple of 16): the levels from shared
+// memory (constant memory serialises divergent reads), one absmax per 16 weights.
+__global__ void nf4_dequant16(const uint2* __restrict__ packed, const float* __restrict__ absmax, int64_t per_block16,
+                              int64_t groups, uint4* __restrict__ out) {
+  __shared__ float lv[16];
+  if (threadIdx.x < 16) lv[threadIdx.x] = kNF4Levels[threadIdx.x];
+  __syncthreads();
+  for (int64_t gi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; gi < groups;
+       gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint2 p = packed[gi];
+    const float a = absmax[gi / per_block16];
+    const uint32_t words[2] = {p.x, p.y};
+    uint32_t res[8];
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t byte = (words[w] >> (8 * b)) & 0xFF;
+        res[4 * w + b] = pack_bf16x2(__fmul_rn(lv[byte >> 4], a), __fmul_rn(lv[byte & 0xF], a));
+      }
+    }
+    out[2 * gi] = make_uint4(res[0], res[1], res[2], res[3]);
+    out[2 * gi + 1] = make_uint4(res[4], res[5], res[6], res[7]);
+  }
+}
+
 inline unsigned grid_for(int64_t n, int threads = 256) {
   int64_t b = (n + threads - 1) / threads;
   if (b > 148 * 32) b = 148 * 32;
@@ -219,7 +294,12 @@ int meep2b_fp8_stack_dequantize(const uint8_t* codes, const float* scale, int32_
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
   const int64_t total = per_expert * experts;
-  stack_dequant<<<grid_for(total), 256, 0, s>>>(codes, scale, per_expert, total, static_cast<__nv_bfloat16*>(out));
+  if (per_expert % 16 == 0 && aligned16(codes) && aligned16(out)) {
+    stack_dequant16<<<grid_for(total / 16), 256, 0, s>>>(reinterpret_cast<const uint4*>(codes), scale, per_expert / 16,
+                                                         total / 16, static_cast<uint4*>(out));
+  } else {
+    stack_dequant<<<grid_for(total), 256, 0, s>>>(codes, scale, per_expert, total, static_cast<__nv_bfloat16*>(out));
+  }
   return launch_status();
 }
 
@@ -230,8 +310,14 @@ int meep2b_fp8_block_dequantize(const uint8_t* codes, int64_t matrices, int64_t 
   MEEP2B_TRY(bind_stream_device(s));
   const int64_t br = (rows + sr - 1) / sr, bc = (cols + sc - 1) / sc;
   const int64_t total = matrices * rows * cols;
-  block_dequant<<<grid_for(total), 256, 0, s>>>(codes, rows, cols, scale_inv, sr, sc, br, bc, total,
-                                                static_cast<__nv_bfloat16*>(out));
+  if (cols % 16 == 0 && bc % 16 == 0 && aligned16(codes) && aligned16(out)) {
+    block_dequant16<<<grid_for(total / 16), 256, 0, s>>>(reinterpret_cast<const uint4*>(codes), rows, cols / 16,
+                                                         scale_inv, sr, sc, br, bc, total / 16,
+                                                         static_cast<uint4*>(out));
+  } else {
+    block_dequant<<<grid_for(total), 256, 0, s>>>(codes, rows, cols, scale_inv, sr, sc, br, bc, total,
+                                                  static_cast<__nv_bfloat16*>(out));
+  }
   return launch_status();
 }
 
@@ -291,9 +377,13 @@ int meep2b_nf4_dequantize(const uint8_t* packed, const uint8_t* absmax, const fl
   nf4_absmax<<<grid_for(blocks), 256, 0, s>>>(absmax, absmax2, code2, offset, blocksize2, blocks, absmax_out);
   const int64_t bytes = n / 2;
   const int64_t groups = bytes / 8;
-  if (groups > 0)
+  if (groups > 0 && blocksize % 16 == 0) {
+    nf4_dequant16<<<grid_for(groups), 256, 0, s>>>(reinterpret_cast<const uint2*>(packed), absmax_out,
+                                                   blocksize / 16, groups, static_cast<uint4*>(out));
+  } else if (groups > 0) {
     nf4_dequant<<<grid_for(groups), 256, 0, s>>>(reinterpret_cast<const uint2*>(packed), absmax_out, blocksize, groups,
                                                  static_cast<uint4*>(out));
+  }
   if (groups * 8 < bytes)
     nf4_dequant_tail<<<1, 256, 0, s>>>(packed, absmax_out, blocksize, groups * 8, bytes,
                                        static_cast<__nv_bfloat16*>(out));
