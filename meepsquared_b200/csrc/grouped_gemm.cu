@@ -1079,6 +1079,7 @@ static int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMa
 }
 
 #include "grouped_gemm_q.cuh"
+#include "grouped_gemm_qpair.cuh"
 
 }  // namespace gemm
 }  // namespace meep2b
@@ -1091,7 +1092,7 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   const bool quantised = a->weight_dtype == MEEP2B_NF4 || a->weight_dtype == MEEP2B_E4M3 ||
                          a->weight_dtype == MEEP2B_E4M3_BLOCKS;
   if (a->weight_dtype != MEEP2B_BF16 && !quantised) return MEEP2B_ERR_UNSUPPORTED;
-  if (quantised && a->block_m == 256) return MEEP2B_ERR_UNSUPPORTED;
+  if (quantised && a->block_m == 256 && a->b_mn) return MEEP2B_ERR_UNSUPPORTED;  // quantised pairs: K-major only
   if (a->rows < 0 || a->k < 1 || a->n < 1 || a->experts < 1) return MEEP2B_ERR_SHAPE;
   if (a->k % 8 || a->n % 8 || a->ldx % 8 || a->ldo % 8 || a->ldx < a->k) return MEEP2B_ERR_ALIGN;
   if (a->rows > INT32_MAX || a->k > INT32_MAX || a->n > INT32_MAX) return MEEP2B_ERR_SHAPE;
@@ -1205,6 +1206,7 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
 
   const int block_m = a->block_m == 0 ? 128 : a->block_m;
   if (block_m != 128 && block_m != 256) return MEEP2B_ERR_UNSUPPORTED;
+  if (quantised && block_m == 256) return launch_quantized_pair(a, tx, prm, sms, s);
   if (block_m == 256) {
     PairMaps maps;
     maps.x = tx;

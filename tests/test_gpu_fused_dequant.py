@@ -46,10 +46,13 @@ def bits(t):
 
 
 @pytest.mark.parametrize("kind", KINDS)
-@pytest.mark.parametrize("mode", ["fwd_plain", "fwd_swiglu", "bwd_plain", "bwd_dswiglu"])
+@pytest.mark.parametrize("mode", ["fwd_plain", "fwd_swiglu", "bwd_plain", "bwd_dswiglu", "fwd_plain_pair",
+                                  "fwd_swiglu_pair"])
 @pytest.mark.parametrize("lora", [False, True])
 def test_the_fused_dequantisation_gives_the_dequantised_stacks_product_bit_for_bit(kind, mode, lora, monkeypatch):
-    monkeypatch.setenv("MEEP2B_PAIR", "0")  # both products on one-CTA tiles
+    # both products on one-CTA tiles, or both on CTA pairs (the forward, K-major products)
+    monkeypatch.setenv("MEEP2B_PAIR", "1" if mode.endswith("_pair") else "0")
+    mode = mode.replace("_pair", "")
     gen = torch.Generator().manual_seed(11 + KINDS.index(kind))
     rows_per_expert = [37, 0, 200, 129]
     experts, rows = len(rows_per_expert), sum(rows_per_expert)
