@@ -102,9 +102,27 @@ class DeviceError(RuntimeError):
     pass
 
 
+# Kernels each entry point launches per successful call (the ones this package calls on its hot path), for the
+# count of the library's launches in a timed region (benchmark); `launches` accumulates them per entry point.
+KERNELS_PER_CALL = {
+    "meep2b_route": 3, "meep2b_route_noalloc": 3, "meep2b_routed_rows": 1, "meep2b_gather": 1,
+    "meep2b_unpermute": 1, "meep2b_unpermute_backward": 1, "meep2b_tile_map": 1, "meep2b_grouped_product": 1,
+    "meep2b_grouped_reduce": 1, "meep2b_grouped_reduce_rows": 1, "meep2b_fp8_stack_dequantize": 1,
+    "meep2b_fp8_block_dequantize": 1, "meep2b_nf4_dequantize": 2, "meep2b_nf4_absmax": 1,
+    "meep2b_quant_multipliers": 1,
+}
+launches = {}
+
+
+def launch_count() -> int:
+    """Kernels the library launched through the calls checked so far (see KERNELS_PER_CALL)."""
+    return sum(KERNELS_PER_CALL.get(k, 1) * v for k, v in launches.items())
+
+
 def check(status: int, what: str):
     """Raises the reference's exception kind for a non-zero status (ValueError for sizes, ...)."""
     if status == OK:
+        launches[what] = launches.get(what, 0) + 1
         return
     msg = f"{what}: {load().meep2b_status_string(status).decode()}"
     if status in (ERR_SHAPE, ERR_ALIGN):
