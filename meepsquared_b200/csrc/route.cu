@@ -130,8 +130,18 @@ __global__ void __launch_bounds__(256) gather_rows(const uint4* __restrict__ hid
   uint4* dst = selected + row * vec_per_row;
   if (weights_g != nullptr && lane == 0) weights_g[row] = weights[src];
   if (row < valid) {
+    // eight 16-byte loads in flight per lane before their stores; the stores stream (the sorted copy is read once,
+    // later, by the product) so that the token-major source stays in L2 for the other k - 1 reads of each row
     const uint4* s = hidden + (src / top_k) * vec_per_row;
-    for (int64_t v = lane; v < vec_per_row; v += 32) dst[v] = __ldg(s + v);
+    int64_t v = lane;
+    for (; v + 7 * 32 < vec_per_row; v += 8 * 32) {
+      uint4 q[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = __ldg(s + v + 32 * i);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) __stcs(dst + v + 32 * i, q[i]);
+    }
+    for (; v < vec_per_row; v += 32) __stcs(dst + v, __ldg(s + v));
   } else {
     for (int64_t v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
   }
