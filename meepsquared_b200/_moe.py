@@ -169,13 +169,14 @@ class _RoutedExperts(torch.autograd.Function):
         t = st.is_transposed
         ad1 = _grouped._Adapters(lhs1.detach(), rhs1.detach(), t) if lhs1 is not None else None
         ad2 = _grouped._Adapters(lhs2.detach(), rhs2.detach(), t) if lhs2 is not None else None
-        if isinstance(st.gate_up, _grouped.QuantStack):
+        gate_up = _stack(st.gate_up)
+        if isinstance(gate_up, _grouped.QuantStack):
             b_mn = 1 if t else 0
         else:
-            _, b_mn = _grouped._stack_memory(st.gate_up, not t)
+            _, b_mn = _grouped._stack_memory(gate_up, not t)
         if b_mn != 0:
             raise NotImplementedError("SwiGLU is fused for a gate/up stack stored (experts, 2I, hidden), k contiguous")
-        two_i = st.gate_up.shape[2] if t else st.gate_up.shape[1]
+        two_i = gate_up.shape[2] if t else gate_up.shape[1]
         rows = routing.perm.numel()
         gu = torch.empty((rows, two_i), dtype=torch.bfloat16, device=hidden.device)
         token_rows = w32 = None
@@ -188,10 +189,11 @@ class _RoutedExperts(torch.autograd.Function):
                 x, x_rows = hidden, token_rows
             else:
                 x, x_rows = gather(hidden, routing, None), None
-        h, low1 = _grouped._launch(x, st.gate_up, st.gate_up_scale, routing.offsets, not t, ad1, st.scaling1,
+        h, low1 = _grouped._launch(x, gate_up, st.gate_up_scale, routing.offsets, not t, ad1, st.scaling1,
                                    st.gate_up_bias, True, tiles=tiles, epilogue=_lib.EPI_SWIGLU, aux=gu,
                                    x_rows=x_rows)
-        y, low2 = _grouped._launch(h, st.down, st.down_scale, routing.offsets, not t, ad2, st.scaling2,
+        del gate_up  # a stack dequantised for this product alone is released before the next one is made
+        y, low2 = _grouped._launch(h, _stack(st.down), st.down_scale, routing.offsets, not t, ad2, st.scaling2,
                                    st.down_bias, True, tiles=tiles)
         out = unpermute(y, routing, weights_g)
         kept = (x, gu, h, y) if mode == "copy" else (hidden, gu, h, token_rows, w32)
@@ -220,8 +222,9 @@ class _RoutedExperts(torch.autograd.Function):
             grad_out = grad_out.to(torch.bfloat16)
         if mode == "copy":
             grad_y, grad_w = unpermute_backward(grad_out, y, routing)
-            dgu, low2b = _grouped._launch(grad_y, st.down, st.down_scale, routing.offsets, t, ad2, st.scaling2, None,
-                                          True, backward=True, tiles=tiles, epilogue=_lib.EPI_DSWIGLU, aux=gu)
+            dgu, low2b = _grouped._launch(grad_y, _stack(st.down), st.down_scale, routing.offsets, t, ad2,
+                                          st.scaling2, None, True, backward=True, tiles=tiles,
+                                          epilogue=_lib.EPI_DSWIGLU, aux=gu)
         else:
             # the down stack's input gradient over the upstream gradient's rows, each weighted by its routing weight,
             # SwiGLU's backward in the epilogue, and <dh, h> per row and 96 columns for the routing weights' gradient
@@ -231,13 +234,13 @@ class _RoutedExperts(torch.autograd.Function):
                 g, g_rows = grad_out, token_rows
             else:
                 g, g_rows = gather(grad_out, routing, None), None
-            dgu, low2b = _grouped._launch(g, st.down, st.down_scale, routing.offsets, t, ad2, st.scaling2, None,
+            dgu, low2b = _grouped._launch(g, _stack(st.down), st.down_scale, routing.offsets, t, ad2, st.scaling2, None,
                                           True, backward=True, tiles=tiles, epilogue=_lib.EPI_DSWIGLU, aux=gu,
                                           x_rows=g_rows, row_scale=w32, w_grad=parts)
             grad_w = torch.empty(routing.perm.numel(), dtype=torch.float32, device=grad_out.device)
             grad_w[routing.perm] = parts.sum(dim=1)  # a fixed order: the same bits on every run
-        dsel, low1b = _grouped._launch(dgu, st.gate_up, st.gate_up_scale, routing.offsets, t, ad1, st.scaling1, None,
-                                       True, backward=True, tiles=tiles)
+        dsel, low1b = _grouped._launch(dgu, _stack(st.gate_up), st.gate_up_scale, routing.offsets, t, ad1, st.scaling1,
+                                       None, True, backward=True, tiles=tiles)
         grads = [None, None, None, None]
         if ad1 is not None:
             if mode == "copy":
@@ -259,24 +262,47 @@ class _RoutedExperts(torch.autograd.Function):
         return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None)
 
 
+class _PerProduct:
+    """A quantised stack dequantised to a bf16 copy each time a product reads it, the copy released after that
+    product: for the forward product and again for the backward one, as the reference treats an FP8 stack
+    (meepsquared/_fp8.py:140-156), so at most one layer stack is ever held in bf16."""
+
+    def __init__(self, make):
+        self.make = make
+
+
+def _stack(s):
+    return s.make() if isinstance(s, _PerProduct) else s
+
+
 def _kernel_stack(experts, name):
     """(stack, scale) for the kernels. A bf16 stack as it is. A quantised one goes to the products as a QuantStack,
     dequantised in shared memory between the TMA load and the MMA: FP8 (e4m3) with its `<name>_scale_inv` (one
     scale per expert, applied in the epilogue, or a 128 x 128 grid of blocks) or NF4 (an NF4State in the
-    attribute's place). A quantised stack without whole 64-weight blocks is dequantised for this call instead, and
-    so is every quantised stack with MEEP2B_DEQUANT=call (a bf16 copy held for the layer call: more memory, the
-    bf16 products' speed)."""
+    attribute's place). A quantised stack without whole 64-weight blocks is dequantised to bf16 for each product
+    instead, and so is every quantised stack with MEEP2B_DEQUANT=product (the dequantisation kernel's HBM traffic
+    each time, the bf16 products' speed)."""
     from . import _fp8, _nf4
 
     weight = getattr(experts, name)
-    per_call = os.environ.get("MEEP2B_DEQUANT", "fused") == "call"
+    per_product = os.environ.get("MEEP2B_DEQUANT", "fused") == "product"
     if isinstance(weight, _nf4.NF4State):
-        fused = None if per_call else _grouped.QuantStack.from_nf4(weight)
-        return (fused if fused is not None else _nf4.dequantize(weight)), None
+        fused = None if per_product else _grouped.QuantStack.from_nf4(weight)
+        return (fused if fused is not None else _PerProduct(lambda: _nf4.dequantize(weight))), None
     if weight.dtype == torch.float8_e4m3fn:
         scale = getattr(experts, name + _fp8.STACK_SCALE)
-        if per_call:
-            return _fp8.dequantize(weight.detach(), scale), None
+        # one scale per expert is applied to the accumulator, the codes converted exactly (_grouped.py:200-208);
+        # a grid of block scales goes into the converted weights (quantize.py:131-157)
+        per_expert = scale.dim() == 1
+        epi_scale = scale.float().contiguous() if per_expert else None
+        w8 = weight.detach()
+        if per_expert:
+            ones = torch.ones(w8.shape[0], device=w8.device, dtype=torch.float32)
+            copy = _PerProduct(lambda: _fp8.dequantize_stack(w8, ones, torch.bfloat16))
+        else:
+            copy = _PerProduct(lambda: _fp8.dequantize_blocks(w8, scale))
+        if per_product:
+            return copy, epi_scale
         # the multipliers of a block-scaled stack are prepared once and kept while the stack and scale are unchanged
         cache = experts.__dict__.setdefault("_meep2b_quant_stacks", {})
         key = (weight.data_ptr(), weight._version, scale.data_ptr(), scale._version)
@@ -284,11 +310,9 @@ def _kernel_stack(experts, name):
         if hit is not None and hit[0] == key:
             fused = hit[1]
         else:
-            fused = _grouped.QuantStack.from_fp8(weight.detach(), scale)
+            fused = _grouped.QuantStack.from_fp8(w8, scale)
             cache[name] = (key, fused)
-        if fused is None:
-            return _fp8.dequantize(weight.detach(), scale), None
-        return fused, (scale.float().contiguous() if fused.kind == _lib.E4M3 else None)
+        return (fused if fused is not None else copy), epi_scale
     if weight.dtype != torch.bfloat16:
         raise TypeError(f"expert stacks in bf16, FP8 (e4m3) or NF4; got {weight.dtype}")
     return weight.detach(), None

@@ -117,10 +117,9 @@ def _dequantised(ex, name):
     return _fp8.dequantize(w, getattr(ex, name + "_scale_inv")).float().cpu()
 
 
-@pytest.mark.parametrize("kind", ["nf4", "fp8_expert", "fp8_block128"])
-def test_layer_with_quantised_stacks_matches_the_oracle_on_the_dequantised_weights(kind):
-    """QLoRA (NF4) and FP8 stacks (one scale per expert, or 128 x 128 blocks) in the routed layer: the layer equals
-    the float32 computation with the stacks dequantised as the reference dequantises them."""
+def _quantised_layer(kind):
+    """(the layer's inputs, an experts module with its stacks quantised as `kind`, a function running the layer
+    forward and backward and returning the outputs and gradients)."""
     from meepsquared_b200 import _fp8, _nf4
 
     inp = layer_inputs.layer(**dict(layer_inputs.QWEN3_30B, tokens=256, experts=16))
@@ -133,15 +132,47 @@ def test_layer_with_quantised_stacks_matches_the_oracle_on_the_dequantised_weigh
     else:
         assert _fp8.convert_stacks(experts, block=128 if kind == "fp8_block128" else None) == 2
         assert experts.gate_up_proj.dtype == torch.float8_e4m3fn
-    hidden = bf("hidden").requires_grad_()
-    weights = inp["top_k_weights"].to(DEV).requires_grad_()
-    leaves = {n: bf(n).requires_grad_() for n in ("gate_up_lhs", "gate_up_rhs", "down_lhs", "down_rhs")}
-    factors = {"gate_up_proj": (leaves["gate_up_lhs"], leaves["gate_up_rhs"], inp["scaling"]),
-               "down_proj": (leaves["down_lhs"], leaves["down_rhs"], inp["scaling"])}
-    out = mb.routed_forward(experts, hidden, idx.to(DEV), weights, factors)
-    out.backward(inp["grad"].to(DEV, torch.bfloat16))
-    res = {"out": out.detach(), "grad_hidden": hidden.grad, "grad_weights": weights.grad}
-    for n, t in leaves.items():
-        res[f"grad_{n}"] = t.grad
+
+    def run():
+        hidden = bf("hidden").requires_grad_()
+        weights = inp["top_k_weights"].to(DEV).requires_grad_()
+        leaves = {n: bf(n).requires_grad_() for n in ("gate_up_lhs", "gate_up_rhs", "down_lhs", "down_rhs")}
+        factors = {"gate_up_proj": (leaves["gate_up_lhs"], leaves["gate_up_rhs"], inp["scaling"]),
+                   "down_proj": (leaves["down_lhs"], leaves["down_rhs"], inp["scaling"])}
+        out = mb.routed_forward(experts, hidden, idx.to(DEV), weights, factors)
+        out.backward(inp["grad"].to(DEV, torch.bfloat16))
+        res = {"out": out.detach(), "grad_hidden": hidden.grad, "grad_weights": weights.grad}
+        for n, t in leaves.items():
+            res[f"grad_{n}"] = t.grad
+        return res
+
+    return inp, experts, run
+
+
+@pytest.mark.parametrize("dequant", ["fused", "product"])
+@pytest.mark.parametrize("kind", ["nf4", "fp8_expert", "fp8_block128"])
+def test_layer_with_quantised_stacks_matches_the_oracle_on_the_dequantised_weights(kind, dequant, monkeypatch):
+    """QLoRA (NF4) and FP8 stacks (one scale per expert, or 128 x 128 blocks) in the routed layer, dequantised in
+    the products' shared memory or to a bf16 copy per product: the layer equals the float32 computation with the
+    stacks dequantised as the reference dequantises them."""
+    monkeypatch.setenv("MEEP2B_DEQUANT", dequant)
+    inp, experts, run = _quantised_layer(kind)
+    res = run()
+    idx = inp["top_k_index"]
     ref_inp = dict(inp, gate_up=_dequantised(experts, "gate_up_proj"), down=_dequantised(experts, "down_proj"))
     check_against(res, oracle_layer(ref_inp, idx), scaled=True)
+
+
+@pytest.mark.parametrize("kind", ["nf4", "fp8_expert", "fp8_block128"])
+def test_quantised_stacks_give_the_same_bits_fused_or_dequantised_per_product(kind, monkeypatch):
+    """The fused conversion writes exactly the bf16 stack the dequantisation kernels write, so with the same
+    routed-row mode and tile kernels the whole layer's outputs and gradients are identical bit for bit."""
+    monkeypatch.setenv("MEEP2B_ROUTED_ROWS", "copy")
+    monkeypatch.setenv("MEEP2B_PAIR", "0")
+    _, _, run = _quantised_layer(kind)
+    monkeypatch.setenv("MEEP2B_DEQUANT", "fused")
+    fused = run()
+    monkeypatch.setenv("MEEP2B_DEQUANT", "product")
+    per_product = run()
+    for k in fused:
+        assert torch.equal(fused[k], per_product[k]), k
