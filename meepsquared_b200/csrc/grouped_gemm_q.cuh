@@ -15,22 +15,35 @@
 // codes included), not with the float conversion instructions, whose throughput is a fraction of the ALU's.
 //
 // Per CTA (one per SM), 16 warps:
-//   warp 0      TMA producer: per k-step the x tile, the LoRA panel (bf16) and the raw quantised B tile (codes,
-//               no swizzle) into ring 1; the deferred up factor as in the bf16 kernel;
-//   warp 1      TMEM owner and MMA issuer: A from ring 1, B from ring 2;
-//   warps 2-7   converters (192 threads): raw codes of ring 1 -> bf16 B tile of ring 2 in the 128-byte-swizzled
-//               layout the MMA reads (what TMA writes for a bf16 stack), plus a copy of the panel rows;
-//   warps 8-15  epilogue, as in the bf16 kernel.
-// Registers: launched with 128 per thread (512 threads); warpgroups 0-1 give theirs down to 80 and the epilogue's
-// two warpgroups take 176 (2 x 128 x 80 + 2 x 128 x 176 = 65536, the launch's total).
+//   warp 0       TMA producer: per k-step the x tile, the LoRA panel (bf16) and the raw quantised B tile (codes,
+//                swizzled) into ring 1; the deferred up factor as in the bf16 kernel;
+//   warp 1       TMEM owner and MMA issuer: A from ring 1, B from ring 2;
+//   warps 2-11   converters (320 threads, a few 8-weight tasks each per k-step): raw codes of ring 1 -> bf16 B
+//                tile of ring 2 in the 128-byte-swizzled layout the MMA reads (what TMA writes for a bf16 stack),
+//                plus a copy of the panel rows;
+//   warps 12-15  epilogue, one warp per TMEM lane quarter taking both column halves of a unit in turn
+// (dSwiGLU products: warps 2-7 convert and warps 8-15 run the epilogue, as QRoles says).
+// Registers: launched with 128 per thread (512 threads); the roles' warpgroups give theirs down with setmaxnreg and
+// the epilogue's take 176, to the launch's total of 65536.
 
 enum QuantFormat { QF_NF4 = 1, QF_E4M3 = 2, QF_E4M3_BLOCKS = 3 };
 
 constexpr int Q_THREADS = 512;
 constexpr int Q_CONV_WARP0 = 2;
-constexpr int Q_CONV_WARPS = 6;
-constexpr int Q_CONV_THREADS = Q_CONV_WARPS * 32;  // one B row (K-major) or one 64-column group of a k row (MN)
-constexpr int Q_EPI_WARP0 = 8;
+
+// Converter warps per CTA: ten (warps 2-11), with one epilogue warp per TMEM lane quarter (warps 12-15) taking both
+// column halves of a unit in turn; six (warps 2-7) for the dSwiGLU products over e4m3 codes, whose epilogue (the
+// pre-activations read back and the SwiGLU derivative per element) then bounds the unit and needs two warps per
+// lane quarter (warps 8-15, one half each). NF4's conversion (a level look-up per weight) keeps ten converters
+// throughout (measured faster). Registers: 3 x 128 x 112 + 128 x 176, or 2 x 128 x 80 + 2 x 128 x 176
+// (setmaxnreg), 65536 either way.
+template <int EPI, int QF>
+struct QRoles {
+  static constexpr int CONV_WARPS = EPI == MEEP2B_EPI_DSWIGLU && QF != QF_NF4 ? 6 : 10;
+  static constexpr int CONV_THREADS = CONV_WARPS * 32;
+  static constexpr int EPI_WARP0 = Q_CONV_WARP0 + CONV_WARPS;
+  static constexpr int EPI_HALVES = EPI_WARP0 == 8 ? 1 : 2;  // column halves each epilogue warp takes
+};
 
 // Shared memory: ring 1 (S1 stages) = x tile | panel | raw codes | multipliers; ring 2 (S2 stages) = bf16 B tile
 // (+ panel rows).
@@ -98,61 +111,59 @@ __device__ __forceinline__ uint4 e4m3_chunk(uint2 c, __nv_bfloat162 m2) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// One converter thread's share of a k-step: 64 consecutive weights of the stored matrix (one row of the K-major
-// B tile, or one 64-column group of a k row of the MN-major tile) into 8 swizzled 16-byte chunks of ring 2.
-template <bool B_MN, int QF, bool SWIGLU>
-__device__ __forceinline__ void convert_row(const Params& p, int nb, int ct, const uint8_t* raw, const float* mult,
-                                            uint8_t* bdst, const float* lv) {
-  using QP = QPlan<B_MN, QF>;
-  bool valid;
-  float m = 1.0f;
-  uint8_t* out_row;     // the 128-byte row of the swizzled chunk the 64 weights land in
-  uint32_t sw;          // its swizzle phase (row & 7)
-  const uint8_t* src;   // their codes in ring 1
-  int rr;               // the raw row (its swizzle phase)
-  if (!B_MN) {
-    const int r = ct;  // B row = stored row n, 64 k
-    if (SWIGLU) {
-      valid = (r < 96 ? nb * 96 + r : nb * 96 + r - 96) < p.inter;
-    } else {
-      valid = nb * BN + r < p.N;
-    }
-    if (QF != QF_E4M3) m = mult[r];
-    out_row = bdst + r * 128;
-    sw = r & 7;
-    rr = r;
-  } else {
-    const int g = ct >> 6, kr = ct & 63;  // 64-column group, k row of the tile (a warp stays in one group)
-    valid = nb * BN + 64 * g < p.N;
-    if (QF != QF_E4M3) m = mult[g * 64 + kr];
-    out_row = bdst + g * (64 * BK * 2) + kr * 128;
-    sw = kr & 7;
-    rr = g * 64 + kr;
-  }
-  src = raw + rr * QP::RAW_ROW;
-  // 16-byte chunk j of a raw row sits at j ^ (row >> 2 & 1) (32-byte swizzle) or j ^ (row >> 1 & 3) (64-byte)
-  const uint32_t rsw = QF == QF_NF4 ? ((rr >> 2) & 1) : ((rr >> 1) & 3);
-  uint4 o[8];
-  if (!valid) {
+// The converters' share of a k-step: the raw codes of `rows` B rows into the bf16 B tile, in tasks of 8 weights.
+// Task q is chunk c = q % 8 of B row r = q / 8: its 8 weights become one 16-byte chunk of the row's 128 bytes, so
+// the eight chunks of a row go to eight consecutive threads, which read the row's codes as one 64-byte (e4m3) or
+// 32-byte (NF4) run and write its bf16 chunks as one 128-byte row (no bank conflicts either way). Both B layouts
+// put row r (K-major: a stored row; MN-major: 64-column group r / 64, k row r % 64) at byte r * 128 with the chunk
+// swizzle r % 8, its codes at raw row r (16-byte chunk j at j ^ (r / 4 % 2) for NF4's 32-byte swizzle, j ^ (r / 2
+// % 4) for e4m3's 64-byte one) and its multiplier at mult[r]. A thread's code loads are all issued before its
+// conversions; rows for which valid(r) is false (past the stack's end) are written as zeros.
+template <int QF, int ROWS, int NT, typename Valid>
+__device__ __forceinline__ void convert_tasks(int ct, int rows, const uint8_t* raw, const float* mult, uint8_t* bdst,
+                                              const float* lv, Valid valid) {
+  constexpr int RAW_ROW = QF == QF_NF4 ? 32 : 64;
+  constexpr int MAXT = (ROWS * 8 + NT - 1) / NT;
+  const int total = rows * 8;
+  uint2 code[MAXT];
+  float m[MAXT];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) o[c] = make_uint4(0u, 0u, 0u, 0u);
-  } else if (QF == QF_NF4) {
-    const uint4 w0 = *reinterpret_cast<const uint4*>(src + ((0u ^ rsw) << 4));
-    const uint4 w1 = *reinterpret_cast<const uint4*>(src + ((1u ^ rsw) << 4));
-    const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-    for (int c = 0; c < 8; ++c) o[c] = nf4_chunk(w[c], m, lv);
-  } else {
-    const __nv_bfloat162 m2 = __float2bfloat162_rn(m);  // m holds a bf16 value: exact
-#pragma unroll
-    for (int c = 0; c < 8; c += 2) {
-      const uint4 w = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c >> 1) ^ rsw) << 4));
-      o[c] = e4m3_chunk<QF>(make_uint2(w.x, w.y), m2);
-      o[c + 1] = e4m3_chunk<QF>(make_uint2(w.z, w.w), m2);
+  for (int i = 0; i < MAXT; ++i) {
+    const int q = ct + i * NT;
+    code[i] = make_uint2(0u, 0u);
+    m[i] = 1.0f;
+    if (q < total) {
+      const int r = q >> 3, c = q & 7;
+      const uint8_t* src = raw + r * RAW_ROW;
+      if (QF == QF_NF4) {
+        const uint32_t rsw = (r >> 2) & 1;
+        code[i].x = *reinterpret_cast<const uint32_t*>(src + (((static_cast<uint32_t>(c) >> 2) ^ rsw) << 4) +
+                                                       ((c & 3) << 2));
+      } else {
+        const uint32_t rsw = (r >> 1) & 3;
+        code[i] = *reinterpret_cast<const uint2*>(src + (((static_cast<uint32_t>(c) >> 1) ^ rsw) << 4) +
+                                                  ((c & 1) << 3));
+      }
+      if (QF != QF_E4M3) m[i] = mult[r];
     }
   }
 #pragma unroll
-  for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(out_row + ((c ^ sw) << 4)) = o[c];
+  for (int i = 0; i < MAXT; ++i) {
+    const int q = ct + i * NT;
+    if (q < total) {
+      const int r = q >> 3, c = q & 7;
+      uint4 o;
+      if (!valid(r)) {
+        o = make_uint4(0u, 0u, 0u, 0u);
+      } else if (QF == QF_NF4) {
+        o = nf4_chunk(code[i].x, m[i], lv);
+      } else {
+        o = e4m3_chunk<QF>(code[i], __float2bfloat162_rn(m[i]));  // m holds a bf16 value: exact
+      }
+      *reinterpret_cast<uint4*>(bdst + r * 128 + ((static_cast<uint32_t>(c) ^ static_cast<uint32_t>(r & 7)) << 4)) =
+          o;
+    }
+  }
 }
 
 // Warps 0-7 of the quantised kernel: TMA producer, MMA issuer, converters.
@@ -357,12 +368,17 @@ __device__ __forceinline__ void q_mainloop_roles(const CUtensorMap& tm_x, const 
         if (!mbar_wait(bar_full1(s1), ph1) || !mbar_wait(bar_empty2(s2), ph2 ^ 1)) { ok = false; break; }
         const uint8_t* st1 = smem + QP::OFF_R1 + s1 * QP::S1_BYTES;
         uint8_t* bdst = smem + QP::OFF_R2 + s2 * QP::B_BYTES;
-        convert_row<B_MN, QF, SWIGLU>(p, nb, ct, st1 + QP::OFF_RAW, reinterpret_cast<const float*>(st1 + QP::OFF_MULT),
-                                      bdst, lv);
+        auto valid = [&](int r) {
+          if (B_MN) return nb * BN + 64 * (r >> 6) < p.N;
+          if (SWIGLU) return (r < 96 ? nb * 96 + r : nb * 96 + r - 96) < p.inter;
+          return nb * BN + r < p.N;
+        };
+        convert_tasks<QF, BN, QRoles<EPI, QF>::CONV_THREADS>(ct, BN, st1 + QP::OFF_RAW, reinterpret_cast<const float*>(st1 + QP::OFF_MULT), bdst, lv,
+                              valid);
         if (LORA) {  // the panel rows (K-major: B rows 192..207; MN-major: the fourth 64-column chunk), verbatim
           const uint4* ps = reinterpret_cast<const uint4*>(st1 + A_BYTES);
           uint4* pd = reinterpret_cast<uint4*>(bdst + (B_MN ? 3 * 64 * BK * 2 : BN * BK * 2));
-          for (int i = ct; i < QP::PANEL_BYTES / 16; i += Q_CONV_THREADS) pd[i] = ps[i];
+          for (int i = ct; i < QP::PANEL_BYTES / 16; i += QRoles<EPI, QF>::CONV_THREADS) pd[i] = ps[i];
         }
         fence_proxy_async_smem();  // the bf16 tile, written by these threads, is read by the tensor cores
         __syncwarp();
@@ -389,6 +405,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
                           const __grid_constant__ CUtensorMap tm_mult, const __grid_constant__ CUtensorMap tm_p,
                           const __grid_constant__ CUtensorMap tm_u, const Params p) {
   using QP = QPlan<B_MN, QF>;
+  using R = QRoles<EPI, QF>;
   constexpr int S1 = QP::S1, S2 = QP::S2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -414,10 +431,10 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S1; ++s) {
       mbar_init(bar_full1(s), 1);
-      mbar_init(bar_empty1(s), Q_CONV_WARPS + 1);  // each converter warp has read the codes; the MMAs the x tile
+      mbar_init(bar_empty1(s), R::CONV_WARPS + 1);  // each converter warp has read the codes; the MMAs the x tile
     }
     for (int s = 0; s < S2; ++s) {
-      mbar_init(bar_full2(s), Q_CONV_WARPS);
+      mbar_init(bar_full2(s), R::CONV_WARPS);
       mbar_init(bar_empty2(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -442,8 +459,12 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int total = (*p.tiles) * p.nblocks;
 
-  if (warp < Q_EPI_WARP0) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
+  if (warp < R::EPI_WARP0) {
+    if (R::CONV_WARPS == 10) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 112;");
+    } else {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
+    }
     q_mainloop_roles<B_MN, LORA, EPI, QF>(tm_x, tm_raw, tm_mult, tm_p, tm_u, p, smem, sbase, tmem_base, total, warp,
                                           lane);
   } else {
@@ -451,14 +472,15 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
     // ------------------------------------------------------------------------------------------ epilogue
     const uint32_t bar1 = sbase + QP::OFF_BAR + 8u * (2 * S1 + 2 * S2);
     const int qd = warp & 3;
-    const int half = (warp - Q_EPI_WARP0) >> 2;
+    const int half0 = R::EPI_HALVES == 1 ? (warp - R::EPI_WARP0) >> 2 : 0;
     int it = 0;
-    for (int u = blockIdx.x; u < total; u += gridDim.x, ++it) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++it) {
       const int ab = it & 1;
-      if (!epilogue_unit<EPI, LORA, false>(p, u, it, 0, smem + QP::OFF_LOW, tmem_base, qd, half, lane,
-                                           bar1 + 8u * (4 + ab), bar1 + 8u * 6, bar1 + 8u * ab,
-                                           bar1 + 8u * (2 + ab)))
-        break;
+      for (int h = 0; h < R::EPI_HALVES && ok; ++h)
+        ok = epilogue_unit<EPI, LORA, false>(p, u, it, 0, smem + QP::OFF_LOW, tmem_base, qd, half0 + h, lane,
+                                             bar1 + 8u * (4 + ab), bar1 + 8u * 6, bar1 + 8u * ab,
+                                             bar1 + 8u * (2 + ab));
     }
   }
 
@@ -476,8 +498,8 @@ static int launch_q(const CUtensorMap& tx, const CUtensorMap& traw, const CUtens
   auto kern = grouped_gemm_q_kernel<B_MN, LORA, EPI, QF>;
   static bool configured = false;
   if (!configured) {
-    // setmaxnreg.inc draws on the registers the block was launched with: the split (2 x 128 x 80 + 2 x 128 x 176)
-    // needs exactly 128 per thread at launch, else the epilogue's increase could never be granted
+    // setmaxnreg.inc draws on the registers the block was launched with: the splits of QRoles need exactly 128
+    // per thread at launch, else the epilogue's increase could never be granted
     cudaFuncAttributes attr;
     if (cudaFuncGetAttributes(&attr, kern) != cudaSuccess || attr.numRegs != 128 ||
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, QPlan<B_MN, QF>::SMEM_BYTES) !=

@@ -8,8 +8,8 @@
 //
 // Per CTA, 16 warps: warp 0 the TMA producer (the x tile by a pair load completing on the leader's barrier; the raw
 // codes, multipliers and panel of this CTA's rows by local loads on a local barrier), warp 1 the leader's MMA issuer,
-// warps 2-7 converters (this CTA's B rows -> bf16, 128-byte swizzle; arrivals on the leader's barrier), warps 8-15
-// the epilogue of this CTA's 128 rows. Registers as in the one-CTA quantised kernel (setmaxnreg 80 / 176).
+// warps 2-11 converters (this CTA's B rows -> bf16, 128-byte swizzle; arrivals on the leader's barrier), warps 12-15
+// the epilogue of this CTA's 128 rows. Registers as in the one-CTA quantised kernel (setmaxnreg 112 / 176).
 
 template <bool LORA, int QF>
 struct QPairPlan {
@@ -266,47 +266,18 @@ __device__ __forceinline__ void qpair_mainloop_roles(const QPairMaps& m, const P
       const int nb = u % p.nblocks;
       const QPairRows rows = qpair_rows<LORA, EPI>(p, nb, rank);
       const int conv_rows = rows.n1 + rows.n2;
-      // this thread's B row: its validity (rows past the stack's end are zero-filled)
-      const int r = ct;
-      const bool mine = r < conv_rows;
-      const bool valid = mine && (r < rows.n1 ? r < rows.lim1 : r - rows.n1 < rows.lim2);
+      // the validity of B row r (rows past the stack's end are zero-filled)
+      auto valid = [&](int r) { return r < rows.n1 ? r < rows.lim1 : r - rows.n1 < rows.lim2; };
       for (int kb = 0; kb < p.kblocks; ++kb) {
         if (!mbar_wait(bar_fullr(s1), ph1) || !mbar_wait(bar_empty2(s2), ph2 ^ 1)) { ok = false; break; }
         const uint8_t* st1 = smem + QP::OFF_R1 + s1 * QP::S1_BYTES;
         uint8_t* bdst = smem + QP::OFF_R2 + s2 * QP::B_BYTES;
-        if (mine) {
-          const uint8_t* src = st1 + QP::OFF_RAW + r * QP::RAW_ROW;
-          const uint32_t rsw = QF == QF_NF4 ? ((r >> 2) & 1) : ((r >> 1) & 3);
-          const float mlt = QF == QF_E4M3 ? 1.0f : reinterpret_cast<const float*>(st1 + QP::OFF_MULT)[r];
-          uint4 o[8];
-          if (!valid) {
-#pragma unroll
-            for (int c = 0; c < 8; ++c) o[c] = make_uint4(0u, 0u, 0u, 0u);
-          } else if (QF == QF_NF4) {
-            const uint4 w0 = *reinterpret_cast<const uint4*>(src + ((0u ^ rsw) << 4));
-            const uint4 w1 = *reinterpret_cast<const uint4*>(src + ((1u ^ rsw) << 4));
-            const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-            for (int c = 0; c < 8; ++c) o[c] = nf4_chunk(w[c], mlt, lv);
-          } else {
-            const __nv_bfloat162 m2 = __float2bfloat162_rn(mlt);
-#pragma unroll
-            for (int c = 0; c < 8; c += 2) {
-              const uint4 w = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c >> 1) ^ rsw) << 4));
-              o[c] = e4m3_chunk<QF>(make_uint2(w.x, w.y), m2);
-              o[c + 1] = e4m3_chunk<QF>(make_uint2(w.z, w.w), m2);
-            }
-          }
-          uint8_t* out_row = bdst + r * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(out_row + ((static_cast<uint32_t>(c) ^ static_cast<uint32_t>(r & 7)) << 4)) =
-                o[c];
-        }
+        convert_tasks<QF, QP::B_ROWS, QRoles<EPI, QF>::CONV_THREADS>(ct, conv_rows, st1 + QP::OFF_RAW,
+                                      reinterpret_cast<const float*>(st1 + QP::OFF_MULT), bdst, lv, valid);
         if (LORA && rank == 1) {  // the panel: B rows 88..103 of the second CTA, verbatim (same swizzle phase)
           const uint4* ps = reinterpret_cast<const uint4*>(st1 + QP::OFF_PANEL);
           uint4* pd = reinterpret_cast<uint4*>(bdst + 88 * 128);
-          for (int i = ct; i < QP::PANEL_BYTES / 16; i += Q_CONV_THREADS) pd[i] = ps[i];
+          for (int i = ct; i < QP::PANEL_BYTES / 16; i += QRoles<EPI, QF>::CONV_THREADS) pd[i] = ps[i];
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -351,10 +322,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Q_THREADS, 1)
     for (int s = 0; s < S1; ++s) {
       mbar_init(bar0 + 8u * s, 1);                      // x tiles (leader's)
       mbar_init(bar0 + 8u * (S1 + s), 1);               // codes, multipliers, panel (local)
-      mbar_init(bar0 + 8u * (2 * S1 + s), Q_CONV_WARPS + 1);  // the converters and the pair's MMAs
+      mbar_init(bar0 + 8u * (2 * S1 + s), QRoles<EPI, QF>::CONV_WARPS + 1);  // the converters and the pair's MMAs
     }
     for (int s = 0; s < S2; ++s) {
-      mbar_init(bar0 + 8u * (3 * S1 + s), 2 * Q_CONV_WARPS);  // both CTAs' converters (leader's)
+      mbar_init(bar0 + 8u * (3 * S1 + s), 2 * QRoles<EPI, QF>::CONV_WARPS);  // both CTAs' converters (leader's)
       mbar_init(bar0 + 8u * (3 * S1 + S2 + s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -379,20 +350,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Q_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int total = (*p.tiles) * p.nblocks;
 
-  if (warp < Q_EPI_WARP0) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
+  static_assert(QRoles<EPI, QF>::CONV_WARPS == 10, "the pair kernel runs the forward products' roles");
+  if (warp < QRoles<EPI, QF>::EPI_WARP0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 112;");
     qpair_mainloop_roles<LORA, EPI, QF>(m, p, smem, sbase, tmem_base, total, warp, lane, rank, pair_id, pairs);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 176;");
     const int qd = warp & 3;
-    const int half = (warp - Q_EPI_WARP0) >> 2;
     int it = 0;
-    for (int u = pair_id; u < total; u += pairs, ++it) {
+    bool ok = true;
+    for (int u = pair_id; u < total && ok; u += pairs, ++it) {
       const int ab = it & 1;
-      if (!epilogue_unit<EPI, LORA, true>(p, u, it, 128 * static_cast<int>(rank), smem + QP::OFF_LOW, tmem_base, qd,
-                                          half, lane, bar1 + 8u * (4 + ab), bar1 + 8u * 6, bar1 + 8u * ab,
-                                          bar1 + 8u * (2 + ab)))
-        break;
+      for (int half = 0; half < 2 && ok; ++half)
+        ok = epilogue_unit<EPI, LORA, true>(p, u, it, 128 * static_cast<int>(rank), smem + QP::OFF_LOW, tmem_base,
+                                            qd, half, lane, bar1 + 8u * (4 + ab), bar1 + 8u * 6, bar1 + 8u * ab,
+                                            bar1 + 8u * (2 + ab));
     }
   }
 
