@@ -229,6 +229,7 @@ def run_meep2b(a):
 
     def step(h, ids, wts, g):
         bucket.zero()
+        h.grad = None  # the input gradient is made fresh each step (in a model it flows on to the previous layer)
         out = mb.routed_forward(ex, h, ids, wts, factors)
         out.backward(g)
         bucket.reduce()

@@ -8,13 +8,18 @@ namespace meep2b {
 
 int bind_stream_device(cudaStream_t stream) {
   int want = -1;
-  if (stream != nullptr) {
-    if (cudaStreamGetDevice(stream, &want) != cudaSuccess) {
-      cudaGetLastError();
-      return MEEP2B_ERR_LAUNCH;
-    }
-  } else {
-    return MEEP2B_OK;
+  if (stream == nullptr) return MEEP2B_OK;
+  // a stream being captured into a CUDA graph is not queried for its device (the query is not a capturable
+  // operation); the caller captures on the current device
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capturing) != cudaSuccess) {
+    cudaGetLastError();
+    return MEEP2B_ERR_LAUNCH;
+  }
+  if (capturing != cudaStreamCaptureStatusNone) return MEEP2B_OK;
+  if (cudaStreamGetDevice(stream, &want) != cudaSuccess) {
+    cudaGetLastError();
+    return MEEP2B_ERR_LAUNCH;
   }
   int cur = -1;
   if (cudaGetDevice(&cur) != cudaSuccess) {
