@@ -100,18 +100,21 @@ class TileMaps:
         return self._maps[block_m]
 
 
-def _pair_tiles(b_mn: int, rows: int, experts: int, k: int, adapters: bool, quantised: bool = False) -> bool:
+def _pair_tiles(b_mn: int, rows: int, experts: int, k: int, adapters: bool, quant_kind=None) -> bool:
     """Whether a product runs on CTA pairs (tiles of 256 rows): enough rows per expert on average that the wider
     tiles waste little, and a long enough contraction (k >= 1024) that the pair's cross-CTA hand-offs at the end
     of each tile stay hidden. A stack read MN-major (the input gradient) goes to pairs only without adapters: its
     rank panel arrives as a separate 32-column atom of which the MMA uses 8, and on B200 the one-CTA kernel is
-    measured faster for it. A quantised stack (dequantised in shared memory) stays on one CTA: its converters'
-    per-k-step latency bounds both forms alike and the pair adds its cross-CTA hand-offs (measured slower, e.g.
-    370 against 663 TFLOP/s for an e4m3 gate/up stack at config-2 size). MEEP2B_PAIR=0 or 1 overrides."""
+    measured faster for it. A quantised stack (quant_kind, dequantised in shared memory) goes to pairs when it is
+    NF4, at any k: each SM then converts half of the stack tile, which is what bounds the NF4 products (measured
+    ~1.5x the one-CTA rate at config-2 size); e4m3 stacks stay on one CTA (the two forms measured alike). MN-major
+    quantised products have no pair form. MEEP2B_PAIR=0 or 1 overrides."""
     forced = os.environ.get("MEEP2B_PAIR")
     if forced in ("0", "1"):
         return forced == "1"
-    if quantised or (b_mn != 0 and adapters):
+    if quant_kind is not None:
+        return quant_kind == _lib.NF4 and b_mn == 0 and rows >= 384 * experts
+    if b_mn != 0 and adapters:
         return False
     return rows >= 384 * experts and k >= 1024
 
@@ -305,7 +308,8 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
     if tiles is None:
         tiles = TileMaps(offsets, rows)
     pair_ok = (x_rows is None or b_mn == 0) and (not quant or b_mn == 0)  # quantised pairs: K-major only
-    block_m = 256 if pair_ok and _pair_tiles(b_mn, rows, experts, K, adapters is not None, quant) else 128
+    block_m = 256 if pair_ok and _pair_tiles(b_mn, rows, experts, K, adapters is not None,
+                                             weight.kind if quant else None) else 128
     tmap = tiles.get(block_m)
     panel = up = None
     if adapters is not None:

@@ -24,7 +24,8 @@ struct QPairPlan {
   static constexpr int S1_BYTES = ((OFF_MULT + MULT_BYTES + 1023) / 1024) * 1024;
   static constexpr int B_BYTES = PAIR_B_ROWS * BK * 2;             // 104 rows of 128 bytes (13 KB)
   static constexpr int U_BYTES_P = 4096;
-  static constexpr int S2 = 4;
+  static constexpr int S2 = 6;
+  static constexpr int FWD_BATCH = 1;  // converted stages the forwarder waits for before passing them on (measured best)
   static constexpr int BUDGET = 232448 - 1024 - 1024 - 1024;
   static constexpr int S1_FIT = (BUDGET - S2 * B_BYTES - U_BYTES_P - LOW_BYTES) / S1_BYTES;
   static constexpr int S1 = S1_FIT > 6 ? 6 : S1_FIT;
@@ -34,7 +35,7 @@ struct QPairPlan {
   static constexpr int OFF_LOW = OFF_U + U_BYTES_P;
   static constexpr int OFF_LUT = OFF_LOW + LOW_BYTES;
   static constexpr int OFF_BAR = OFF_LUT + 1024;
-  static constexpr int NUM_BARS = 3 * S1 + 2 * S2 + 10;
+  static constexpr int NUM_BARS = 3 * S1 + 3 * S2 + 10;
   static constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;
   static_assert(S1 >= 3, "the quantised pair ring needs three stages");
@@ -105,6 +106,7 @@ __device__ __forceinline__ void qpair_mainloop_roles(const QPairMaps& m, const P
   auto bar_full2 = [&](int s) { return bar0 + 8u * (3 * S1 + s); };  // leader's: both halves converted
   auto bar_empty2 = [&](int s) { return bar0 + 8u * (3 * S1 + S2 + s); };
   const uint32_t bar1 = bar0 + 8u * (3 * S1 + 2 * S2);
+  auto bar_conv = [&](int s) { return bar1 + 8u * (10 + s); };  // second CTA: its own converters done (local)
   auto bar_tfull = [&](int b) { return bar1 + 8u * b; };
   auto bar_tempty = [&](int b) { return bar1 + 8u * (2 + b); };
   auto bar_lowfull = [&](int b) { return bar1 + 8u * (4 + b); };
@@ -183,6 +185,53 @@ __device__ __forceinline__ void qpair_mainloop_roles(const QPairMaps& m, const P
           mbar_wait_drain(bar_fullr(s), last_parity[s]);
           if (rank == 0) mbar_wait_drain(bar_fulla(s), last_parity[s]);
         }
+      }
+    }
+  } else if (warp == 1 && rank == 1) {
+    // ------------------------------------------------------------------------------------------ forwarder
+    // The second CTA's converter warps arrive on a local barrier (a release at CTA scope); this thread passes the
+    // completed stages on to the leader's barriers in batches, under one cluster-scope fence followed by relaxed
+    // arrives (a release pattern per arrive). A cluster-scope release from every converter warp, or one per stage,
+    // stalls on the memory barrier it implies (measured: the pair's rate rose from 390 to ~600 TFLOP/s with e4m3
+    // codes as the per-warp releases became batched ones).
+    if (lane == 0) {
+      const int units = pair_id < total ? (total - 1 - pair_id) / pairs + 1 : 0;
+      const int64_t stages = static_cast<int64_t>(units) * p.kblocks;
+      int s2 = 0;
+      uint32_t ph2 = 0;
+      bool ok = true;
+      for (int64_t done = 0; done < stages && ok;) {
+        // wait for a batch of stages (fewer at the end), then take any further ones already converted; each is
+        // observed before the arrives below
+        const int batch = static_cast<int>(stages - done < QP::FWD_BATCH ? stages - done : QP::FWD_BATCH);
+        int n = 0;
+        int t = s2;
+        uint32_t pt = ph2;
+        while (n < S2 && done + n < stages) {
+          if (n < batch) {
+            if (!mbar_wait(bar_conv(t), pt)) {
+              ok = false;
+              break;
+            }
+          } else if (!mbar_test(bar_conv(t), pt)) {
+            break;
+          }
+          ++n;
+          if (++t == S2) {
+            t = 0;
+            pt ^= 1;
+          }
+        }
+        if (!ok) break;
+        fence_cluster();
+        for (int i = 0; i < n; ++i) {
+          mbar_arrive_remote_relaxed(bar_full2(s2), 0);
+          if (++s2 == S2) {
+            s2 = 0;
+            ph2 ^= 1;
+          }
+        }
+        done += n;
       }
     }
   } else if (warp == 1) {
@@ -282,11 +331,7 @@ __device__ __forceinline__ void qpair_mainloop_roles(const QPairMaps& m, const P
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (rank == 0) {
-            mbar_arrive(bar_full2(s2));
-          } else {
-            mbar_arrive_remote(bar_full2(s2), 0);
-          }
+          mbar_arrive(rank == 0 ? bar_full2(s2) : bar_conv(s2));
           mbar_arrive(bar_empty1(s1));
         }
         if (++s1 == S1) {
@@ -325,8 +370,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Q_THREADS, 1)
       mbar_init(bar0 + 8u * (2 * S1 + s), QRoles<EPI, QF>::CONV_WARPS + 1);  // the converters and the pair's MMAs
     }
     for (int s = 0; s < S2; ++s) {
-      mbar_init(bar0 + 8u * (3 * S1 + s), 2 * QRoles<EPI, QF>::CONV_WARPS);  // both CTAs' converters (leader's)
+      // the leader's converter warps and the second CTA's forwarder (leader's barrier)
+      mbar_init(bar0 + 8u * (3 * S1 + s), QRoles<EPI, QF>::CONV_WARPS + 1);
       mbar_init(bar0 + 8u * (3 * S1 + S2 + s), 1);
+      mbar_init(bar1 + 8u * (10 + s), QRoles<EPI, QF>::CONV_WARPS);  // the second CTA's converter warps (local)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar1 + 8u * b, 1);

@@ -23,3 +23,23 @@ def test_quantised_stacks_are_fused_only_with_whole_64_blocks():
     assert _grouped.QuantStack.from_fp8(ok, torch.ones(2, 2, 4)).grid == (2, 4)  # 64 x 64 blocks
     assert _grouped.QuantStack.from_fp8(ok, torch.ones(2, 2, 8)) is None  # 32-column blocks
     assert _grouped.QuantStack.from_fp8(torch.zeros(2, 80, 256, dtype=torch.float8_e4m3fn), torch.ones(2)) is None
+
+
+def test_the_tile_kernel_choice(monkeypatch):
+    """CTA pairs for long K-major bf16 products with many rows per expert, for MN-major ones only without
+    adapters; for quantised stacks only NF4 K-major (at any k); MEEP2B_PAIR overrides."""
+    monkeypatch.delenv("MEEP2B_PAIR", raising=False)
+    rows, experts = 131072, 128  # 1024 rows per expert
+    assert _grouped._pair_tiles(0, rows, experts, 2048, True)
+    assert not _grouped._pair_tiles(0, rows, experts, 768, True)  # short contraction
+    assert not _grouped._pair_tiles(0, 16384, experts, 2048, True)  # 128 rows per expert
+    assert not _grouped._pair_tiles(1, rows, experts, 2048, True)
+    assert _grouped._pair_tiles(1, rows, experts, 2048, False)
+    assert _grouped._pair_tiles(0, rows, experts, 768, True, _lib.NF4)
+    assert not _grouped._pair_tiles(1, rows, experts, 2048, False, _lib.NF4)
+    assert not _grouped._pair_tiles(0, rows, experts, 2048, True, _lib.E4M3_BLOCKS)
+    assert not _grouped._pair_tiles(0, rows, experts, 2048, True, _lib.E4M3)
+    monkeypatch.setenv("MEEP2B_PAIR", "1")
+    assert _grouped._pair_tiles(0, 16384, experts, 768, True, _lib.E4M3)
+    monkeypatch.setenv("MEEP2B_PAIR", "0")
+    assert not _grouped._pair_tiles(0, rows, experts, 2048, True)
