@@ -421,77 +421,35 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
   return true;
 }
 
-// The x tile of a gathered product (x row i of the tile = row src of a token-major tensor: the routed rows read
-// where they are, without an expert-sorted copy), copied by two warps, warp gw taking rows 64 gw .. 64 gw + 63:
-// 64 columns from k0 as 16-byte cp.async copies into the 128-byte-swizzled layout a TMA load of the tile gives
-// (columns past K read zero). Eight lanes cover one row's 128 bytes, so each instruction moves four whole rows
-// (coalesced line requests): lane l copies chunk l % 8 of rows 64 gw + 4 i + l / 8, i = 0..15, sources in src[i].
-constexpr int GATHER_WARP0 = 2;  // warps 2 and 3 (idle otherwise)
-__device__ __forceinline__ void gather_x_stage(uint32_t a_dst, const __nv_bfloat16* src_base, int64_t ld, int K,
-                                               int k0, const int (&src)[16], int gw, int lane) {
-  const int c = lane & 7, rg = lane >> 3;
-  const int k = k0 + 8 * c;
-  const bool ok = k < K;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int r = 64 * gw + 4 * i + rg;
-    const __nv_bfloat16* row = src_base + static_cast<int64_t>(src[i]) * ld;
-    const uint32_t dst = a_dst + r * 128 + ((static_cast<uint32_t>(c) ^ static_cast<uint32_t>(r & 7)) << 4);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(ok ? row + k : src_base),
-                 "r"(ok ? 16 : 0)
-                 : "memory");
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-// The source rows of the tile rows this lane copies; rows past the product's end read row 0 (the epilogue drops
-// them).
-__device__ __forceinline__ void gather_rows_of_tile(const int32_t* a_rows, int rows, int row0, int gw, int lane,
-                                                    int (&src)[16]) {
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int r = row0 + 64 * gw + 4 * i + (lane >> 3);
-    src[i] = r < rows ? __ldg(a_rows + r) : 0;
-  }
-}
-
-// After this lane's copies of the oldest stage in flight (all but the PENDING newest groups) have landed: make the
-// warp's writes visible to the tensor cores (async proxy) and arrive once, for the warp, on that stage's barrier.
-template <int PENDING>
-__device__ __forceinline__ void gather_signal(uint32_t bar, int lane, bool to_leader) {
-  asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory");
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0) {
-    if (to_leader) {
-      mbar_arrive_remote(bar, 0);
-    } else {
-      mbar_arrive(bar);
-    }
-  }
-}
-
-// Warps 2-3 of a gathered product: the x rows of every k-step, in the producer's stage order, into the x ring at
-// a_ring (stage s at a_ring + s * A_BYTES). The stage's full barrier (the pair leader's, to_leader) gets one arrival
-// per warp once the warp's copies have landed; a ring slot is refilled after its empty barrier completes.
+// Gathered x rows (products whose x rows are read where they are, from a token-major tensor through a_rows,
+// without an expert-sorted copy): warp GATHER_WARP loads the x tile of every k-step by TMA gather4 loads (four rows
+// of 64 columns each, at any rows of the source tensor), lane l taking tile rows 4 l .. 4 l + 3, into the x ring
+// at a_ring (stage s at a_ring + s * A_BYTES) in the 128-byte-swizzled layout a tile load gives. The loads
+// complete on the stage's full barrier (the pair leader's for a pair), whose bytes the producer announces with the
+// stack's; a ring slot is refilled after its empty barrier completes. Tile rows past the product's end read row 0
+// (the epilogue drops them).
+constexpr int GATHER_WARP = 2;  // idle otherwise
 template <int STAGES>
-__device__ __forceinline__ void gather_role(const Params& p, int first_unit, int unit_stride, int total, int row_shift,
-                                            uint32_t a_ring, uint32_t bar0, int gw, int lane, bool to_leader) {
-  int stage = 0, sig_stage = 0, in_flight = 0;
+__device__ __forceinline__ void gather_role(const Params& p, const CUtensorMap* tm_src, int first_unit,
+                                            int unit_stride, int total, int row_shift, uint32_t a_ring, uint32_t bar0,
+                                            int lane, bool pair) {
+  int stage = 0;
   uint32_t phase = 0;
   bool ok = true;
   for (int u = first_unit; u < total && ok; u += unit_stride) {
     const int t = u / p.nblocks;
-    int src[16];
-    gather_rows_of_tile(p.a_rows, p.rows, p.tile_row[t] + row_shift, gw, lane, src);
+    const int r = p.tile_row[t] + row_shift + 4 * lane;
+    int src[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) src[j] = r + j < p.rows ? __ldg(p.a_rows + r + j) : 0;
     for (int kb = 0; kb < p.kblocks; ++kb) {
       ok = __all_sync(0xffffffffu, mbar_wait(bar0 + 8u * (STAGES + stage), phase ^ 1));
       if (!ok) break;
-      gather_x_stage(a_ring + stage * A_BYTES, p.a_src, p.lda, p.K, kb * BK, src, gw, lane);
-      if (++in_flight > STAGES - 1) {
-        gather_signal<STAGES - 1>(bar0 + 8u * sig_stage, lane, to_leader);
-        sig_stage = sig_stage + 1 == STAGES ? 0 : sig_stage + 1;
-        --in_flight;
+      const uint32_t dst = a_ring + stage * A_BYTES + lane * 512;
+      if (pair) {
+        tma_gather4_pair(dst, tm_src, map_to_rank(bar0 + 8u * stage, 0), kb * BK, src[0], src[1], src[2], src[3]);
+      } else {
+        tma_gather4(dst, tm_src, bar0 + 8u * stage, kb * BK, src[0], src[1], src[2], src[3]);
       }
       if (++stage == STAGES) {
         stage = 0;
@@ -499,18 +457,10 @@ __device__ __forceinline__ void gather_role(const Params& p, int first_unit, int
       }
     }
   }
-  if (in_flight > 0) {  // the last stages (also on the way out of a failed run: the copies land before exit)
-    gather_signal<0>(bar0 + 8u * sig_stage, lane, to_leader);
-    for (int i = 1; i < in_flight; ++i) {
-      sig_stage = sig_stage + 1 == STAGES ? 0 : sig_stage + 1;
-      if (lane == 0) {
-        if (to_leader) {
-          mbar_arrive_remote(bar0 + 8u * sig_stage, 0);
-        } else {
-          mbar_arrive(bar0 + 8u * sig_stage);
-        }
-      }
-    }
+  if (!ok) {
+    // another role gave up after a bounded wait (its barrier may never complete): let this warp's last loads land
+    // before the CTA's shared memory is released
+    for (int i = 0; i < 64; ++i) __nanosleep(1000);
   }
 }
 
@@ -540,7 +490,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full(s), GATHER ? 3 : 1);  // gathered: the stack's TMA bytes, then the two gather warps
+      mbar_init(bar_full(s), 1);
       mbar_init(bar_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -567,17 +517,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------------------ TMA producer
-    // (gathered x: warps 2-3 copy the x rows; this thread loads the stack and the adapters)
+    // (gathered x: the gather warp loads the x rows; this thread announces their bytes with the stack's)
     if (lane == 0) {
       const bool lead = true;
-      if (!GATHER) tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_x);
       tma_prefetch_desc(&tm_w);
       if (LORA) {
         tma_prefetch_desc(&tm_p);
         tma_prefetch_desc(&tm_u);
       }
       constexpr uint32_t B_TX = 64 * BN * 2 + (LORA ? (B_MN ? 64 * 64 * 2 : RP * 64 * 2) : 0);
-      constexpr uint32_t STAGE_TX = (GATHER ? 0 : A_BYTES) + B_TX;
+      constexpr uint32_t STAGE_TX = A_BYTES + B_TX;
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool { return mbar_wait(bar, parity); };
       int stage = 0;
       uint32_t phase = 0;
@@ -655,9 +605,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (issued[s]) mbar_wait_drain(bar_full(s), last_parity[s]);
       }
     }
-  } else if (GATHER && (warp == GATHER_WARP0 || warp == GATHER_WARP0 + 1)) {
+  } else if (GATHER && warp == GATHER_WARP) {
     // ------------------------------------------------------------------------------------------ x-row gather
-    gather_role<STAGES>(p, blockIdx.x, gridDim.x, total, 0, sbase + P::OFF_A, bar0, warp - GATHER_WARP0, lane, false);
+    gather_role<STAGES>(p, &tm_x, blockIdx.x, gridDim.x, total, 0, sbase + P::OFF_A, bar0, lane, false);
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -825,7 +775,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PP::STAGES; ++s) {
-      mbar_init(bar_full(s), GATHER ? 5 : 1);  // gathered: the TMA bytes, then the two gather warps of each CTA
+      mbar_init(bar_full(s), 1);
       mbar_init(bar_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -853,11 +803,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const bool lead = true;
-      if (!GATHER) tma_prefetch_desc(&m.x);
+      tma_prefetch_desc(&m.x);
       // K-major: with the panel the 208 B rows split 104 / 104 (the second CTA's last 16 are the panel), without it
       // 96 / 96. MN-major: 96 stack columns per CTA, plus 8 panel columns (one 16-column atom) with the adapters.
       constexpr uint32_t CTA_TX =
-          (GATHER ? 0 : A_BYTES) + (B_MN ? 3 * 64 * 64 + (LORA ? 64 * 64 : 0) : (LORA ? PAIR_B_ROWS : BN / 2) * 128);
+          A_BYTES + (B_MN ? 3 * 64 * 64 + (LORA ? 64 * 64 : 0) : (LORA ? PAIR_B_ROWS : BN / 2) * 128);
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool { return mbar_wait(bar, parity); };
       int stage = 0;
       uint32_t phase = 0;
@@ -945,10 +895,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (issued[s] && rank == 0) mbar_wait_drain(bar_full(s), last_parity[s]);
       }
     }
-  } else if (GATHER && (warp == GATHER_WARP0 || warp == GATHER_WARP0 + 1)) {
+  } else if (GATHER && warp == GATHER_WARP) {
     // ------------------------------------------------------------------------------------------ x-row gather
-    gather_role<PP::STAGES>(p, pair_id, pairs, total, 128 * static_cast<int>(rank), sbase, bar0,
-                            warp - GATHER_WARP0, lane, rank != 0);
+    gather_role<PP::STAGES>(p, &m.x, pair_id, pairs, total, 128 * static_cast<int>(rank), sbase, bar0, lane, true);
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && rank == 0) {
@@ -987,8 +936,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + ab * ACC_STRIDE;
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          // gathered x: the second CTA's rows are generic-proxy writes released at cluster scope
-          if (!(GATHER ? mbar_wait_cluster(bar_full(stage), phase) : mbar_wait(bar_full(stage), phase))) {
+          if (!mbar_wait(bar_full(stage), phase)) {
             ok = false;
             break;
           }
@@ -1120,7 +1068,7 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   {
     const uint64_t dims[2] = {K, x_rows_in_map};
     const uint64_t strides[1] = {static_cast<uint64_t>(a->ldx) * 2};
-    const uint32_t box[2] = {64, 128};
+    const uint32_t box[2] = {64, gather ? 1u : 128u};  // gathered rows: tile::gather4 loads, one-row boxes
     MEEP2B_TRY(encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->x, dims, strides, box,
                             CU_TENSOR_MAP_SWIZZLE_128B));
   }
