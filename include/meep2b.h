@@ -240,6 +240,18 @@ int meep2b_nf4_dequantize(const uint8_t* packed, const uint8_t* absmax, const fl
                           const float* offset, int32_t blocksize, int32_t blocksize2, int64_t n, float* absmax_out,
                           void* out, void* stream);
 
+/* ------------------------------------------------------------------------------------------------ merged save */
+
+/* _save._merged_stack (_save.py:79-95): out[e] = dtype(W_e + scaling * (lhs_e @ rhs_e)) for every expert, float32
+ * arithmetic, the stack's own layout: W (experts, rows, cols) in f32, bf16 or e4m3 (then dequantised as
+ * _fp8.dequantize_stack does for float32, f32(code) * scale[e]); lhs (experts, rows, rank) and rhs
+ * (experts, rank, cols) float32, contiguous (rank <= 128), the factors of _moe._delta_factors (_moe.py:150-163),
+ * or rank 0 and null factors for the stack alone (out = dtype(W_e)); out in f32 or bf16 (round to nearest even).
+ * The rank products are summed in order, with fused multiply-adds. */
+int meep2b_merge_stack(const void* weight, int32_t weight_dtype, const float* scale, const float* lhs,
+                       const float* rhs, int32_t rank, float scaling, int64_t experts, int64_t rows, int64_t cols,
+                       void* out, int32_t out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

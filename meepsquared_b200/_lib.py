@@ -57,6 +57,8 @@ _SIGNATURES = {
     "meep2b_nf4_absmax": (ctypes.c_int, [_p, _p, _p, _p, _i32, _i64, _p, _p]),
     "meep2b_quant_multipliers": (ctypes.c_int, [_i32, _p, _i32, _i64, _i64, _i32, _i32, _p, _p]),
     "meep2b_nf4_dequantize": (ctypes.c_int, [_p, _p, _p, _p, _p, _i32, _i32, _i64, _p, _p, _p]),
+    "meep2b_merge_stack": (ctypes.c_int, [_p, _i32, _p, _p, _p, _i32, ctypes.c_float, _i64, _i64, _i64, _p, _i32,
+                                          _p]),
 }
 
 _lib = None
@@ -109,6 +111,7 @@ KERNELS_PER_CALL = {
     "meep2b_unpermute": 1, "meep2b_unpermute_backward": 1, "meep2b_tile_map": 1, "meep2b_grouped_product": 1,
     "meep2b_grouped_reduce": 1, "meep2b_grouped_reduce_rows": 1, "meep2b_fp8_stack_dequantize": 1,
     "meep2b_fp8_block_dequantize": 1, "meep2b_nf4_dequantize": 2, "meep2b_nf4_absmax": 1,
+    "meep2b_merge_stack": 1,
     "meep2b_quant_multipliers": 1,
 }
 launches = {}

@@ -4,3 +4,4 @@
 #include "grouped_gemm.cu"
 #include "reduce.cu"
 #include "quant.cu"
+#include "merge.cu"

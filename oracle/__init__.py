@@ -15,7 +15,8 @@ MoE-LoRA path (thinkube/meepsquared):
   ``meepsquared/_fp8.py:122-134``, the 128x128 block FP8 of
   ``meepsquared/_vendor/axolotl/quantize.py:131-157,238-263`` and the NF4
   double quantisation that ``quantize.py:52-101`` hands to bitsandbytes 0.50.2;
-* ``layer``    -- the whole routed layer, forward and backward, in float32.
+* ``layer``    -- the whole routed layer, forward and backward, in float32;
+* ``merge``    -- the merged save of an expert stack, ``meepsquared/_save.py:79-95``.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 ``--impl reference`` legs of ``bench.py`` may import this package, and only as

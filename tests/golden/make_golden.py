@@ -207,6 +207,41 @@ def grouped_case(grouped):
     return out
 
 
+def merged_stacks(root, fp8):
+    """_save._merged_stack (_save.py:79-95) on expert stacks with a PEFT-shaped stand-in for the wrapper (the
+    attributes _moe._delta_factors and _save._the_adapter read): bf16 and FP8 stacks, both layouts, bf16 and float32
+    outputs."""
+    save = importlib.import_module("meepsquared._save")
+    out = {}
+    g = torch.Generator().manual_seed(6)
+    E, rows, cols, rank = 3, 40, 72, 8
+    for swapped in (True, False):  # True: the stack is (experts, out, in); False: (experts, in, out)
+        p = "n_" if swapped else "t_"
+        a = layer_inputs.bf16_valued(torch.randn(E * rank, cols if swapped else rows, generator=g) * 0.2)
+        b = layer_inputs.bf16_valued(torch.randn(rows if swapped else cols, rank * E, generator=g) * 0.2)
+        wrapper = types.SimpleNamespace(active_adapters=["default"], use_dora={}, num_experts=E,
+                                        _did_swap_in_out_features=swapped, scaling={"default": 1.5},
+                                        lora_A={"default": types.SimpleNamespace(weight=a)},
+                                        lora_B={"default": types.SimpleNamespace(weight=b)})
+        stack = layer_inputs.bf16_valued(torch.randn(E, rows, cols, generator=g) * 0.05).to(torch.bfloat16)
+        moe = importlib.import_module("meepsquared._moe")
+        lhs, rhs, scaling = moe._delta_factors(wrapper, "default", torch.float32)
+        out[p + "lhs"], out[p + "rhs"] = lhs.contiguous().numpy(), rhs.contiguous().numpy()
+        out[p + "scaling"] = np.array(scaling, dtype=np.float64)
+        experts = types.SimpleNamespace(stack=stack)
+        out[p + "stack"] = bits(stack)
+        out[p + "merged_bf16"] = bits(save._merged_stack(experts, "stack", wrapper, torch.bfloat16))
+        out[p + "merged_f32"] = save._merged_stack(experts, "stack", wrapper, torch.float32).numpy()
+        w8, scale = fp8.quantize_stack(stack)
+        experts8 = types.SimpleNamespace(stack=w8)
+        setattr(experts8, "stack" + fp8.STACK_SCALE, scale)
+        out[p + "codes"], out[p + "scale"] = w8.view(torch.uint8).numpy(), scale.numpy()
+        out[p + "fp8_merged_f32"] = save._merged_stack(experts8, "stack", wrapper, torch.float32).numpy()
+        out[p + "fp8_merged_bf16"] = bits(save._merged_stack(experts8, "stack", wrapper, torch.bfloat16))
+        out[p + "fp8_alone_f32"] = save._merged_stack(experts8, "stack", None, torch.float32).numpy()
+    return out
+
+
 def main(root):
     moe, grouped, fp8 = import_reference(root)
     q = import_quantize(root)
@@ -226,6 +261,7 @@ def main(root):
     np.savez_compressed(os.path.join(HERE, "fp8_stack.npz"), **fp8_stacks(fp8))
     np.savez_compressed(os.path.join(HERE, "fp8_block.npz"), **fp8_blocks(q))
     np.savez_compressed(os.path.join(HERE, "grouped.npz"), **grouped_case(grouped))
+    np.savez_compressed(os.path.join(HERE, "merged.npz"), **merged_stacks(root, fp8))
     print("golden vectors written to", HERE)
 
 

@@ -144,3 +144,23 @@ def test_nf4_round_trip_stays_within_the_level_spacing():
     err = np.abs(back.reshape(-1, 64) - w.reshape(-1, 64)).max(axis=1)
     assert np.all(err <= 0.21 * blocks + 1e-6)  # half the widest NF4 gap, plus absmax requantisation
     assert state["packed"].size == w.size // 2 and state["absmax"].size == w.size // 64
+
+
+@pytest.mark.parametrize("prefix", ["n_", "t_"])
+def test_merged_stack_matches_the_reference_merged_save(golden, prefix):
+    """_save._merged_stack (_save.py:79-95): bf16 and FP8 stacks with their adapters merged, float32 and bf16
+    outputs. The oracle's float32 matmul may sum the rank products in another order than torch's bmm: float32
+    results agree to a few ulps, bf16 results bit for bit but for rounding-boundary cases."""
+    from oracle import merge
+
+    g = golden("merged")
+    p = prefix
+    lhs, rhs, s = g[p + "lhs"], g[p + "rhs"], float(g[p + "scaling"])
+    w = quant.bf16_to_f32(g[p + "stack"])
+    np.testing.assert_allclose(merge.merged_stack(w, lhs, rhs, s), g[p + "merged_f32"], rtol=1e-6, atol=1e-7)
+    got = merge.merged_stack(w, lhs, rhs, s, "bf16")
+    assert np.mean(got != g[p + "merged_bf16"]) < 1e-3
+    np.testing.assert_allclose(quant.bf16_to_f32(got), quant.bf16_to_f32(g[p + "merged_bf16"]), rtol=2 ** -7)
+    w8 = merge.dequantized_f32(codes=g[p + "codes"], scale=g[p + "scale"])
+    np.testing.assert_array_equal(w8, g[p + "fp8_alone_f32"])
+    np.testing.assert_allclose(merge.merged_stack(w8, lhs, rhs, s), g[p + "fp8_merged_f32"], rtol=1e-6, atol=1e-7)
