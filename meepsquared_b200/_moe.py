@@ -318,17 +318,104 @@ def _kernel_stack(experts, name):
     return weight.detach(), None
 
 
-def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
-    """The routed layer of a gated experts module with its adapters: _moe._routed_forward's contract.
+class _GatherRows(torch.autograd.Function):
+    """The hidden rows in expert order (selected = hidden[perm // k], sentinel rows zero, _moe.py:80,87); the
+    backward sums the rows' gradients back onto their tokens (the un-permute without weights)."""
 
-    experts: a Transformers experts module (num_experts, has_gate, has_bias, is_transposed, gate_up_proj,
-    down_proj; FP8 stacks with ``<name>_scale_inv`` of one scale per expert or a 128 x 128 block grid; NF4 stacks
-    as an ``_nf4.NF4State`` in the stack's place). factors: {stack name: (lhs, rhs, scaling)} in PEFT's layout.
+    @staticmethod
+    def forward(ctx, hidden, routing, top_k_weights):
+        ctx.routing = routing
+        return gather(hidden, routing, top_k_weights)
+
+    @staticmethod
+    def backward(ctx, grad):
+        return unpermute(grad.contiguous().to(torch.bfloat16), ctx.routing, None), None, None
+
+
+class _Combine(torch.autograd.Function):
+    """out[t] = sum_j w[t, j] * y[row(t, j)] (_moe.py:123-126), sentinel rows contributing nothing; the backward
+    gives the rows' gradients and the routing weights' gradient <g[t], y[row]>."""
+
+    @staticmethod
+    def forward(ctx, y, top_k_weights, routing):
+        y = y.contiguous()
+        ctx.save_for_backward(y)
+        ctx.routing, ctx.weights_dtype = routing, top_k_weights.dtype
+        return unpermute(y, routing, routing.weights_g)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (y,) = ctx.saved_tensors
+        grad = grad.contiguous()
+        if grad.dtype != torch.bfloat16:
+            grad = grad.to(torch.bfloat16)
+        grad_y, grad_w = unpermute_backward(grad, y, ctx.routing)
+        return grad_y, grad_w.to(ctx.weights_dtype), None
+
+
+def _default_swiglu(experts) -> bool:
+    """Whether the module's gate is what the products' SwiGLU epilogues compute: Transformers' default gate
+    (``_default_apply_gate``: the activation of the first half of the gate/up output times the second half) with a
+    SiLU activation, on a gate/up stack stored (experts, 2I, hidden). A module without ``_apply_gate`` or ``act_fn``
+    is taken as that default."""
+    if not experts.has_gate or experts.is_transposed:
+        return False
+    gate = getattr(type(experts), "_apply_gate", None)
+    if gate is not None:
+        try:
+            from transformers.integrations.moe import _default_apply_gate
+        except ImportError:
+            return False
+        if gate is not _default_apply_gate:
+            return False
+    act = getattr(experts, "act_fn", None)
+    return act is None or isinstance(act, torch.nn.SiLU) or type(act).__name__ == "SiLUActivation"
+
+
+def _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors):
+    """The routed layer for modules whose gate the epilogues do not compute (another activation or gating
+    function, an ungated up projection, a transposed stack): the reference's structure (_moe.py:70-126) with every
+    product on the grouped kernels (one autograd node per projection, as lora_linear), the routing, the gather and
+    the weighted un-permute on this package's kernels, and the module's own gate or activation in between."""
+    routing = route(top_k_index, top_k_weights, experts.num_experts)
+    x = _GatherRows.apply(hidden_states.to(torch.bfloat16), routing, top_k_weights)
+    rows = routing.perm.numel()  # rows past the last expert's end are the sentinels (ids >= num_experts)
+    sentinel = (torch.arange(rows, device=x.device) >= routing.offsets[-1].long()).unsqueeze(-1)
+    t = bool(experts.is_transposed)
+
+    def project(x, name, bias_name):
+        stack, scale = _kernel_stack(experts, name)
+        lhs, rhs, scaling = factors.get(name, (None, None, 1.0))
+        cast = lambda f: f.to(torch.bfloat16) if f is not None and f.dtype != torch.bfloat16 else f  # noqa: E731
+        bias = getattr(experts, bias_name) if experts.has_bias else None
+        if bias is not None:
+            bias = bias.detach().to(torch.bfloat16).contiguous()
+        out = _grouped._LoraGroupedProduct.apply(x.to(torch.bfloat16).contiguous(), _stack(stack), scale,
+                                                 routing.offsets, t, cast(lhs), cast(rhs), float(scaling), bias, None)
+        return out.masked_fill(sentinel, 0.0)  # rows past the experts' ends are not written by the products
+
+    if experts.has_gate:
+        h = experts._apply_gate(project(x, "gate_up_proj", "gate_up_proj_bias"))
+    else:
+        h = experts.act_fn(project(x, "up_proj", "up_proj_bias"))
+    y = project(h, "down_proj", "down_proj_bias")
+    return _Combine.apply(y, top_k_weights, routing).to(hidden_states.dtype)
+
+
+def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
+    """The routed layer of an experts module with its adapters: _moe._routed_forward's contract.
+
+    experts: a Transformers experts module (num_experts, has_gate, has_bias, is_transposed, gate_up_proj or
+    up_proj, down_proj; FP8 stacks with ``<name>_scale_inv`` of one scale per expert or a 128 x 128 block grid; NF4
+    stacks as an ``_nf4.NF4State`` in the stack's place). factors: {stack name: (lhs, rhs, scaling)} in PEFT's
+    layout. A gated module with Transformers' default SiLU gate and a gate/up stack stored (experts, 2I, hidden)
+    runs the fused layer (SwiGLU in the products' epilogues, one autograd node); any other module runs the
+    unfused form, its own gate or activation between the products.
     """
-    if not experts.has_gate:
-        raise NotImplementedError("the fused layer needs a gated experts module (gate_up_proj)")
     if not hidden_states.is_cuda:
         raise RuntimeError("the routed layer runs on a CUDA GPU (compute capability 10.0)")
+    if not _default_swiglu(experts):
+        return _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)
     bias1 = experts.gate_up_proj_bias if experts.has_bias else None
     bias2 = experts.down_proj_bias if experts.has_bias else None
     lhs1, rhs1, s1 = factors.get("gate_up_proj", (None, None, 1.0))

@@ -218,3 +218,100 @@ def test_the_layer_step_replays_from_a_cuda_graph_with_the_eager_bits():
     assert torch.equal(hidden.grad, eager["grad_hidden"])
     for n, t in leaves.items():
         assert torch.equal(t.grad, eager[n]), n
+
+
+def torch_routed(inp, act, gated=True):
+    """A float32 torch computation of the reference's routed layer (_moe.py:70-126) per expert, with the gate
+    act(first half) * second half (gated) or act(up) (ungated), its autograd gradients for the layer's inputs."""
+    dev = DEV
+    hidden = inp["hidden"].to(dev).requires_grad_()
+    weights = inp["top_k_weights"].to(dev).requires_grad_()
+    idx = inp["top_k_index"].to(dev)
+    lv = {n: inp[n].to(dev).requires_grad_() for n in ("gate_up_lhs", "gate_up_rhs", "down_lhs", "down_rhs")}
+    s = inp["scaling"]
+    w1 = inp["gate_up"].to(dev) if gated else inp["gate_up"][:, : inp["gate_up"].shape[1] // 2].to(dev)
+    l1 = lv["gate_up_lhs"] if gated else lv["gate_up_lhs"][:, : w1.shape[1]]
+    w2 = inp["down"].to(dev)
+    out = torch.zeros_like(hidden)
+    for e in range(w1.shape[0]):
+        tok, slot = torch.where(idx == e)
+        if tok.numel() == 0:
+            continue
+        x = hidden[tok]
+        p = x @ (w1[e] + s * l1[e] @ lv["gate_up_rhs"][e]).t()
+        if gated:
+            g, u = p.chunk(2, dim=-1)
+            h = act(g) * u
+        else:
+            h = act(p)
+        y = h @ (w2[e] + s * lv["down_lhs"][e] @ lv["down_rhs"][e]).t()
+        out = out.index_add(0, tok, y * weights[tok, slot, None])
+    out.backward(inp["grad"].to(dev))
+    res = {"out": out.detach(), "grad_hidden": hidden.grad, "grad_weights": weights.grad}
+    for n, t in lv.items():
+        res[f"grad_{n}"] = t.grad if gated or n != "gate_up_lhs" else t.grad[:, : w1.shape[1]]
+    return res
+
+
+def run_module(inp, experts, factors):
+    hidden = inp["hidden"].to(DEV, torch.bfloat16).requires_grad_()
+    weights = inp["top_k_weights"].to(DEV).requires_grad_()
+    out = mb.routed_forward(experts, hidden, inp["top_k_index"].to(DEV), weights, factors)
+    out.backward(inp["grad"].to(DEV, torch.bfloat16))
+    res = {"out": out.detach(), "grad_hidden": hidden.grad, "grad_weights": weights.grad}
+    return res
+
+
+class GatedExperts(torch.nn.Module):
+    """A Transformers-style experts module with an activation and, optionally, transposed stacks."""
+
+    def __init__(self, gate_up, down, act, transposed):
+        super().__init__()
+        self.num_experts = gate_up.shape[0]
+        self.has_gate, self.has_bias, self.is_transposed = True, False, transposed
+        if transposed:
+            gate_up, down = gate_up.transpose(1, 2).contiguous(), down.transpose(1, 2).contiguous()
+        self.gate_up_proj = torch.nn.Parameter(gate_up, requires_grad=False)
+        self.down_proj = torch.nn.Parameter(down, requires_grad=False)
+        self.act_fn = act
+
+    def _apply_gate(self, gate_up_out):
+        gate, up = gate_up_out.chunk(2, dim=-1)
+        return self.act_fn(gate) * up
+
+
+@pytest.mark.parametrize("case", ["transposed_silu", "gelu", "ungated_gelu"])
+def test_modules_the_epilogues_do_not_fuse_take_the_unfused_layer(case):
+    """Transposed stacks, another activation (the module's own gate) or an ungated up projection: the products on
+    the grouped kernels, the module's gate in between, against a float32 torch computation of the reference."""
+    inp = layer_inputs.layer(**layer_inputs.CONFIG1)
+    bf = lambda n: inp[n].to(DEV, torch.bfloat16)  # noqa: E731
+    s = inp["scaling"]
+    transposed = case == "transposed_silu"
+    act = torch.nn.SiLU() if transposed else torch.nn.GELU(approximate="tanh")
+    leaves = {n: bf(n).requires_grad_() for n in ("gate_up_lhs", "gate_up_rhs", "down_lhs", "down_rhs")}
+    if case == "ungated_gelu":
+        inter = inp["gate_up"].shape[1] // 2
+        experts = GatedExperts(bf("gate_up")[:, :inter], bf("down"), act, False)
+        experts.has_gate = False
+        experts.up_proj = experts.gate_up_proj
+        del experts.gate_up_proj
+        factors = {"up_proj": (leaves["gate_up_lhs"][:, :inter], leaves["gate_up_rhs"], s),
+                   "down_proj": (leaves["down_lhs"], leaves["down_rhs"], s)}
+    elif transposed:  # delta (in, out) = rhs^T lhs^T
+        experts = GatedExperts(bf("gate_up"), bf("down"), act, True)
+        factors = {"gate_up_proj": (leaves["gate_up_rhs"].transpose(1, 2), leaves["gate_up_lhs"].transpose(1, 2), s),
+                   "down_proj": (leaves["down_rhs"].transpose(1, 2), leaves["down_lhs"].transpose(1, 2), s)}
+    else:
+        experts = GatedExperts(bf("gate_up"), bf("down"), act, False)
+        factors = {"gate_up_proj": (leaves["gate_up_lhs"], leaves["gate_up_rhs"], s),
+                   "down_proj": (leaves["down_lhs"], leaves["down_rhs"], s)}
+    assert not mb._moe._default_swiglu(experts)
+    got = run_module(inp, experts, factors)
+    for n, t in leaves.items():
+        got[f"grad_{n}"] = t.grad if t.grad is not None else torch.zeros_like(t)
+    want = torch_routed(inp, act, gated=case != "ungated_gelu")
+    if case == "ungated_gelu":
+        got["grad_gate_up_lhs"] = got["grad_gate_up_lhs"][:, : inp["gate_up"].shape[1] // 2]
+    check_against(got, {k: v.cpu().numpy() for k, v in want.items()}, scaled=True)
+

@@ -43,3 +43,40 @@ def test_the_tile_kernel_choice(monkeypatch):
     assert _grouped._pair_tiles(0, 16384, experts, 768, True, _lib.E4M3)
     monkeypatch.setenv("MEEP2B_PAIR", "0")
     assert not _grouped._pair_tiles(0, rows, experts, 2048, True)
+
+
+def test_only_the_default_silu_gate_on_a_k_major_stack_is_fused():
+    """The fused layer computes Transformers' default gate with SiLU (the epilogues' SwiGLU) on a gate/up stack
+    stored (experts, 2I, hidden); another activation, gating function, an ungated module or a transposed stack takes
+    the unfused layer."""
+    from transformers.activations import ACT2FN
+    from transformers.integrations.moe import _default_apply_gate
+
+    from meepsquared_b200 import _moe
+
+    class Experts(torch.nn.Module):
+        _apply_gate = _default_apply_gate
+
+        def __init__(self):
+            super().__init__()
+            self.num_experts, self.has_gate, self.has_bias, self.is_transposed = 2, True, False, False
+            self.act_fn = ACT2FN["silu"]
+
+    experts = Experts()
+    assert _moe._default_swiglu(experts)
+    experts.act_fn = torch.nn.SiLU()
+    assert _moe._default_swiglu(experts)
+    experts.act_fn = ACT2FN["gelu"]
+    assert not _moe._default_swiglu(experts)
+    experts.act_fn = ACT2FN["silu"]
+    experts.is_transposed = True
+    assert not _moe._default_swiglu(experts)
+    experts.is_transposed, experts.has_gate = False, False
+    assert not _moe._default_swiglu(experts)
+
+    class Custom(Experts):
+        def _apply_gate(self, gate_up_out):
+            gate, up = gate_up_out.chunk(2, dim=-1)
+            return self.act_fn(gate.clamp(max=7.0)) * up
+
+    assert not _moe._default_swiglu(Custom())
