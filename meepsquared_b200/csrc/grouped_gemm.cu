@@ -68,10 +68,8 @@ struct Params {
   __nv_bfloat16* low;
   __nv_bfloat16* aux;
   bool v8;  // out, aux and low rows 32-byte aligned: whole-sector stores
-  // gathered x (GATHER kernels): tile row i reads row a_rows[i] of a_src (row stride lda)
+  // gathered x (GATHER kernels): tile row i is row a_rows[i] of the tensor the x map addresses
   const int32_t* a_rows;
-  const __nv_bfloat16* a_src;
-  int64_t lda;
   // dSwiGLU with the un-permute's backward folded in: the product is scaled by row_scale[row] (the routing weight)
   // and, when w_grad is set, w_grad[row * w_ld + block] = <unscaled product, h> over each 96-column block
   const float* row_scale;
@@ -1138,8 +1136,6 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   prm.aux = static_cast<__nv_bfloat16*>(a->aux);
   auto aligned32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 31u) == 0; };
   prm.a_rows = a->x_rows;
-  prm.a_src = static_cast<const __nv_bfloat16*>(a->x);
-  prm.lda = a->ldx;
   prm.row_scale = a->row_scale;
   prm.w_grad = a->w_grad;
   prm.w_ld = a->w_ld;
