@@ -159,9 +159,7 @@ def _rank_rows(factor: torch.Tensor) -> torch.Tensor:
     e, r, d = factor.shape
     if r == RANK_MULTIPLE and factor.dtype == torch.bfloat16 and factor.is_contiguous():
         return factor
-    out = factor.new_zeros((e, RANK_MULTIPLE, d), dtype=torch.bfloat16)
-    out[:, :r] = factor
-    return out
+    return torch.nn.functional.pad(factor.to(torch.bfloat16), (0, 0, 0, RANK_MULTIPLE - r)).contiguous()  # one pass
 
 
 def _rank_cols(factor: torch.Tensor, width: int) -> torch.Tensor:
@@ -169,9 +167,7 @@ def _rank_cols(factor: torch.Tensor, width: int) -> torch.Tensor:
     e, d, r = factor.shape
     if r == width and factor.dtype == torch.bfloat16 and factor.is_contiguous():
         return factor
-    out = factor.new_zeros((e, d, width), dtype=torch.bfloat16)
-    out[:, :, :r] = factor
-    return out
+    return torch.nn.functional.pad(factor.to(torch.bfloat16), (0, width - r)).contiguous()  # values and zeros
 
 
 class _Adapters:
