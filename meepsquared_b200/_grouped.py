@@ -18,6 +18,8 @@ library or a compute capability 10.0 GPU the functions raise.
 
 import os
 
+import types
+
 import torch
 
 from . import _lib
@@ -182,8 +184,8 @@ class _Adapters:
 
     def __init__(self, lhs, rhs, is_transposed):
         self.rank = lhs.shape[2]
-        if self.rank > RANK_MULTIPLE:
-            raise NotImplementedError(f"LoRA rank {self.rank}: the kernels take ranks up to {RANK_MULTIPLE}")
+        if self.rank > RANK_MULTIPLE:  # larger ranks go to the products in 16-rank chunks (_rank_chunks)
+            raise NotImplementedError(f"LoRA rank {self.rank}: one fused panel takes ranks up to {RANK_MULTIPLE}")
         self.lhs, self.rhs, self.is_transposed = lhs, rhs, is_transposed
         self._cache = {}
 
@@ -396,36 +398,77 @@ def _to_lhs_rhs(grad_rows_k, grad_cols_n, adapters):
     return grad_cols_n[:, :, :rank], grad_rows_k.transpose(1, 2)[:, :rank, :]  # lhs (E,out,r), rhs (E,r,in)
 
 
+def _rank_chunks(lhs, rhs, is_transposed):
+    """The adapters as rank-16 chunks (_Adapters each): delta = sum over chunks of lhs_c @ rhs_c. The reference pads
+    any rank to a multiple of 16 (_grouped.py:275-282); the fused panel holds 16 ranks."""
+    rank = lhs.shape[2]
+    chunks = []
+    for c in range(0, rank, RANK_MULTIPLE):
+        lc, rc = lhs[:, :, c:c + RANK_MULTIPLE], rhs[:, c:c + RANK_MULTIPLE, :]
+        pad = RANK_MULTIPLE - lc.shape[2]
+        if rank > RANK_MULTIPLE and pad:  # a ragged last chunk of a large rank: zero ranks, as the reference pads
+            lc, rc = torch.nn.functional.pad(lc, (0, pad)), torch.nn.functional.pad(rc, (0, 0, 0, pad))
+        chunks.append(_Adapters(lc, rc, is_transposed))
+    return chunks
+
+
+def _low_rank_pass(x, first, second, offsets, tiles):
+    """(x @ first (rows, 16) bf16, (x @ first) @ second): the two small products of one rank chunk beyond the first,
+    each on the grouped kernel with the factor as its stack, (experts, 16, k) and (experts, n, 16)."""
+    low = _launch(x, first.transpose(1, 2).contiguous(), None, offsets, True, None, 1.0, None, False, tiles=tiles)[0]
+    delta = _launch(low, second.transpose(1, 2).contiguous(), None, offsets, True, None, 1.0, None, False,
+                    tiles=tiles)[0]
+    return low, delta
+
+
 class _LoraGroupedProduct(torch.autograd.Function):
-    """The experts' product with the adapters; gradients for x and the adapters, none for the frozen stack."""
+    """The experts' product with the adapters; gradients for x and the adapters, none for the frozen stack.
+
+    Ranks up to 16 ride in the fused product's panel. A larger rank is split into 16-rank chunks: the first in the
+    fused product, each further one as two small grouped products added to the output (an extra read of x per
+    chunk), and the adapter gradients reduced chunk by chunk."""
 
     @staticmethod
     def forward(ctx, x, weight, scale, offsets, is_transposed, lhs, rhs, scaling, bias, products_fp8):
-        adapters = _Adapters(lhs.detach(), rhs.detach(), is_transposed) if lhs is not None else None
+        chunks = _rank_chunks(lhs.detach(), rhs.detach(), is_transposed) if lhs is not None else []
+        adapters = chunks[0] if chunks else None
         tiles = TileMaps(offsets, x.shape[0])
         out, low = _launch(x, weight, scale, offsets, not is_transposed, adapters, scaling, bias, True, tiles=tiles)
-        ctx.save_for_backward(x, offsets, *((low,) if low is not None else ()))
+        lows = [low] if low is not None else []
+        for ad in chunks[1:]:
+            first, second = ad.factors(False)
+            low_c, delta = _low_rank_pass(x, first, second, offsets, tiles)
+            out.add_(delta, alpha=scaling)
+            lows.append(low_c)
+        ctx.save_for_backward(x, offsets, *lows)
         ctx.weight = weight  # the frozen stack (a tensor or a QuantStack), read again by the backward product
-        ctx.adapters, ctx.scale, ctx.is_transposed, ctx.scaling, ctx.tiles = adapters, scale, is_transposed, scaling, tiles
+        ctx.chunks, ctx.scale, ctx.is_transposed, ctx.scaling, ctx.tiles = chunks, scale, is_transposed, scaling, tiles
+        ctx.rank = lhs.shape[2] if lhs is not None else 0
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        x, offsets, *rest = ctx.saved_tensors
+        x, offsets, *lows = ctx.saved_tensors
         weight = ctx.weight
-        adapters = ctx.adapters
+        chunks = ctx.chunks
         grad_out = grad_out.contiguous()
-        if adapters is None:
+        if not chunks:
             grad_x, _ = _launch(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, None, 1.0, None, False,
                                 backward=True, tiles=ctx.tiles)
             return grad_x, None, None, None, None, None, None, None, None, None
-        low = rest[0]
         # grad_x = grad @ W (the stack read the other way) + s (grad @ B^T) @ A^T: the adapters swap roles
-        grad_x, low2 = _launch(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, adapters, ctx.scaling, None,
+        grad_x, low2 = _launch(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, chunks[0], ctx.scaling, None,
                                True, backward=True, tiles=ctx.tiles)
-        grad_first = _reduce(x, low2, offsets, ctx.scaling)        # (E, K_fwd, 16)
-        grad_second = _reduce(grad_out, low, offsets, ctx.scaling)  # (E, N_fwd, 16)
-        grad_lhs, grad_rhs = _to_lhs_rhs(grad_first, grad_second, adapters)
+        lows2 = [low2]
+        for ad in chunks[1:]:
+            first, second = ad.factors(True)
+            low2_c, delta = _low_rank_pass(grad_out, first, second, offsets, ctx.tiles)
+            grad_x.add_(delta, alpha=ctx.scaling)
+            lows2.append(low2_c)
+        grad_first = torch.cat([_reduce(x, l2, offsets, ctx.scaling) for l2 in lows2], dim=2)  # (E, K_fwd, R)
+        grad_second = torch.cat([_reduce(grad_out, l, offsets, ctx.scaling) for l in lows], dim=2)  # (E, N_fwd, R)
+        whole = types.SimpleNamespace(rank=ctx.rank, is_transposed=ctx.is_transposed)
+        grad_lhs, grad_rhs = _to_lhs_rhs(grad_first, grad_second, whole)
         return grad_x, None, None, None, None, grad_lhs, grad_rhs, None, None, None
 
 

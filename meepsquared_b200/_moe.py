@@ -394,10 +394,16 @@ def _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)
                                                  routing.offsets, t, cast(lhs), cast(rhs), float(scaling), bias, None)
         return out.masked_fill(sentinel, 0.0)  # rows past the experts' ends are not written by the products
 
+    act = getattr(experts, "act_fn", None) or torch.nn.functional.silu
     if experts.has_gate:
-        h = experts._apply_gate(project(x, "gate_up_proj", "gate_up_proj_bias"))
+        gate_up = project(x, "gate_up_proj", "gate_up_proj_bias")
+        if hasattr(experts, "_apply_gate"):
+            h = experts._apply_gate(gate_up)
+        else:  # Transformers' default gate
+            gate, up = gate_up.chunk(2, dim=-1)
+            h = act(gate) * up
     else:
-        h = experts.act_fn(project(x, "up_proj", "up_proj_bias"))
+        h = act(project(x, "up_proj", "up_proj_bias"))
     y = project(h, "down_proj", "down_proj_bias")
     return _Combine.apply(y, top_k_weights, routing).to(hidden_states.dtype)
 
@@ -414,7 +420,9 @@ def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
     """
     if not hidden_states.is_cuda:
         raise RuntimeError("the routed layer runs on a CUDA GPU (compute capability 10.0)")
-    if not _default_swiglu(experts):
+    if not _default_swiglu(experts) or any(f[0] is not None and f[0].shape[2] > _grouped.RANK_MULTIPLE
+                                           for f in factors.values()):
+        # another gate, or adapters of rank above 16 (the products take them in 16-rank chunks)
         return _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)
     bias1 = experts.gate_up_proj_bias if experts.has_bias else None
     bias2 = experts.down_proj_bias if experts.has_bias else None

@@ -79,8 +79,11 @@ def check_lora(got, x, weight, scale, offsets, is_transposed, lhs, rhs, scaling,
     out = ogrouped.lora_forward(x, weight, scale, offsets, is_transposed, lhs, rhs, scaling, bias)
     gx, gl, gr = ogrouped.lora_backward(x, grad, weight, scale, offsets, is_transposed, lhs, rhs, scaling)
     rows = int(offsets[-1])
-    assert_close(got[0][:rows], out[:rows], "out")
-    assert_close(got[1][:rows], gx[:rows], "grad_x")
+    # ranks above 16: each chunk past the first adds its bf16 update to the bf16 output (two more roundings), so the
+    # allowance follows the tensor's size there, as the reference's own tests allow for its kernel
+    chunked = lhs is not None and lhs.shape[2] > 16
+    assert_close(got[0][:rows], out[:rows], "out", scaled=chunked)
+    assert_close(got[1][:rows], gx[:rows], "grad_x", scaled=chunked)
     assert_close(got[2], gl, "grad_lhs", scaled=True)
     assert_close(got[3], gr, "grad_rhs", scaled=True)
 
@@ -100,7 +103,7 @@ def test_lora_matches_the_reference_golden_vectors(golden, prefix, is_transposed
 
 
 @pytest.mark.parametrize("is_transposed", [False, True])
-@pytest.mark.parametrize("rank", [4, 8, 16])
+@pytest.mark.parametrize("rank", [4, 8, 16, 20, 32, 64])  # above 16: the fused chunk plus 16-rank chunks
 @pytest.mark.parametrize("rows_per_expert,K,N", [([37, 0, 200, 64, 1], 96, 80), ([1000, 3, 0, 700], 2048, 1536),
                                                   ([513, 256], 768, 2048)])
 def test_lora_forward_and_backward_match_float32(is_transposed, rank, rows_per_expert, K, N, pair_mode):

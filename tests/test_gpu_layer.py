@@ -98,6 +98,15 @@ def test_layer_at_baseline_shapes_matches_the_oracle(cfg, pair_mode, routed_rows
     check_against(res, oracle_layer(inp, idx), scaled=True)
 
 
+@pytest.mark.parametrize("rank", [32, 40])
+def test_layer_with_adapters_of_rank_above_16_matches_the_oracle(rank):
+    """Ranks above one fused panel's 16 (the reference pads any rank to a multiple of 16): the layer runs unfused,
+    each product taking the adapters in 16-rank chunks."""
+    inp = layer_inputs.layer(**dict(layer_inputs.CONFIG1, rank=rank, alpha=2 * rank))
+    res, idx = run_layer(inp)
+    check_against(res, oracle_layer(inp, idx), scaled=True)
+
+
 def test_full_size_layer_step_is_finite_and_deterministic():
     """BASELINE config 2 at full size (T=16384, E=128, top-8): two runs give identical bits, all finite."""
     inp = layer_inputs.layer(**layer_inputs.QWEN3_30B)
