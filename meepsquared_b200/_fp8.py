@@ -106,6 +106,26 @@ def dequantize_blocks(codes: torch.Tensor, scale_inv: torch.Tensor) -> torch.Ten
     return out
 
 
+def grouped_product(x, weight8, scale, offsets, bias, is_transposed: bool) -> torch.Tensor:
+    """x against a stack held as FP8, per expert group, with x's gradient (meepsquared/_fp8.py:137-164), in x's
+    dtype. The grouped kernel reads the e4m3 codes and converts them in shared memory, for the forward product and
+    again for the backward one; nothing dequantised is kept. One scale per expert is applied to the accumulator; a
+    grid of block scales (scale (E, sr, sc)) to the converted weights, as the routed layer reads such a stack."""
+    from . import _grouped
+
+    if scale.dim() == 1:
+        out = _grouped.lora_linear(x.to(torch.bfloat16), weight8, scale, offsets, is_transposed, bias=bias,
+                                   products_fp8=False)
+        return out.to(x.dtype)
+    stack = _grouped.QuantStack.from_fp8(weight8.detach(), scale)
+    if stack is None:
+        stack = dequantize_blocks(weight8.detach(), scale)
+    bias = bias.detach().to(torch.bfloat16).contiguous() if bias is not None else None
+    out = _grouped._LoraGroupedProduct.apply(x.to(torch.bfloat16), stack, None, offsets.to(torch.int32),
+                                             is_transposed, None, None, 1.0, bias, None)
+    return out.to(x.dtype)
+
+
 def convert_stacks(experts, block: int | None = None) -> int:
     """Every frozen stack of an experts module held as FP8, its scale as <name>_scale_inv; returns how many.
 

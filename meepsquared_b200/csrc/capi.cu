@@ -8,25 +8,27 @@ namespace meep2b {
 
 int bind_stream_device(cudaStream_t stream) {
   int want = -1;
-  if (stream == nullptr) return MEEP2B_OK;
-  // a stream being captured into a CUDA graph is not queried for its device (the query is not a capturable
-  // operation); the caller captures on the current device
-  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &capturing) != cudaSuccess) {
+  if (stream != nullptr) {
+    // a stream being captured into a CUDA graph is not queried for its device (the query is not a capturable
+    // operation); the caller captures on the current device
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &capturing) != cudaSuccess) {
+      cudaGetLastError();
+      return MEEP2B_ERR_LAUNCH;
+    }
+    if (capturing != cudaStreamCaptureStatusNone) return MEEP2B_OK;
+    if (cudaStreamGetDevice(stream, &want) != cudaSuccess) {
+      cudaGetLastError();
+      return MEEP2B_ERR_LAUNCH;
+    }
+  } else if (cudaGetDevice(&want) != cudaSuccess) {
     cudaGetLastError();
     return MEEP2B_ERR_LAUNCH;
   }
-  if (capturing != cudaStreamCaptureStatusNone) return MEEP2B_OK;
-  if (cudaStreamGetDevice(stream, &want) != cudaSuccess) {
-    cudaGetLastError();
-    return MEEP2B_ERR_LAUNCH;
-  }
-  int cur = -1;
-  if (cudaGetDevice(&cur) != cudaSuccess) {
-    cudaGetLastError();
-    return MEEP2B_ERR_LAUNCH;
-  }
-  if (cur != want && cudaSetDevice(want) != cudaSuccess) {
+  // cudaSetDevice also makes the device's primary context current on this thread. The tensor-map encoding is a
+  // driver call and needs it: a thread that has made no runtime call yet (autograd runs the backward pass on its
+  // own thread) has no current context, and the encoding would fail with an invalid-context error.
+  if (cudaSetDevice(want) != cudaSuccess) {
     cudaGetLastError();
     return MEEP2B_ERR_LAUNCH;
   }

@@ -98,3 +98,56 @@ def test_fp8_dequantize_takes_either_form_of_scale():
     assert torch.equal(_fp8.dequantize(c2, s2), _fp8.dequantize_blocks(c2, s2))
     with pytest.raises(ValueError):
         _fp8.dequantize(c2, s2[0])
+
+
+@pytest.mark.parametrize("block", [None, 128])
+def test_the_fp8_grouped_product_matches_the_dequantized_stack(block):
+    """_fp8.grouped_product (meepsquared/_fp8.py:137-164): x against an FP8 stack and x's gradient, against float32
+    over the stack as the reference dequantises it."""
+    from oracle import grouped as ogrouped
+    from parity import as_np, assert_close
+
+    gen = torch.Generator().manual_seed(12)
+    rows_per_expert, K, N = [37, 0, 200, 64, 1], 256, 192
+    offsets = torch.cumsum(torch.tensor(rows_per_expert, dtype=torch.int32), 0, dtype=torch.int32).to("cuda")
+    w = (torch.randn(5, N, K, generator=gen) * 0.05).to("cuda")
+    if block is None:
+        w8, scale = _fp8.quantize_stack(w)
+    else:
+        w8, scale = _fp8.quantize_blocks(w, block=block)
+    x = torch.randn(sum(rows_per_expert), K, generator=gen).to("cuda", torch.bfloat16).requires_grad_()
+    out = _fp8.grouped_product(x, w8, scale, offsets, None, False)
+    grad = torch.randn(out.shape, generator=gen).to("cuda", torch.bfloat16)
+    out.backward(grad)
+    w_deq = as_np(_fp8.dequantize(w8, scale))
+    want = ogrouped.lora_forward(as_np(x.detach()), w_deq, None, as_np(offsets), False)
+    gx, _, _ = ogrouped.lora_backward(as_np(x.detach()), as_np(grad), w_deq, None, as_np(offsets), False, None, None,
+                                      1.0)
+    assert_close(out.detach(), want, "out", scaled=True)
+    assert_close(x.grad, gx, "grad_x", scaled=True)
+
+
+def test_a_backward_pass_on_a_thread_new_to_cuda_runs(tmp_path):
+    """The first library call of autograd's backward thread can be a tensor-map encoding (an FP8 stack's product
+    without adapters): the library makes the device's context current on that thread first. Run in a fresh process,
+    where nothing else has touched CUDA on that thread."""
+    import subprocess
+    import sys
+
+    script = tmp_path / "backward_thread.py"
+    script.write_text(
+        "import sys, torch\n"
+        f"sys.path.insert(0, {repr(str(__import__('pathlib').Path(__file__).resolve().parents[1]))})\n"
+        "import meepsquared_b200 as mb\n"
+        "from meepsquared_b200 import _fp8\n"
+        "g = torch.Generator().manual_seed(0)\n"
+        "offsets = torch.tensor([37, 37, 237, 301, 302], dtype=torch.int32, device='cuda')\n"
+        "w8, scale = _fp8.quantize_stack((torch.randn(5, 192, 256, generator=g) * 0.05).cuda())\n"
+        "x = torch.randn(302, 256, generator=g).to('cuda', torch.bfloat16).requires_grad_()\n"
+        "out = mb.lora_linear(x, w8, scale, offsets, False)\n"
+        "out.backward(torch.randn(out.shape, generator=g).to('cuda', torch.bfloat16))\n"
+        "torch.cuda.synchronize()\n"
+        "assert torch.isfinite(x.grad.float()).all()\n"
+        "print('ok')\n")
+    run = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, timeout=600)
+    assert run.returncode == 0 and run.stdout.strip().endswith("ok"), run.stderr[-2000:]
