@@ -183,6 +183,57 @@ typedef struct meep2b_product {
 
 int meep2b_grouped_product(const meep2b_product* p, void* stream);
 
+/* ---------------------------------------------------------------------------------------------- FP8 products */
+
+/* The activations of an FP8 product, quantised as the reference's X_FP8 path quantises each x tile
+ * (_grouped.py:194-197), with tiles of 128 columns: for row r and block b of columns 128b..128b+127,
+ * scales[b * ld_scales + r] = max(max |x[r, j]|, 1e-12) / 448 (float32) and codes[r * k + j] = e4m3(x[r, j] / that
+ * scale), rounded to nearest even. x (rows, k) bf16 with row stride ldx (a multiple of 4); k a multiple of 16. */
+int meep2b_fp8_rows_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, uint8_t* codes, float* scales,
+                             int64_t ld_scales, void* stream);
+
+/* One launch of the FP8 product, the reference's _grouped_gemm_kernel with W_FP8 and X_FP8 (_grouped.py:141-146,
+ * 194-197, 202-219; selected by fp8_products, :70-80): for each tile of 128 rows of one expert e and 128 columns,
+ *   acc  = sum over k-blocks b of (x8_b W8_{e,b}^T) * xscale[b, row] (* the stack's block scale)
+ *          (tcgen05 kind::f8f6f4: e4m3 codes, float32 partial sums, one per 128-column k-block, promoted in registers)
+ *   acc  = acc * scale_e + scaling * (low U_e^T) + bias_e,   out = bf16(acc)
+ * x8 / xscale come from meep2b_fp8_rows_quantize (codes (rows, k), row stride k; scales (ceil(k/128), ld_xscale)).
+ * weight: e4m3 codes, (experts, n, k) when b_mn == 0, (experts, k, n) when b_mn == 1. scale (experts,) or NULL.
+ * wblock: NULL, or the stack's block scales: the partial sum of k-block b and column block c = col / 128 of expert e
+ * is multiplied by wblock[e * wb_stride_e + (b / wb_div_k) * wb_stride_k + (c / wb_div_n) * wb_stride_n].
+ * low (rows, 16) bf16: bf16(x A_e^T), the adapters' panel of the bf16 x (the reference multiplies the adapters with
+ * the bf16 x tile, :141-146,203-213), or NULL without adapters; up (experts, n, 16) bf16, the rank padded with
+ * zeros. offsets / tile_expert / tile_row / tiles / max_tiles as meep2b_product (block_m 128). k and n multiples
+ * of 16; out (rows, n) bf16 with row stride ldo (a multiple of 8). */
+typedef struct meep2b_product_f8 {
+  const uint8_t* x8;
+  int64_t rows, k;
+  const float* xscale;
+  int64_t ld_xscale;
+  const uint8_t* weight;
+  int32_t experts;
+  int64_t n;
+  int32_t b_mn;
+  const float* scale;
+  const float* wblock;
+  int64_t wb_stride_e, wb_stride_k, wb_stride_n;
+  int32_t wb_div_k, wb_div_n;
+  const void* low;
+  const void* up;
+  float scaling;
+  const void* bias;
+  const int32_t* offsets;
+  const int32_t* tile_expert;
+  const int32_t* tile_row;
+  const int32_t* tiles;
+  int64_t max_tiles;
+  void* out;
+  int64_t ldo;
+  int32_t sm_limit; /* 0: one CTA per SM */
+} meep2b_product_f8;
+
+int meep2b_grouped_product_f8(const meep2b_product_f8* p, void* stream);
+
 /* _grouped._reduce / _grouped_reduce_kernel (_grouped.py:233-256,362-370): the adapters' gradients,
  * out[e, j, r] = bf16(scaling * sum over expert e's rows of g[row, j] * low[row, r]) for r < 16; g (rows, n) bf16
  * with row stride ldg, low (rows, 16) bf16, out (experts, n, 16) bf16. */

@@ -356,6 +356,122 @@ def set_launch_observer(observer):
     _launch_observer = observer
 
 
+class Fp8Stack:
+    """An e4m3 stack whose products run on the FP8 tensor cores (the reference's X_FP8 path, _grouped.py:141-146,
+    194-197): the activations are quantised per row and 128-column tile, the codes of both multiply as they are,
+    and the scales are applied to the float32 partial sums.
+
+    codes: the stored (experts, rows, cols) stack, cols contiguous. scale: (experts,) float32 (one scale per
+    expert, the reference's FP8 stack), or None with `blocks` = (scales (experts, sr, sc) float32, the block
+    height, the block width) for a stack with a grid of block scales whose blocks are whole 128 x 128 tiles.
+    """
+
+    def __init__(self, codes, scale=None, blocks=None):
+        self.codes, self.scale, self.blocks = codes, scale, blocks
+        self.shape = tuple(codes.shape)
+
+    @classmethod
+    def of(cls, weight8: torch.Tensor, scale):
+        """The stack for the FP8 products; NotImplementedError for sizes the kernel does not take."""
+        e, rows, cols = weight8.shape
+        if rows % 16 or cols % 16:
+            raise NotImplementedError(f"FP8 products need stack sizes that are multiples of 16: {tuple(weight8.shape)}")
+        codes = weight8.contiguous()
+        if scale is None:
+            return cls(codes)
+        if scale.dim() <= 1:
+            return cls(codes, scale.reshape(-1).to(torch.float32).contiguous())
+        if scale.dim() == 3 and scale.shape[0] == e:
+            sr, sc = int(scale.shape[1]), int(scale.shape[2])
+            br, bc = -(-rows // sr), -(-cols // sc)
+            if (br % 128 == 0 or sr == 1) and (bc % 128 == 0 or sc == 1):
+                # the scale as the reference's dequantisation applies it: rounded to bf16 (quantize.py:131-157)
+                return cls(codes, None, (scale.to(torch.bfloat16).float().contiguous(), br, bc))
+        raise NotImplementedError(f"FP8 products take one scale per expert or 128 x 128 block scales, not "
+                                  f"{tuple(scale.shape)} over {tuple(weight8.shape)}")
+
+
+def _quantize_rows(x: torch.Tensor):
+    """(codes (rows, k) uint8, scales (ceil(k/128), rows) float32): x quantised per row and 128-column tile."""
+    rows, k = x.shape
+    codes = torch.empty((rows, k), device=x.device, dtype=torch.uint8)
+    scales = torch.empty((-(-k // 128), rows), device=x.device, dtype=torch.float32)
+    if rows:
+        _lib.check(_lib.load().meep2b_fp8_rows_quantize(_lib.ptr(x), rows, k, x.stride(0), _lib.ptr(codes),
+                                                        _lib.ptr(scales), rows, _lib.stream_of(x)),
+                   "meep2b_fp8_rows_quantize")
+    return codes, scales
+
+
+def _launch_f8(x, stack: Fp8Stack, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward=False,
+               tiles=None):
+    """The FP8 product (meep2b_grouped_product_f8); returns (out, low) as _launch does."""
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"the grouped kernel computes in bf16: x {x.dtype}")
+    if x.stride(1) != 1 or x.stride(0) % 8:
+        x = x.contiguous()
+    rows, K = x.shape
+    b_mn = 0 if k_contiguous_layout else 1
+    experts, srows, scols = stack.shape
+    N = srows if b_mn == 0 else scols
+    if (scols if b_mn == 0 else srows) != K:
+        raise ValueError(f"an FP8 stack {stack.shape} does not take x with {K} columns")
+    if K % 16:
+        raise NotImplementedError(f"FP8 products need x with a multiple of 16 columns: {K}")
+    out = torch.empty((rows, N), device=x.device, dtype=x.dtype)
+    if tiles is None:
+        tiles = TileMaps(offsets, rows)
+    low = None
+    up = None
+    if adapters is not None:
+        panel, up = adapters.operands(0, backward)  # (E, 16, K) and (E, N, 16)
+        low = _launch(x, panel, None, offsets, True, None, 1.0, None, False, tiles=tiles)[0]
+    if rows == 0:
+        return out, (low if store_low else None)
+    codes, xscale = _quantize_rows(x)
+    tmap = tiles.get(128)
+    p = _lib.ProductF8()
+    p.x8, p.rows, p.k, p.xscale, p.ld_xscale = codes.data_ptr(), rows, K, xscale.data_ptr(), rows
+    p.weight, p.experts, p.n, p.b_mn = stack.codes.data_ptr(), experts, N, b_mn
+    p.scale = stack.scale.data_ptr() if stack.scale is not None else None
+    if stack.blocks is not None:
+        ws, br, bc = stack.blocks
+        sr, sc = ws.shape[1], ws.shape[2]
+        huge = 1 << 30
+        div_r, div_c = (br // 128 if sr > 1 else huge), (bc // 128 if sc > 1 else huge)
+        p.wblock, p.wb_stride_e = ws.data_ptr(), sr * sc
+        if b_mn == 0:  # k runs along the stored columns, n along the rows
+            p.wb_stride_k, p.wb_div_k, p.wb_stride_n, p.wb_div_n = 1, div_c, sc, div_r
+        else:
+            p.wb_stride_k, p.wb_div_k, p.wb_stride_n, p.wb_div_n = sc, div_r, 1, div_c
+    p.low = low.data_ptr() if low is not None else None
+    p.up = up.data_ptr() if up is not None else None
+    p.scaling = float(scaling)
+    p.bias = bias.data_ptr() if bias is not None else None
+    p.offsets = offsets.data_ptr()
+    p.tile_expert, p.tile_row, p.tiles = tmap[0].data_ptr(), tmap[1].data_ptr(), tmap[2].data_ptr()
+    p.max_tiles = tmap[0].numel()
+    p.out, p.ldo = out.data_ptr(), out.stride(0)
+    p.sm_limit = 0
+    observer = _launch_observer
+    if observer is not None:
+        observer.before(x)
+    _lib.check(_lib.load().meep2b_grouped_product_f8(p, _lib.stream_of(x)), "meep2b_grouped_product_f8")
+    if observer is not None:
+        observer.after(x, 2 * rows * N * K)
+    return out, (low if store_low else None)
+
+
+def _product(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward=False,
+             tiles=None):
+    """One grouped product over a bf16, quantised or FP8-products stack."""
+    if isinstance(weight, Fp8Stack):
+        return _launch_f8(x, weight, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward,
+                          tiles)
+    return _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward,
+                   tiles=tiles)
+
+
 def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: float, g_rows=None,
             row_scale=None) -> torch.Tensor:
     """(experts, N, 16) bf16: scaling * sum over each expert's rows of g^T @ low (_grouped.py:362-370).
@@ -433,7 +549,7 @@ class _LoraGroupedProduct(torch.autograd.Function):
         chunks = _rank_chunks(lhs.detach(), rhs.detach(), is_transposed) if lhs is not None else []
         adapters = chunks[0] if chunks else None
         tiles = TileMaps(offsets, x.shape[0])
-        out, low = _launch(x, weight, scale, offsets, not is_transposed, adapters, scaling, bias, True, tiles=tiles)
+        out, low = _product(x, weight, scale, offsets, not is_transposed, adapters, scaling, bias, True, tiles=tiles)
         lows = [low] if low is not None else []
         for ad in chunks[1:]:
             first, second = ad.factors(False)
@@ -453,12 +569,12 @@ class _LoraGroupedProduct(torch.autograd.Function):
         chunks = ctx.chunks
         grad_out = grad_out.contiguous()
         if not chunks:
-            grad_x, _ = _launch(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, None, 1.0, None, False,
-                                backward=True, tiles=ctx.tiles)
+            grad_x, _ = _product(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, None, 1.0, None, False,
+                                 backward=True, tiles=ctx.tiles)
             return grad_x, None, None, None, None, None, None, None, None, None
         # grad_x = grad @ W (the stack read the other way) + s (grad @ B^T) @ A^T: the adapters swap roles
-        grad_x, low2 = _launch(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, chunks[0], ctx.scaling, None,
-                               True, backward=True, tiles=ctx.tiles)
+        grad_x, low2 = _product(grad_out, weight, ctx.scale, offsets, ctx.is_transposed, chunks[0], ctx.scaling, None,
+                                True, backward=True, tiles=ctx.tiles)
         lows2 = [low2]
         for ad in chunks[1:]:
             first, second = ad.factors(True)
@@ -472,10 +588,9 @@ class _LoraGroupedProduct(torch.autograd.Function):
         return grad_x, None, None, None, None, grad_lhs, grad_rhs, None, None, None
 
 
-def _check_fp8_products(weight, products_fp8, device):
-    if weight.dtype == torch.float8_e4m3fn and (fp8_products(device) if products_fp8 is None else products_fp8):
-        raise NotImplementedError("FP8 tensor-core products (activations quantized per row) are not built yet; "
-                                  "an FP8 stack is dequantized to bf16 (products_fp8=False)")
+def _fp8_products_on(weight, products_fp8, device) -> bool:
+    """Whether an FP8 stack's products run on the FP8 tensor cores (_grouped.py:316-320)."""
+    return weight.dtype == torch.float8_e4m3fn and bool(fp8_products(device) if products_fp8 is None else products_fp8)
 
 
 def _dequantized(weight, scale):
@@ -503,7 +618,9 @@ def grouped_linear(x: torch.Tensor, weight: torch.Tensor, offsets: torch.Tensor,
     """
     _require(x, "grouped_linear")
     _stack_strides(weight, x.shape[1], is_transposed)
-    _check_fp8_products(weight, products_fp8, x.device)
+    if _fp8_products_on(weight, products_fp8, x.device):
+        return _launch_f8(x, Fp8Stack.of(weight, None), offsets.to(torch.int32), not is_transposed, None, 1.0, None,
+                          False)[0]
     weight, _ = _dequantized(weight, None)
     return _launch(x, weight, None, offsets, not is_transposed, None, 1.0, None, False)[0]
 
@@ -517,8 +634,10 @@ def lora_linear(x, weight, scale, offsets, is_transposed: bool, lhs=None, rhs=No
     """
     _require(x, "lora_linear")
     _stack_strides(weight, x.shape[1], is_transposed)
-    _check_fp8_products(weight, products_fp8, x.device)
-    weight, scale = _dequantized(weight, scale)
+    if _fp8_products_on(weight, products_fp8, x.device):
+        weight, scale = Fp8Stack.of(weight, scale), None
+    else:
+        weight, scale = _dequantized(weight, scale)
     if lhs is not None and (lhs.dtype != torch.bfloat16 or rhs.dtype != torch.bfloat16):
         lhs, rhs = lhs.to(torch.bfloat16), rhs.to(torch.bfloat16)
     if bias is not None and bias.dtype != torch.bfloat16:

@@ -33,6 +33,20 @@ class Product(ctypes.Structure):
     ]
 
 
+class ProductF8(ctypes.Structure):
+    """struct meep2b_product_f8 (include/meep2b.h)."""
+
+    _fields_ = [
+        ("x8", _p), ("rows", _i64), ("k", _i64), ("xscale", _p), ("ld_xscale", _i64),
+        ("weight", _p), ("experts", _i32), ("n", _i64), ("b_mn", _i32), ("scale", _p),
+        ("wblock", _p), ("wb_stride_e", _i64), ("wb_stride_k", _i64), ("wb_stride_n", _i64),
+        ("wb_div_k", _i32), ("wb_div_n", _i32),
+        ("low", _p), ("up", _p), ("scaling", _f32), ("bias", _p),
+        ("offsets", _p), ("tile_expert", _p), ("tile_row", _p), ("tiles", _p), ("max_tiles", _i64),
+        ("out", _p), ("ldo", _i64), ("sm_limit", _i32),
+    ]
+
+
 _SIGNATURES = {
     "meep2b_version": (ctypes.c_char_p, []),
     "meep2b_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -59,6 +73,8 @@ _SIGNATURES = {
     "meep2b_nf4_dequantize": (ctypes.c_int, [_p, _p, _p, _p, _p, _i32, _i32, _i64, _p, _p, _p]),
     "meep2b_merge_stack": (ctypes.c_int, [_p, _i32, _p, _p, _p, _i32, ctypes.c_float, _i64, _i64, _i64, _p, _i32,
                                           _p]),
+    "meep2b_fp8_rows_quantize": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _i64, _p]),
+    "meep2b_grouped_product_f8": (ctypes.c_int, [ctypes.POINTER(ProductF8), _p]),
 }
 
 _lib = None
@@ -112,7 +128,7 @@ KERNELS_PER_CALL = {
     "meep2b_grouped_reduce": 1, "meep2b_grouped_reduce_rows": 1, "meep2b_fp8_stack_dequantize": 1,
     "meep2b_fp8_block_dequantize": 1, "meep2b_nf4_dequantize": 2, "meep2b_nf4_absmax": 1,
     "meep2b_merge_stack": 1,
-    "meep2b_quant_multipliers": 1,
+    "meep2b_quant_multipliers": 1, "meep2b_fp8_rows_quantize": 1, "meep2b_grouped_product_f8": 1,
 }
 launches = {}
 

@@ -5,3 +5,4 @@
 #include "reduce.cu"
 #include "quant.cu"
 #include "merge.cu"
+#include "fp8_products.cu"

@@ -94,6 +94,48 @@ def lora_backward(x, grad, weight, scale, offsets, is_transposed, lhs=None, rhs=
     return grad_x, grad_lhs, grad_rhs
 
 
+def fp8_product(x, codes, scale, offsets, is_transposed, lhs=None, rhs=None, scaling=1.0, bias=None, block=128,
+                block_scale=None):
+    """The reference's FP8 product (_grouped.py:141-146,194-219 with W_FP8 and X_FP8), float32, tiles of `block`
+    columns: per expert, acc = sum over k-blocks b of (x8_b @ W8_b) * xscale[b, row]; acc *= scale_e;
+    acc += s * bf16(x @ F1) @ F2 (the adapters multiply the bf16 x, the panel rounded to bf16 as the kernel's
+    `low`); + bias_e. codes: the e4m3 stack as stored ((E, out, in), or (E, in, out) when is_transposed).
+    block_scale: None, or a function (e, b, c) -> the stack's scale of k-block b and 128-column block c (a
+    block-scaled stack; then scale is None).
+    """
+    from .quant import bf16, e4m3_to_f32, quantize_rows
+
+    x = np.asarray(x, dtype=np.float32)
+    x8, xs = quantize_rows(x, block)
+    xv = e4m3_to_f32(x8)
+    n = codes.shape[2] if is_transposed else codes.shape[1]
+    k = x.shape[1]
+    out = np.zeros((x.shape[0], n), dtype=np.float32)
+    for e, start, end in _segments(offsets):
+        if end == start:
+            continue
+        w = e4m3_to_f32(codes[e])
+        w = w if is_transposed else w.T  # (k, n)
+        acc = np.zeros((end - start, n), dtype=np.float32)
+        for b in range(-(-k // block)):
+            ks = slice(b * block, min(k, (b + 1) * block))
+            part = (xv[start:end, ks] @ w[ks]).astype(np.float32)
+            factor = xs[b, start:end][:, None]
+            if block_scale is not None:
+                cols = np.array([block_scale(e, b, c // 128) for c in range(n)], dtype=np.float32)[None, :]
+                factor = (factor * cols).astype(np.float32)
+            acc = acc + part * factor
+        if scale is not None:
+            acc = acc * np.float32(scale[e])
+        if lhs is not None:
+            f1, f2 = _factors(lhs, rhs, e, is_transposed)
+            acc = acc + np.float32(scaling) * (bf16(x[start:end] @ f1) @ f2)
+        if bias is not None:
+            acc = acc + np.asarray(bias[e], dtype=np.float32)
+        out[start:end] = acc
+    return out
+
+
 def silu(v):
     v = np.asarray(v, dtype=np.float32)
     return (v / (np.float32(1.0) + np.exp(-v))).astype(np.float32)

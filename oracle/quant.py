@@ -5,6 +5,7 @@
   round-to-nearest-even, values of magnitude >= 480 (and the band rounding past
   448) give the NaN code 0x7F, as ``torch.float8_e4m3fn`` casts do.
 * Per-expert FP8 stacks: ``meepsquared/_fp8.py:122-134``.
+* The activations of an FP8 product, per row and tile: ``meepsquared/_grouped.py:194-197``.
 * 128x128 block FP8: ``meepsquared/_vendor/axolotl/quantize.py:131-157``
   (dequantize, multiply in bf16) and ``:238-263`` (quantize, clamp to +-448).
 * NF4 with double-quantised absmax: the format bitsandbytes 0.50.2 implements
@@ -99,6 +100,25 @@ def dequantize_stack(codes, scale) -> np.ndarray:
     v = e4m3_to_f32(codes)
     s = np.asarray(scale, dtype=np.float32).reshape(-1, *([1] * (v.ndim - 1)))
     return bf16_bits((v * s).astype(np.float32))
+
+
+# ----------------------------------------------------------------------------- activations of an FP8 product
+
+def quantize_rows(x, block=128) -> tuple[np.ndarray, np.ndarray]:
+    """The x tile quantisation of the reference's FP8 product (_grouped.py:194-197), tiles of `block` columns:
+    per row r and block b, scale = max(max |x[r, block b]|, 1e-12) / 448 (float32), codes = e4m3(x / scale).
+
+    Returns (codes (rows, k) uint8, scales (ceil(k/block), rows) float32: scales[b, r]).
+    """
+    x = np.asarray(x, dtype=np.float32)
+    rows, k = x.shape
+    nb = -(-k // block)
+    padded = np.zeros((rows, nb * block), dtype=np.float32)
+    padded[:, :k] = x
+    blocks = padded.reshape(rows, nb, block)
+    scale = (np.maximum(np.abs(blocks).max(axis=2), np.float32(1e-12)) / np.float32(E4M3_MAX)).astype(np.float32)
+    q = (blocks / scale[:, :, None]).astype(np.float32).reshape(rows, nb * block)[:, :k]
+    return f32_to_e4m3(q), np.ascontiguousarray(scale.T)
 
 
 # ----------------------------------------------------------------------------- FP8 with 128x128 block scales

@@ -164,3 +164,40 @@ def test_merged_stack_matches_the_reference_merged_save(golden, prefix):
     w8 = merge.dequantized_f32(codes=g[p + "codes"], scale=g[p + "scale"])
     np.testing.assert_array_equal(w8, g[p + "fp8_alone_f32"])
     np.testing.assert_allclose(merge.merged_stack(w8, lhs, rhs, s), g[p + "fp8_merged_f32"], rtol=1e-6, atol=1e-7)
+
+
+def test_activation_quantisation_known_answers():
+    """The FP8 product's x tiles (reference _grouped.py:194-197): the row's largest magnitude maps to 448, an
+    all-zero row takes the 1e-12 floor, and the codes round like torch's float8_e4m3fn cast of x / scale."""
+    x = np.zeros((3, 160), dtype=np.float32)
+    x[0, :4] = [2.0, -1.0, 0.5, 0.1]
+    x[0, 130] = 3.0          # the second tile of row 0 has its own scale
+    x[2] = np.linspace(-5, 7, 160, dtype=np.float32)
+    codes, scales = quant.quantize_rows(x)
+    assert codes.shape == (3, 160) and scales.shape == (2, 3)
+    assert scales[0, 0] == np.float32(2.0) / np.float32(448.0) and scales[1, 0] == np.float32(3.0) / np.float32(448.0)
+    assert scales[0, 1] == np.float32(1e-12) / np.float32(448.0) and not codes[1].any()
+    assert quant.e4m3_to_f32(codes[0, :1])[0] == 448.0 and quant.e4m3_to_f32(codes[0, 130:131])[0] == 448.0
+    for r in range(3):
+        for b in range(2):
+            cols = slice(128 * b, min(160, 128 * (b + 1)))
+            want = torch.from_numpy(x[r, cols] / scales[b, r]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+            np.testing.assert_array_equal(codes[r, cols], want)
+
+
+def test_fp8_product_is_exact_on_representable_activations():
+    """Activations that are e4m3 values times a power of two (the row's largest 448 * 2^j) quantise without error,
+    so the oracle's FP8 product equals the float32 product over the decoded stack."""
+    rng = np.random.default_rng(4)
+    levels = quant.e4m3_to_f32(np.arange(0, 0x7E, dtype=np.uint8))
+    rows, k, n = 40, 256, 48
+    x = rng.choice(levels, size=(rows, k)) * rng.choice([-1.0, 1.0], size=(rows, k))
+    x[:, 0] = 448.0
+    x[:, 128] = 448.0
+    x = (x * np.exp2(rng.integers(-6, 3, size=(rows, 1)))).astype(np.float32)
+    codes = rng.integers(0, 0x7E, size=(2, n, k)).astype(np.uint8)
+    offsets = np.array([15, 40])
+    got = grouped.fp8_product(x, codes, np.array([0.5, 2.0], dtype=np.float32), offsets, False)
+    w = quant.e4m3_to_f32(codes)
+    want = np.concatenate([x[:15] @ w[0].T * 0.5, x[15:] @ w[1].T * 2.0]).astype(np.float32)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-3 * np.abs(want).max())
