@@ -188,7 +188,7 @@ int meep2b_grouped_product(const meep2b_product* p, void* stream);
 /* The activations of an FP8 product, quantised as the reference's X_FP8 path quantises each x tile
  * (_grouped.py:194-197), with tiles of 128 columns: for row r and block b of columns 128b..128b+127,
  * scales[b * ld_scales + r] = max(max |x[r, j]|, 1e-12) / 448 (float32) and codes[r * k + j] = e4m3(x[r, j] / that
- * scale), rounded to nearest even. x (rows, k) bf16 with row stride ldx (a multiple of 4); k a multiple of 16. */
+ * scale), rounded to nearest even. x (rows, k) bf16 with row stride ldx (a multiple of 8); k a multiple of 16. */
 int meep2b_fp8_rows_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, uint8_t* codes, float* scales,
                              int64_t ld_scales, void* stream);
 

@@ -291,6 +291,10 @@ def _kernel_stack(experts, name):
         return (fused if fused is not None else _PerProduct(lambda: _nf4.dequantize(weight))), None
     if weight.dtype == torch.float8_e4m3fn:
         scale = getattr(experts, name + _fp8.STACK_SCALE)
+        if _grouped.fp8_products(weight.device):
+            # MEEPSQUARED_FP8_PRODUCTS=1: the products run on the FP8 tensor cores, the activations quantised per
+            # row and 128-column tile (the reference's _moe passes products_fp8=None, so the switch decides)
+            return _grouped.Fp8Stack.of(weight.detach(), scale), None
         # one scale per expert is applied to the accumulator, the codes converted exactly (_grouped.py:200-208);
         # a grid of block scales goes into the converted weights (quantize.py:131-157)
         per_expert = scale.dim() == 1
@@ -420,9 +424,12 @@ def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
     """
     if not hidden_states.is_cuda:
         raise RuntimeError("the routed layer runs on a CUDA GPU (compute capability 10.0)")
-    if not _default_swiglu(experts) or any(f[0] is not None and f[0].shape[2] > _grouped.RANK_MULTIPLE
-                                           for f in factors.values()):
-        # another gate, or adapters of rank above 16 (the products take them in 16-rank chunks)
+    fp8_products = any(getattr(experts, n, None) is not None and getattr(experts, n).dtype == torch.float8_e4m3fn
+                       for n in ("gate_up_proj", "down_proj")) and _grouped.fp8_products(hidden_states.device)
+    if not _default_swiglu(experts) or fp8_products or any(f[0] is not None and f[0].shape[2] > _grouped.RANK_MULTIPLE
+                                                           for f in factors.values()):
+        # another gate, FP8 tensor-core products (their kernel has the plain epilogue), or adapters of rank above 16
+        # (the products take them in 16-rank chunks)
         return _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)
     bias1 = experts.gate_up_proj_bias if experts.has_bias else None
     bias2 = experts.down_proj_bias if experts.has_bias else None

@@ -7,28 +7,30 @@
 //
 //  * quantize_rows_kernel: x (rows, k) bf16 -> codes (rows, k) e4m3 and scales (k/128 blocks, rows) float32,
 //    scale = max(amax over the row's 128 columns of the block, 1e-12) / 448, code = e4m3(x / scale) (round to
-//    nearest even); a warp per (row, block), memory bound (2 bytes read, 1 written per element).
-//  * grouped_gemm_f8_kernel: persistent, one CTA per SM, one unit = 128 rows of one expert x 128 columns.
-//    Warp 0 loads the x codes and the stack's codes with TMA (128 x 128 bytes each per k-block, 128-byte
-//    swizzle); warp 1 issues tcgen05.mma kind::f8f6f4 (e4m3 x e4m3, float32 accumulation), four MMAs of depth 32
-//    per 128-column k-block, each k-block into its own tensor-memory buffer (4 buffers of 128 columns); warps
-//    4-11 promote: each thread owns one row and 64 columns of the unit in registers and adds every k-block's
+//    nearest even); a half-warp per (row, block), memory bound (2 bytes read, 1 written per element).
+//  * grouped_gemm_f8_kernel: persistent, one CTA per SM, one unit = 128 rows of one expert x 256 columns.
+//    Warp 0 loads the x codes and the stack's codes with TMA (128 x 128 and 256 x 128 bytes per k-block,
+//    128-byte swizzle); warp 1 issues tcgen05.mma kind::f8f6f4 (e4m3 x e4m3, float32 accumulation), four MMAs of depth 32
+//    per 128-column k-block, each k-block into its own tensor-memory buffer (2 buffers of 256 columns); warps
+//    2-9 promote: each thread owns one row and 128 columns of the unit in registers and adds every k-block's
 //    partial sum times the row's scale of that block (times the stack's block scale, for block-scaled stacks).
 //    The adapters' up product (the bf16 panel x A^T, computed beforehand, times U) is one more bf16 MMA of depth
 //    16 into a buffer, added with the factor s. The epilogue applies the per-expert scale, the bias, rounds to
-//    bf16 and stores the row's 64 columns.
+//    bf16 and stores the row's 128 columns.
 // Every wait is bounded (common.cuh): a role that gives up records MEEP2B_ERR_TIMEOUT and the kernel returns.
 #include <cuda_fp8.h>
 
 namespace meep2b {
 namespace f8 {
 
-constexpr int BM = 128, BN = 128, BK = 128;  // BK is also the activations' quantisation block
-constexpr int STAGES = 6;
-constexpr int NBUF = 4;       // partial-sum buffers in tensor memory, 128 columns each
-constexpr int THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 2-3 idle, warps 4-11 promotion and epilogue
-constexpr int PROMO_WARP0 = 4;
+constexpr int BM = 128, BN = 256, BK = 128;  // BK is also the activations' quantisation block
+constexpr int STAGES = 4;
+constexpr int NBUF = 2;       // partial-sum buffers in tensor memory, 256 columns each
+constexpr int THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 promotion and epilogue (no idle warps: the
+                              // promotion's 128 float32 accumulators a thread need the registers)
+constexpr int PROMO_WARP0 = 2;
 constexpr int PROMO_WARPS = 8;
+constexpr int COLS = BN / 2;  // columns of a unit one promotion thread owns
 constexpr uint32_t A_BYTES = BM * BK;
 constexpr uint32_t B_BYTES = BN * BK;
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -50,7 +52,8 @@ struct Params {
   const float* xscale;  // (kblocks, ld_xscale): the scale of row r over k-block kb at xscale[kb * ld_xscale + r]
   int64_t ld_xscale;
   const float* scale;   // (experts,) or null
-  const float* wblock;  // block scales of the stack or null: wblock[e * se + (kb / div_k) * sk + (nb / div_n) * sn]
+  const float* wblock;  // block scales of the stack or null: wblock[e * se + (kb / div_k) * sk + (c / div_n) * sn],
+                        // c = column / 128
   int64_t wb_se, wb_sk, wb_sn;
   int wb_div_k, wb_div_n;
   const __nv_bfloat16* bias;  // (experts, N) or null
@@ -97,35 +100,62 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// One warp per (row, 128-column block); lane i holds columns 4i..4i+3 of the block.
+// One half-warp per (row, 128-column block), lane i of the half holding columns 8i..8i+7 of the block; each
+// half-warp issues the loads of four blocks before it uses any (16 bytes a lane each), to keep enough bytes in
+// flight for the HBM bandwidth.
+constexpr int Q_UNROLL = 4;
+
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
                                                             int64_t ldx, uint8_t* __restrict__ codes,
                                                             float* __restrict__ scales, int64_t ld_scales) {
   const int kblocks = (k + BK - 1) / BK;
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows * kblocks;
-       w += warps) {
-    const int64_t row = w / kblocks;
-    const int kb = static_cast<int>(w - row * kblocks);
-    const int col = kb * BK + lane * 4;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (col < k) {  // k is a multiple of 16, so a lane's four columns are all in range or all out
-      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + row * ldx + col));
-      v[0] = bf16_lo(raw.x), v[1] = bf16_hi(raw.x), v[2] = bf16_lo(raw.y), v[3] = bf16_hi(raw.y);
-    }
-    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  const int64_t items = rows * kblocks;
+  const bool small = items + static_cast<int64_t>(Q_UNROLL) * gridDim.x * blockDim.x < (int64_t(1) << 32);
+  const int sub = threadIdx.x & 15;
+  const int64_t half = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+  const int64_t halves = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
+  // the loop bound is the warp's first half-warp's (halves is even), so both halves of a warp take the same trips
+  // and every full-mask shuffle has all 32 lanes; items past the end are masked by `valid`
+  for (int64_t warp_base = half & ~int64_t(1); warp_base < items; warp_base += Q_UNROLL * halves) {
+    const int64_t base = warp_base + (half & 1);
+    uint4 raw[Q_UNROLL];
+    int64_t row[Q_UNROLL];
+    int kb[Q_UNROLL];
+    bool in[Q_UNROLL];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float s = fmaxf(amax, 1e-12f) / 448.0f;
-    if (col < k) {
-      const __nv_fp8x2_storage_t lo =
-          __nv_cvt_float2_to_fp8x2(make_float2(v[0] / s, v[1] / s), __NV_SATFINITE, __NV_E4M3);
-      const __nv_fp8x2_storage_t hi =
-          __nv_cvt_float2_to_fp8x2(make_float2(v[2] / s, v[3] / s), __NV_SATFINITE, __NV_E4M3);
-      *reinterpret_cast<uint32_t*>(codes + row * k + col) = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    for (int u = 0; u < Q_UNROLL; ++u) {
+      const int64_t item = base + u * halves;
+      const bool valid = item < items;
+      // a 32-bit division where the item count allows (a 64-bit one is a long emulated sequence)
+      row[u] = !valid ? 0 : (small ? static_cast<int64_t>(static_cast<uint32_t>(item) / static_cast<uint32_t>(kblocks))
+                                   : item / kblocks);
+      kb[u] = valid ? static_cast<int>(item - row[u] * kblocks) : 0;
+      const int col = kb[u] * BK + sub * 8;
+      in[u] = valid && col < k;  // k is a multiple of 16: a lane's eight columns are all in range or all out
+      raw[u] = in[u] ? __ldg(reinterpret_cast<const uint4*>(x + row[u] * ldx + col)) : make_uint4(0, 0, 0, 0);
     }
-    if (lane == 0) scales[static_cast<int64_t>(kb) * ld_scales + row] = s;
+#pragma unroll
+    for (int u = 0; u < Q_UNROLL; ++u) {
+      const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[2 * i] = bf16_lo(w[i]), v[2 * i + 1] = bf16_hi(w[i]);
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));  // within the half
+      const float s = fmaxf(amax, 1e-12f) / 448.0f;
+      if (in[u]) {
+        uint32_t q[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          q[i] = __nv_cvt_float2_to_fp8x2(make_float2(v[2 * i] / s, v[2 * i + 1] / s), __NV_SATFINITE, __NV_E4M3);
+        *reinterpret_cast<uint2*>(codes + row[u] * k + kb[u] * BK + sub * 8) =
+            make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
+      }
+      if (sub == 0 && base + u * halves < items) scales[static_cast<int64_t>(kb[u]) * ld_scales + row[u]] = s;
+    }
   }
 }
 
@@ -201,8 +231,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b_dst = a_dst + A_BYTES;
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
           tma_load_2d(a_dst, &tm_x, fb, kb * BK, row0);
-          if (B_MN) {
+          if (B_MN) {  // two boxes of 128 columns (the 128-byte swizzle spans 128 codes)
             tma_load_3d(b_dst, &tm_w, fb, nb * BN, kb * BK, e);
+            tma_load_3d(b_dst + BK * 128, &tm_w, fb, nb * BN + 128, kb * BK, e);
           } else {
             tma_load_3d(b_dst, &tm_w, fb, kb * BK, nb * BN, e);
           }
@@ -258,7 +289,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024, 2);
             const uint64_t bdesc =
-                B_MN ? smem_desc(b_addr + kk * 4096, 16384, 1024, 2) : smem_desc(b_addr + kk * 32, 16, 1024, 2);
+                B_MN ? smem_desc(b_addr + kk * 4096, BK * 128, 1024, 2) : smem_desc(b_addr + kk * 32, 16, 1024, 2);
             mma_e4m3(d, adesc, bdesc, IDESC, kk != 0);
           }
           mma_commit(bar_empty(stage));
@@ -290,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp >= PROMO_WARP0) {
     // ------------------------------------------------------------------------------------------ promotion
     const int q = warp & 3;                          // TMEM lane quarter this warp may read
-    const int half = (warp - PROMO_WARP0) >> 2;      // which 64 of the unit's 128 columns
+    const int half = (warp - PROMO_WARP0) >> 2;      // which 128 of the unit's 256 columns
     const int r = q * 32 + lane;                     // the thread's row within the unit
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     uint32_t g = 0;
@@ -301,41 +332,52 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = row0 + r;
       const int row_end = min(p.offsets[e], p.rows);
       const int row_c = min(row, p.rows - 1);
-      float acc[64];
+      float acc[COLS];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) acc[j] = 0.f;
-      auto promote = [&](float factor) -> bool {
+      for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
+      const int cblock = nb * (BN / 128) + half;  // the 128-column block of the thread's columns
+      auto factor_of = [&](int kb) -> float {
+        if (LORA && kb == p.kblocks) return p.scaling;  // the adapters' up product, after the base's k-blocks
+        float f = __ldg(p.xscale + static_cast<int64_t>(kb) * p.ld_xscale + row_c);
+        if (p.wblock != nullptr)
+          f *= __ldg(p.wblock + e * p.wb_se + (kb / p.wb_div_k) * p.wb_sk + (cblock / p.wb_div_n) * p.wb_sn);
+        return f;
+      };
+      const int steps = p.kblocks + (LORA ? 1 : 0);
+      const float se = p.scale != nullptr ? __ldg(p.scale + e) : 1.f;
+      float f_next = factor_of(0);  // each k-block's scale is loaded one k-block ahead, off the wait's path
+      for (int kb = 0; kb < steps; ++kb) {
+        const float f = f_next;
+        if (kb + 1 < steps) f_next = factor_of(kb + 1);
+        if (kb == p.kblocks) {  // the base sum is complete: the per-expert scale, then the adapters' product
+#pragma unroll
+          for (int j = 0; j < COLS; ++j) acc[j] *= se;
+        }
         const uint32_t b = g % NBUF;
-        if (!mbar_wait(bar_pfull(b), (g / NBUF) & 1)) return false;
+        if (!mbar_wait(bar_pfull(b), (g / NBUF) & 1)) { ok = false; break; }
         tc_fence_after();
-        float v[64];
-        tmem_ld64(tmem_base + lane_addr + b * BN + half * 64, v);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] = fmaf(v[j], factor, acc[j]);
+        for (int c = 0; c < COLS; c += 32) {
+          float v[32];
+          tmem_ld32(tmem_base + lane_addr + b * BN + half * COLS + c, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c + j] = fmaf(v[j], f, acc[c + j]);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_pempty(b));
         ++g;
-        return true;
-      };
-      for (int kb = 0; kb < p.kblocks && ok; ++kb) {
-        float f = __ldg(p.xscale + static_cast<int64_t>(kb) * p.ld_xscale + row_c);
-        if (p.wblock != nullptr)
-          f *= __ldg(p.wblock + e * p.wb_se + (kb / p.wb_div_k) * p.wb_sk + (nb / p.wb_div_n) * p.wb_sn);
-        ok = promote(f);
       }
       if (!ok) break;
-      if (p.scale != nullptr) {
-        const float se = __ldg(p.scale + e);
+      if (!LORA) {
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] *= se;
+        for (int j = 0; j < COLS; ++j) acc[j] *= se;
       }
-      if (LORA && !promote(p.scaling)) { ok = false; break; }
-      const int col0 = nb * BN + half * 64;
+      const int col0 = nb * BN + half * COLS;
       if (p.bias != nullptr) {
         const __nv_bfloat16* bias = p.bias + static_cast<int64_t>(e) * p.N + col0;
 #pragma unroll
-        for (int j = 0; j < 64; j += 8) {
+        for (int j = 0; j < COLS; j += 8) {
           if (col0 + j < p.N) {
             const uint4 w = __ldg(reinterpret_cast<const uint4*>(bias + j));
             const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
@@ -350,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (row < row_end) {
         __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.ldo + col0;
 #pragma unroll
-        for (int j = 0; j < 64; j += 8) {
+        for (int j = 0; j < COLS; j += 8) {
           if (col0 + j < p.N) {
             uint4 w;
             w.x = pack_bf16x2(acc[j], acc[j + 1]);
@@ -395,18 +437,17 @@ extern "C" int meep2b_fp8_rows_quantize(const void* x, int64_t rows, int64_t k, 
                                         float* scales, int64_t ld_scales, void* stream) {
   using namespace meep2b;
   if (rows < 0 || k < 1 || ldx < k || ld_scales < rows || k > INT32_MAX) return MEEP2B_ERR_SHAPE;
-  if (k % 16 || ldx % 4) return MEEP2B_ERR_ALIGN;
-  if ((reinterpret_cast<uintptr_t>(x) & 7u) || !aligned16(codes) || (reinterpret_cast<uintptr_t>(scales) & 3u))
-    return MEEP2B_ERR_ALIGN;
+  if (k % 16 || ldx % 8) return MEEP2B_ERR_ALIGN;
+  if (!aligned16(x) || !aligned16(codes) || (reinterpret_cast<uintptr_t>(scales) & 3u)) return MEEP2B_ERR_ALIGN;
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
   if (rows == 0) return MEEP2B_OK;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t warps = rows * ((k + f8::BK - 1) / f8::BK);
-  const int64_t blocks = (warps + 7) / 8;
-  const int grid = static_cast<int>(blocks < int64_t(sms) * 16 ? blocks : int64_t(sms) * 16);
+  const int64_t items = rows * ((k + f8::BK - 1) / f8::BK);
+  const int64_t blocks = (items + 16 * f8::Q_UNROLL - 1) / (16 * f8::Q_UNROLL);  // 16 half-warps a block
+  const int grid = static_cast<int>(blocks < int64_t(sms) * 8 ? blocks : int64_t(sms) * 8);
   f8::quantize_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,
                                                 codes, scales, ld_scales);
   return launch_status();
@@ -446,7 +487,7 @@ extern "C" int meep2b_grouped_product_f8(const meep2b_product_f8* a, void* strea
   } else {
     const uint64_t dims[3] = {N, K, E};
     const uint64_t strides[2] = {N, K * N};
-    const uint32_t box[3] = {f8::BN, f8::BK, 1};
+    const uint32_t box[3] = {128, f8::BK, 1};  // two loads of 128 columns per tile
     MEEP2B_TRY(encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a->weight, dims, strides, box,
                             CU_TENSOR_MAP_SWIZZLE_128B));
   }
