@@ -100,6 +100,24 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The e4m3 codes (round to nearest even, saturating) of x0 / s and x1 / s, the quotients rounded to float32 as a
+// division rounds them, without a division for almost every element: q = |x| * rcp (rcp = 1 / s correctly rounded)
+// is within 2.5 ulp of the rounded quotient, and rounding to e4m3 is monotonic, so when the codes of q - 6 ulp and
+// q + 6 ulp agree the quotient has that code too. Only near a rounding midpoint of e4m3 (6 ulp in 2^20 of each
+// code's interval) is the quotient computed by division. The sign is the sign of x, as a cast keeps it.
+__device__ __forceinline__ uint32_t e4m3_pair(float a, float b) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
+}
+
+__device__ __forceinline__ uint32_t e4m3_quotients(float x0, float x1, float s, float rcp) {
+  const float a0 = fabsf(x0), a1 = fabsf(x1);
+  const uint32_t b0 = __float_as_uint(a0 * rcp), b1 = __float_as_uint(a1 * rcp);
+  const uint32_t lo = e4m3_pair(__uint_as_float(b0 > 6u ? b0 - 6u : 0u), __uint_as_float(b1 > 6u ? b1 - 6u : 0u));
+  const uint32_t hi = e4m3_pair(__uint_as_float(b0 + 6u), __uint_as_float(b1 + 6u));
+  const uint32_t mag = lo == hi ? lo : e4m3_pair(a0 / s, a1 / s);
+  return mag | ((__float_as_uint(x0) >> 24) & 0x80u) | ((__float_as_uint(x1) >> 16) & 0x8000u);
+}
+
 // One half-warp per (row, 128-column block), lane i of the half holding columns 8i..8i+7 of the block; each
 // half-warp issues the loads of four blocks before it uses any (16 bytes a lane each), to keep enough bytes in
 // flight for the HBM bandwidth.
@@ -149,8 +167,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
       if (in[u]) {
         uint32_t q[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          q[i] = __nv_cvt_float2_to_fp8x2(make_float2(v[2 * i] / s, v[2 * i + 1] / s), __NV_SATFINITE, __NV_E4M3);
+        for (int i = 0; i < 4; ++i) q[i] = e4m3_quotients(v[2 * i], v[2 * i + 1], s, 1.0f / s);
         *reinterpret_cast<uint2*>(codes + row[u] * k + kb[u] * BK + sub * 8) =
             make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
       }
@@ -357,11 +374,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(bar_pfull(b), (g / NBUF) & 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < COLS; c += 32) {
-          float v[32];
-          tmem_ld32(tmem_base + lane_addr + b * BN + half * COLS + c, v);
+        for (int c = 0; c < COLS; c += 16) {
+          float v[16];
+          tmem_ld16(tmem_base + lane_addr + b * BN + half * COLS + c, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c + j] = fmaf(v[j], f, acc[c + j]);
+          for (int j = 0; j < 16; ++j) acc[c + j] = fmaf(v[j], f, acc[c + j]);
         }
         tc_fence_before();
         __syncwarp();

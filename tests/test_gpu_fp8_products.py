@@ -49,6 +49,29 @@ def test_the_activations_are_quantized_bit_exact_with_the_oracle(shape):
     np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), want_scales.view(np.uint32))
 
 
+def test_quantisation_on_rounding_midpoints_is_bit_exact():
+    """Quotients on e4m3 rounding midpoints (ties to even) and next to them: the kernel's fast path (a multiply by
+    the reciprocal, bracketed) hands these to the division, so the codes stay those of x / scale."""
+    levels = quant.e4m3_to_f32(np.arange(0, 0x7E, dtype=np.uint8)).astype(np.float64)
+    mids = (levels[1:] + levels[:-1]) / 2
+    rows = []
+    for scale_pow in (0, -3, 5):  # a row's largest value 448 * 2^p makes its scale 2^p: the quotients are exact
+        row = np.zeros(128, dtype=np.float32)
+        row[0] = 448.0 * 2.0 ** scale_pow
+        picks = mids[np.linspace(0, len(mids) - 1, 127).astype(int)]
+        row[1:] = (picks * 2.0 ** scale_pow * np.where(np.arange(127) % 2, -1, 1)).astype(np.float32)
+        rows.append(row)
+    rng = np.random.default_rng(0)
+    for _ in range(61):  # odd scales: quotients near the midpoints after rounding
+        row = (rng.choice(mids, 128) * rng.uniform(0.9, 1.1)).astype(np.float32)
+        rows.append(row)
+    x = torch.from_numpy(np.stack(rows)).to(DEV, torch.bfloat16)
+    codes, scales = _grouped._quantize_rows(x)
+    want_codes, want_scales = quant.quantize_rows(as_np(x))
+    np.testing.assert_array_equal(codes.cpu().numpy(), want_codes)
+    np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), want_scales.view(np.uint32))
+
+
 @pytest.mark.parametrize("is_transposed", [False, True])
 def test_the_fp8_product_quantizes_the_activations_per_row_and_stays_close(is_transposed):
     """The reference's test_grouped.py:66-79 on the same shapes, and the oracle's arithmetic."""

@@ -80,3 +80,29 @@ def test_only_the_default_silu_gate_on_a_k_major_stack_is_fused():
             return self.act_fn(gate.clamp(max=7.0)) * up
 
     assert not _moe._default_swiglu(Custom())
+
+
+def test_fp8_products_take_per_expert_scales_and_whole_128_blocks(monkeypatch):
+    """The FP8 products' stack: one scale per expert, or block scales whose blocks are whole 128 x 128 tiles (or
+    one block along a dimension); sizes multiples of 16. Others are refused, as the products cannot apply them."""
+    import pytest
+
+    codes = torch.zeros(3, 256, 384, dtype=torch.float8_e4m3fn)
+    st = _grouped.Fp8Stack.of(codes, torch.ones(3))
+    assert st.scale is not None and st.blocks is None
+    st = _grouped.Fp8Stack.of(codes, torch.full((3, 2, 3), 0.3))
+    ws, br, bc = st.blocks
+    assert (br, bc) == (128, 128) and ws.dtype == torch.float32
+    assert float(ws[0, 0, 0]) == float(torch.tensor(0.3).to(torch.bfloat16))  # rounded to bf16, as dequantised
+    assert _grouped.Fp8Stack.of(codes, torch.ones(3, 1, 1)).blocks[1:] == (256, 384)
+    with pytest.raises(NotImplementedError):
+        _grouped.Fp8Stack.of(codes, torch.ones(3, 4, 3))  # 64-row blocks
+    with pytest.raises(NotImplementedError):
+        _grouped.Fp8Stack.of(torch.zeros(3, 100, 384, dtype=torch.float8_e4m3fn), torch.ones(3))
+    monkeypatch.delenv("MEEPSQUARED_FP8_PRODUCTS", raising=False)
+    assert not _grouped._fp8_products_on(codes, None, torch.device("cpu"))
+    assert _grouped._fp8_products_on(codes, True, torch.device("cpu"))
+    assert not _grouped._fp8_products_on(torch.zeros(2, dtype=torch.bfloat16), True, torch.device("cpu"))
+    monkeypatch.setenv("MEEPSQUARED_FP8_PRODUCTS", "1")
+    assert _grouped._fp8_products_on(codes, None, torch.device("cpu"))
+    assert not _grouped._fp8_products_on(codes, False, torch.device("cpu"))
