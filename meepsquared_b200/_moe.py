@@ -412,6 +412,14 @@ def _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)
     return _Combine.apply(y, top_k_weights, routing).to(hidden_states.dtype)
 
 
+def _fp8_products_layer(experts, device) -> bool:
+    """Whether the layer's products run on the FP8 tensor cores: an FP8 stack (a stack of another kind, an NF4State
+    included, has no e4m3 dtype) and the reference's switch (fp8_products, _grouped.py:70-80)."""
+    fp8 = any(getattr(getattr(experts, n, None), "dtype", None) == torch.float8_e4m3fn
+              for n in ("gate_up_proj", "down_proj"))
+    return fp8 and _grouped.fp8_products(device)
+
+
 def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
     """The routed layer of an experts module with its adapters: _moe._routed_forward's contract.
 
@@ -424,10 +432,8 @@ def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
     """
     if not hidden_states.is_cuda:
         raise RuntimeError("the routed layer runs on a CUDA GPU (compute capability 10.0)")
-    fp8_products = any(getattr(experts, n, None) is not None and getattr(experts, n).dtype == torch.float8_e4m3fn
-                       for n in ("gate_up_proj", "down_proj")) and _grouped.fp8_products(hidden_states.device)
-    if not _default_swiglu(experts) or fp8_products or any(f[0] is not None and f[0].shape[2] > _grouped.RANK_MULTIPLE
-                                                           for f in factors.values()):
+    large_rank = any(f[0] is not None and f[0].shape[2] > _grouped.RANK_MULTIPLE for f in factors.values())
+    if not _default_swiglu(experts) or _fp8_products_layer(experts, hidden_states.device) or large_rank:
         # another gate, FP8 tensor-core products (their kernel has the plain epilogue), or adapters of rank above 16
         # (the products take them in 16-rank chunks)
         return _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)

@@ -106,3 +106,23 @@ def test_fp8_products_take_per_expert_scales_and_whole_128_blocks(monkeypatch):
     monkeypatch.setenv("MEEPSQUARED_FP8_PRODUCTS", "1")
     assert _grouped._fp8_products_on(codes, None, torch.device("cpu"))
     assert not _grouped._fp8_products_on(codes, False, torch.device("cpu"))
+
+
+def test_the_fp8_products_switch_reads_stacks_of_every_kind(monkeypatch):
+    """The routed layer's FP8-products test reads the stacks' dtype without assuming a tensor (an NF4 stack is an
+    NF4State): NF4 and bf16 modules stay on their paths with the switch on, an FP8 module follows the switch."""
+    from meepsquared_b200 import _moe
+
+    class Experts:
+        pass
+
+    nf4, bf16, fp8 = Experts(), Experts(), Experts()
+    nf4.gate_up_proj = nf4.down_proj = _nf4.NF4State.__new__(_nf4.NF4State)
+    bf16.gate_up_proj = bf16.down_proj = torch.zeros(2, 4, 4, dtype=torch.bfloat16)
+    fp8.gate_up_proj = fp8.down_proj = torch.zeros(2, 4, 4, dtype=torch.float8_e4m3fn)
+    cpu = torch.device("cpu")
+    monkeypatch.setenv("MEEPSQUARED_FP8_PRODUCTS", "1")
+    assert not _moe._fp8_products_layer(nf4, cpu) and not _moe._fp8_products_layer(bf16, cpu)
+    assert _moe._fp8_products_layer(fp8, cpu)
+    monkeypatch.delenv("MEEPSQUARED_FP8_PRODUCTS")
+    assert not _moe._fp8_products_layer(fp8, cpu)
