@@ -234,6 +234,19 @@ typedef struct meep2b_product_f8 {
 
 int meep2b_grouped_product_f8(const meep2b_product_f8* p, void* stream);
 
+/* ---------------------------------------------------------------------------------------------- SwiGLU gate */
+
+/* Transformers' _default_apply_gate, which the reference's routed forward calls as experts._apply_gate
+ * (_moe.py:119), for the layer's unfused form: h[r, j] = bf16(bf16(silu(g)) * u) with g = gate_up[r, j] and
+ * u = gate_up[r, inter + j]; gate_up (rows, 2 inter) and h (rows, inter) bf16, contiguous; inter a multiple of 8.
+ * The arithmetic of the fused products' SwiGLU epilogue. */
+int meep2b_swiglu(const void* gate_up, int64_t rows, int64_t inter, void* h, void* stream);
+
+/* Its backward: grad_gate_up[r, j] = bf16(dh u) sig(g) (1 + g (1 - sig(g))), grad_gate_up[r, inter + j] =
+ * dh bf16(silu(g)) (dh = grad_h[r, j]), as the fused dSwiGLU epilogue. */
+int meep2b_swiglu_backward(const void* gate_up, const void* grad_h, int64_t rows, int64_t inter, void* grad_gate_up,
+                           void* stream);
+
 /* _grouped._reduce / _grouped_reduce_kernel (_grouped.py:233-256,362-370): the adapters' gradients,
  * out[e, j, r] = bf16(scaling * sum over expert e's rows of g[row, j] * low[row, r]) for r < 16; g (rows, n) bf16
  * with row stride ldg, low (rows, 16) bf16, out (experts, n, 16) bf16. */

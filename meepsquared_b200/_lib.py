@@ -75,6 +75,8 @@ _SIGNATURES = {
                                           _p]),
     "meep2b_fp8_rows_quantize": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _i64, _p]),
     "meep2b_grouped_product_f8": (ctypes.c_int, [ctypes.POINTER(ProductF8), _p]),
+    "meep2b_swiglu": (ctypes.c_int, [_p, _i64, _i64, _p, _p]),
+    "meep2b_swiglu_backward": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _p]),
 }
 
 _lib = None
@@ -129,6 +131,7 @@ KERNELS_PER_CALL = {
     "meep2b_fp8_block_dequantize": 1, "meep2b_nf4_dequantize": 2, "meep2b_nf4_absmax": 1,
     "meep2b_merge_stack": 1,
     "meep2b_quant_multipliers": 1, "meep2b_fp8_rows_quantize": 1, "meep2b_grouped_product_f8": 1,
+    "meep2b_swiglu": 1, "meep2b_swiglu_backward": 1,
 }
 launches = {}
 

@@ -362,7 +362,13 @@ def _default_swiglu(experts) -> bool:
     (``_default_apply_gate``: the activation of the first half of the gate/up output times the second half) with a
     SiLU activation, on a gate/up stack stored (experts, 2I, hidden). A module without ``_apply_gate`` or ``act_fn``
     is taken as that default."""
-    if not experts.has_gate or experts.is_transposed:
+    return not experts.is_transposed and _default_gate(experts)
+
+
+def _default_gate(experts) -> bool:
+    """Whether the module's gate is Transformers' default SwiGLU gate with a SiLU activation, whatever the layout of
+    its stacks (the gate acts on the gate/up output, (rows, 2I) either way)."""
+    if not experts.has_gate:
         return False
     gate = getattr(type(experts), "_apply_gate", None)
     if gate is not None:
@@ -376,6 +382,32 @@ def _default_swiglu(experts) -> bool:
     return act is None or isinstance(act, torch.nn.SiLU) or type(act).__name__ == "SiLUActivation"
 
 
+class _SwiGLU(torch.autograd.Function):
+    """h = silu(gate) * up over the gate/up output (rows, 2I) on the library's kernel (meep2b_swiglu), the gate of
+    the unfused layer when the module's gate is Transformers' default; the backward on meep2b_swiglu_backward."""
+
+    @staticmethod
+    def forward(ctx, gate_up):
+        gate_up = gate_up.contiguous()
+        rows, inter = gate_up.shape[0], gate_up.shape[1] // 2
+        h = torch.empty((rows, inter), device=gate_up.device, dtype=torch.bfloat16)
+        _lib.check(_lib.load().meep2b_swiglu(_lib.ptr(gate_up), rows, inter, _lib.ptr(h), _lib.stream_of(gate_up)),
+                   "meep2b_swiglu")
+        ctx.save_for_backward(gate_up)
+        return h
+
+    @staticmethod
+    def backward(ctx, grad_h):
+        (gate_up,) = ctx.saved_tensors
+        grad_h = grad_h.contiguous().to(torch.bfloat16)
+        rows, inter = gate_up.shape[0], gate_up.shape[1] // 2
+        grad = torch.empty_like(gate_up)
+        _lib.check(_lib.load().meep2b_swiglu_backward(_lib.ptr(gate_up), _lib.ptr(grad_h), rows, inter,
+                                                      _lib.ptr(grad), _lib.stream_of(gate_up)),
+                   "meep2b_swiglu_backward")
+        return grad
+
+
 def _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors):
     """The routed layer for modules whose gate the epilogues do not compute (another activation or gating
     function, an ungated up projection, a transposed stack): the reference's structure (_moe.py:70-126) with every
@@ -383,8 +415,6 @@ def _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)
     the weighted un-permute on this package's kernels, and the module's own gate or activation in between."""
     routing = route(top_k_index, top_k_weights, experts.num_experts)
     x = _GatherRows.apply(hidden_states.to(torch.bfloat16), routing, top_k_weights)
-    rows = routing.perm.numel()  # rows past the last expert's end are the sentinels (ids >= num_experts)
-    sentinel = (torch.arange(rows, device=x.device) >= routing.offsets[-1].long()).unsqueeze(-1)
     t = bool(experts.is_transposed)
 
     def project(x, name, bias_name):
@@ -394,14 +424,19 @@ def _routed_unfused(experts, hidden_states, top_k_index, top_k_weights, factors)
         bias = getattr(experts, bias_name) if experts.has_bias else None
         if bias is not None:
             bias = bias.detach().to(torch.bfloat16).contiguous()
-        out = _grouped._LoraGroupedProduct.apply(x.to(torch.bfloat16).contiguous(), _stack(stack), scale,
-                                                 routing.offsets, t, cast(lhs), cast(rhs), float(scaling), bias, None)
-        return out.masked_fill(sentinel, 0.0)  # rows past the experts' ends are not written by the products
+        # The rows past the last expert's end (the sentinels, ids >= num_experts, which the reference masks,
+        # _moe.py:113-115) are neither written by the products nor read by anything after them: the products'
+        # tiles, the adapters' reductions and the combine cover the experts' rows only, and every operation in
+        # between is row by row. So no pass over the whole output masks them.
+        return _grouped._LoraGroupedProduct.apply(x.to(torch.bfloat16).contiguous(), _stack(stack), scale,
+                                                  routing.offsets, t, cast(lhs), cast(rhs), float(scaling), bias, None)
 
     act = getattr(experts, "act_fn", None) or torch.nn.functional.silu
     if experts.has_gate:
         gate_up = project(x, "gate_up_proj", "gate_up_proj_bias")
-        if hasattr(experts, "_apply_gate"):
+        if _default_gate(experts) and gate_up.dtype == torch.bfloat16 and (gate_up.shape[1] // 2) % 8 == 0:
+            h = _SwiGLU.apply(gate_up)
+        elif hasattr(experts, "_apply_gate"):
             h = experts._apply_gate(gate_up)
         else:  # Transformers' default gate
             gate, up = gate_up.chunk(2, dim=-1)

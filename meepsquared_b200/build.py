@@ -14,7 +14,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "libmeep2b.so")
 SOURCES = ["libmeep2b.cu", "capi.cu", "route.cu", "grouped_gemm.cu", "grouped_gemm_q.cuh", "grouped_gemm_qpair.cuh",
-           "reduce.cu", "quant.cu", "merge.cu", "fp8_products.cu", "common.cuh", "host.hpp"]
+           "reduce.cu", "quant.cu", "merge.cu", "fp8_products.cu", "swiglu.cu",
+           "common.cuh", "host.hpp"]
 
 
 def nvcc() -> str:

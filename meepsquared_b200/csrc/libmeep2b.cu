@@ -6,3 +6,4 @@
 #include "quant.cu"
 #include "merge.cu"
 #include "fp8_products.cu"
+#include "swiglu.cu"

@@ -98,12 +98,13 @@ def test_layer_at_baseline_shapes_matches_the_oracle(cfg, pair_mode, routed_rows
     check_against(res, oracle_layer(inp, idx), scaled=True)
 
 
+@pytest.mark.parametrize("sentinel", [False, True])
 @pytest.mark.parametrize("rank", [32, 40])
-def test_layer_with_adapters_of_rank_above_16_matches_the_oracle(rank):
+def test_layer_with_adapters_of_rank_above_16_matches_the_oracle(rank, sentinel):
     """Ranks above one fused panel's 16 (the reference pads any rank to a multiple of 16): the layer runs unfused,
-    each product taking the adapters in 16-rank chunks."""
+    each product taking the adapters in 16-rank chunks; with sentinel ids, whose rows nothing writes or reads."""
     inp = layer_inputs.layer(**dict(layer_inputs.CONFIG1, rank=rank, alpha=2 * rank))
-    res, idx = run_layer(inp)
+    res, idx = run_layer(inp, sentinel=sentinel)
     check_against(res, oracle_layer(inp, idx), scaled=True)
 
 
@@ -343,3 +344,19 @@ def test_modules_the_epilogues_do_not_fuse_take_the_unfused_layer(case):
         got["grad_gate_up_lhs"] = got["grad_gate_up_lhs"][:, : inp["gate_up"].shape[1] // 2]
     check_against(got, {k: v.cpu().numpy() for k, v in want.items()}, scaled=True)
 
+
+
+def test_the_unfused_gate_kernels_match_the_oracle():
+    """meep2b_swiglu / meep2b_swiglu_backward (the default gate of the unfused layer) against float32 SwiGLU: the
+    bf16 roundings of the fused epilogues (h = bf16(bf16(silu(g)) u)) and no more."""
+    from meepsquared_b200 import _moe
+    from oracle import grouped as ogrouped
+
+    gen = torch.Generator().manual_seed(9)
+    gate_up = (torch.randn(300, 400, generator=gen) * 3).to(DEV, torch.bfloat16).requires_grad_()
+    h = _moe._SwiGLU.apply(gate_up)
+    grad_h = torch.randn(300, 200, generator=gen).to(DEV, torch.bfloat16)
+    h.backward(grad_h)
+    assert_close(h.detach(), ogrouped.swiglu(as_np(gate_up.detach())), "h", scaled=True)
+    want = ogrouped.swiglu_backward(as_np(gate_up.detach()), as_np(grad_h))
+    assert_close(gate_up.grad, want, "grad_gate_up", scaled=True)
