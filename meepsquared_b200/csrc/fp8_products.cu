@@ -7,7 +7,7 @@
 //
 //  * quantize_rows_kernel: x (rows, k) bf16 -> codes (rows, k) e4m3 and scales (k/128 blocks, rows) float32,
 //    scale = max(amax over the row's 128 columns of the block, 1e-12) / 448, code = e4m3(x / scale) (round to
-//    nearest even); a half-warp per (row, block), memory bound (2 bytes read, 1 written per element).
+//    nearest even); eight lanes per (row, block), 2 bytes read and 1 written per element.
 //  * grouped_gemm_f8_kernel: persistent, one CTA per SM, one unit = 128 rows of one expert x 256 columns.
 //    Warp 0 loads the x codes and the stack's codes with TMA (128 x 128 and 256 x 128 bytes per k-block,
 //    128-byte swizzle); warp 1 issues tcgen05.mma kind::f8f6f4 (e4m3 x e4m3, float32 accumulation), four MMAs of depth 32
@@ -118,10 +118,12 @@ __device__ __forceinline__ uint32_t e4m3_quotients(float x0, float x1, float s, 
   return mag | ((__float_as_uint(x0) >> 24) & 0x80u) | ((__float_as_uint(x1) >> 16) & 0x8000u);
 }
 
-// One half-warp per (row, 128-column block), lane i of the half holding columns 8i..8i+7 of the block; each
-// half-warp issues the loads of four blocks before it uses any (16 bytes a lane each), to keep enough bytes in
-// flight for the HBM bandwidth.
-constexpr int Q_UNROLL = 4;
+// Eight lanes per (row, 128-column block), lane i of the eight holding columns 16i..16i+15 of the block (two
+// 16-byte loads); each group issues the loads of two blocks before it uses any, so 64 bytes a lane are in flight.
+// A block's two divisions (its scale and the scale's reciprocal) and its max reduction are shared by 16 elements a
+// lane.
+constexpr int Q_UNROLL = 2;
+constexpr int Q_LANES = 8;
 
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
                                                             int64_t ldx, uint8_t* __restrict__ codes,
@@ -129,49 +131,54 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
   const int kblocks = (k + BK - 1) / BK;
   const int64_t items = rows * kblocks;
   const bool small = items + static_cast<int64_t>(Q_UNROLL) * gridDim.x * blockDim.x < (int64_t(1) << 32);
-  const int sub = threadIdx.x & 15;
-  const int64_t half = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
-  const int64_t halves = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
-  // the loop bound is the warp's first half-warp's (halves is even), so both halves of a warp take the same trips
-  // and every full-mask shuffle has all 32 lanes; items past the end are masked by `valid`
-  for (int64_t warp_base = half & ~int64_t(1); warp_base < items; warp_base += Q_UNROLL * halves) {
-    const int64_t base = warp_base + (half & 1);
-    uint4 raw[Q_UNROLL];
+  const int sub = threadIdx.x & (Q_LANES - 1);
+  const int64_t group = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / Q_LANES;
+  const int64_t groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) / Q_LANES;
+  constexpr int PER_WARP = 32 / Q_LANES;
+  // the loop bound is the warp's first group's (groups is a multiple of PER_WARP), so all groups of a warp take
+  // the same trips and every full-mask shuffle has all 32 lanes; items past the end are masked by `valid`
+  for (int64_t warp_base = group & ~int64_t(PER_WARP - 1); warp_base < items; warp_base += Q_UNROLL * groups) {
+    const int64_t base = warp_base + (group & (PER_WARP - 1));
+    uint4 raw[Q_UNROLL][2];
     int64_t row[Q_UNROLL];
     int kb[Q_UNROLL];
     bool in[Q_UNROLL];
 #pragma unroll
     for (int u = 0; u < Q_UNROLL; ++u) {
-      const int64_t item = base + u * halves;
+      const int64_t item = base + u * groups;
       const bool valid = item < items;
       // a 32-bit division where the item count allows (a 64-bit one is a long emulated sequence)
       row[u] = !valid ? 0 : (small ? static_cast<int64_t>(static_cast<uint32_t>(item) / static_cast<uint32_t>(kblocks))
                                    : item / kblocks);
       kb[u] = valid ? static_cast<int>(item - row[u] * kblocks) : 0;
-      const int col = kb[u] * BK + sub * 8;
-      in[u] = valid && col < k;  // k is a multiple of 16: a lane's eight columns are all in range or all out
-      raw[u] = in[u] ? __ldg(reinterpret_cast<const uint4*>(x + row[u] * ldx + col)) : make_uint4(0, 0, 0, 0);
+      const int col = kb[u] * BK + sub * 16;
+      in[u] = valid && col < k;  // k is a multiple of 16: a lane's sixteen columns are all in range or all out
+      const uint4* src = reinterpret_cast<const uint4*>(x + row[u] * ldx + col);
+      raw[u][0] = in[u] ? __ldg(src) : make_uint4(0, 0, 0, 0);
+      raw[u][1] = in[u] ? __ldg(src + 1) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < Q_UNROLL; ++u) {
-      const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
-      float v[8];
+      const uint32_t w[8] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w,
+                             raw[u][1].x, raw[u][1].y, raw[u][1].z, raw[u][1].w};
+      float v[16];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[2 * i] = bf16_lo(w[i]), v[2 * i + 1] = bf16_hi(w[i]);
+      for (int i = 0; i < 8; ++i) v[2 * i] = bf16_lo(w[i]), v[2 * i + 1] = bf16_hi(w[i]);
       float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));  // within the half
+      for (int o = Q_LANES / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float s = fmaxf(amax, 1e-12f) / 448.0f;
       if (in[u]) {
-        uint32_t q[4];
+        const float rcp = 1.0f / s;
+        uint32_t q[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = e4m3_quotients(v[2 * i], v[2 * i + 1], s, 1.0f / s);
-        *reinterpret_cast<uint2*>(codes + row[u] * k + kb[u] * BK + sub * 8) =
-            make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
+        for (int i = 0; i < 8; ++i) q[i] = e4m3_quotients(v[2 * i], v[2 * i + 1], s, rcp);
+        *reinterpret_cast<uint4*>(codes + row[u] * k + kb[u] * BK + sub * 16) =
+            make_uint4(q[0] | (q[1] << 16), q[2] | (q[3] << 16), q[4] | (q[5] << 16), q[6] | (q[7] << 16));
       }
-      if (sub == 0 && base + u * halves < items) scales[static_cast<int64_t>(kb[u]) * ld_scales + row[u]] = s;
+      if (sub == 0 && base + u * groups < items) scales[static_cast<int64_t>(kb[u]) * ld_scales + row[u]] = s;
     }
   }
 }
@@ -463,7 +470,8 @@ extern "C" int meep2b_fp8_rows_quantize(const void* x, int64_t rows, int64_t k, 
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t items = rows * ((k + f8::BK - 1) / f8::BK);
-  const int64_t blocks = (items + 16 * f8::Q_UNROLL - 1) / (16 * f8::Q_UNROLL);  // 16 half-warps a block
+  const int64_t per_block = (256 / f8::Q_LANES) * f8::Q_UNROLL;  // items a block takes per trip
+  const int64_t blocks = (items + per_block - 1) / per_block;
   const int grid = static_cast<int>(blocks < int64_t(sms) * 8 ? blocks : int64_t(sms) * 8);
   f8::quantize_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,
                                                 codes, scales, ld_scales);
