@@ -7,11 +7,16 @@ A step is one forward + backward of the routed layer (routing, gather, gate/up w
 the whole backward, adapters' gradients included) over one batch of T tokens of BASELINE config 2 (Qwen3-30B-A3B:
 T=16384, hidden 2048, moe_intermediate 768, 128 experts, top-8, LoRA r=16 alpha 32, bf16). Synthetic seeded data
 (router logits ~N(0,1), stacks ~N(0,0.02)); every per-step tensor is far larger than the 126 MB L2, so no flush.
-At N>1 each rank runs its own batch (weak scaling) and the LoRA gradients are averaged with one NCCL all-reduce
-per step (the reference's DDP exchange). Rank 0 prints one JSON line.
+At N>1 each rank runs its own batch (weak scaling) and the LoRA gradients are averaged with NCCL all-reduces
+(the reference's DDP exchange). Rank 0 prints one JSON line.
 
---impl reference times the reference path's CPU implementation (the numpy oracle port of _moe._routed_forward,
-float32, all host threads) on a bounded sample of the same workload; rank 0 alone runs it.
+Beside the library's own numbers the line carries two baselines, both the reference's path restated with PyTorch
+operations (reference_routed_forward below, meepsquared/_moe.py:48-126 on its non-kernel branch):
+  gpu_baseline  that path on the same GPU in bf16: what the reference runs on a compute capability 10.0 GPU, where
+                its Triton kernel is not chosen (_grouped.wanted, _grouped.py:57-67) and the products are PyTorch's
+                grouped matmuls;
+  cpu_baseline  that path on the host cores in float32 (the reference's CPU path), rank 0 at N=1 only.
+--impl reference times the same CPU path alone (rank 0), with the same config, metric and unit.
 """
 
 import argparse
@@ -38,9 +43,9 @@ CONFIGS = {
     "half": dict(tokens=8192, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
 }
 METRIC = "MoE-LoRA layer fwd+bwd tokens/s"
-# DRAM bytes (read + write) per grouped-product launch at config 2, averaged over the step's four launches: from the
-# ncu capture summarised in profiles/grouped_gemm_half_qwen3_30b.md (half the tokens), weight bytes kept and
-# activation bytes doubled to the full workload.
+# DRAM bytes (read + write) per grouped-product launch at config 2, averaged over the step's four launches: from an
+# ncu capture of the same launches at half the tokens (the profile summary of the grouped products), the weight
+# bytes kept and the activation bytes doubled to the full workload.
 GEMM_TRAFFIC_BYTES_PER_LAUNCH = 1.67e9
 
 
@@ -50,11 +55,21 @@ def flop_per_token(c):
 
 
 def peaks():
+    """(bf16 sustained, bf16 burst, HBM GB/s, "measured" | "fallback") from MEASURED_PEAKS.json."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         p = json.load(open(path))
         return float(p["bf16_tflops_sustained"]), float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
     return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+def pick_peak(clocks, sustained, burst):
+    """The bf16 peak that matches the clock regime of the timed region: the burst figure (a GEMM timed alone, at
+    full clock) when the median SM clock sampled under load is within 5% of the maximum with no power cap seen;
+    the sustained one (seconds of GEMMs under the power cap) otherwise."""
+    sm, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    full = sm is not None and mx and sm >= 0.95 * mx and "sw_power_cap" not in clocks.get("reasons", [])
+    return (burst, "burst") if full else (sustained, "sustained")
 
 
 class ClockSampler:
@@ -261,7 +276,6 @@ def run_meep2b(a):
     timed_launches = mb._lib.launch_count() - launches_before
     sync()
     clocks.mark_stop()
-    clocks.__exit__()
     timer.active = False
     _grouped.set_launch_observer(None)
     ms = start.elapsed_time(stop)
@@ -332,48 +346,67 @@ def run_meep2b(a):
     sync()
     e_ms = e_start.elapsed_time(e_stop)
 
-    times = torch.tensor([ms, e_ms], device=device, dtype=torch.float64)
+    # the reference's own path on this GPU (bf16 stacks only: the reference has no NF4 stacks)
+    gpu_base = None
+    if not a.no_gpu_baseline:
+        gpu_base = gpu_baseline(c, ex, lora, hidden, idx, w, grad, s, a.steps, a.warmup, device)
+        sync()
+    clocks.__exit__()
+
+    times = torch.tensor([ms, e_ms, gpu_base["ms_per_step"] if gpu_base and "ms_per_step" in gpu_base else 0.0],
+                         device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms, e_ms = times.tolist()
+    ms, e_ms, base_ms = times.tolist()
     T = c["tokens"]
     value = world * T * a.steps / (ms / 1e3)
     e_value = world * T * e_steps / (e_ms / 1e3)
-    sustained, burst, hbm, peak_kind = peaks()
+    sustained, burst, hbm, peak_source = peaks()
+    clock_summary = clocks.summary()
+    bf16_peak, regime = pick_peak(clock_summary, sustained, burst)
     # MEEPSQUARED_FP8_PRODUCTS=1 on an FP8 stack: the frozen stack's products run e4m3 x e4m3 (the activations
     # quantised per row and 128-column tile); their roofline is the FP8 dense peak, taken as twice the measured bf16
     # one (the nominal ratio, 4.5 / 2.25 PFLOP/s), since no FP8 GEMM peak is measured on this pool
     fp8_products = str(c.get("quant", "")).startswith("fp8") and os.environ.get("MEEPSQUARED_FP8_PRODUCTS") == "1"
-    gemm_peak = 2 * sustained if fp8_products else sustained
+    gemm_peak = 2 * bf16_peak if fp8_products else bf16_peak
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
     layer_tflops = flop_per_token(c) * value / world / 1e12
     h2d = hidden.numel() * 2 + idx.numel() * idx.element_size() + w.numel() * 4 + grad.numel() * 2
     d2h = bucket.flat.numel() * bucket.flat.element_size()
+    if gpu_base and "ms_per_step" in gpu_base:
+        gpu_base["ms_per_step"] = round(base_ms, 4)
+        gpu_base["value"] = round(world * T / (base_ms / 1e3), 1)
+        gpu_base["frac_of_bf16_peak_layer"] = round(flop_per_token(c) * T / (base_ms / 1e3) / 1e12 / bf16_peak, 4)
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "e4m3 products, bf16 adapters" if fp8_products else "bf16",
         "data": "synthetic (seeded, BASELINE config shapes)",
-        "config": {"workload": a.config + " routed MoE-LoRA layer fwd+bwd", **c, "tokens_per_gpu": T,
-                   "parallelism": f"dp{world}", "l2": "per-step tensors >> 126 MB L2, no flush",
-                   **({"fp8_products": True} if fp8_products else {})},
-        "tensor_tflops_layer": round(layer_tflops, 1),
-        "frac_of_bf16_peak_layer": round(layer_tflops / sustained, 4),
+        "config": bench_config(a, c, world),
         "roofline": {"bound": "tensor", "kernel": "grouped_gemm (tcgen05), all product launches of the step",
                      "achieved": round(achieved, 1) if achieved else None, "peak": gemm_peak,
                      "unit": "TFLOP/s", "frac": round(achieved / gemm_peak, 4) if achieved else None,
-                     "peak_kind": (f"fp8 = 2 x bf16 sustained, {peak_kind}" if fp8_products
-                                   else f"bf16 sustained, {peak_kind}"),
+                     "peak_kind": (f"fp8 = 2 x bf16 {regime}, {peak_source}" if fp8_products
+                                   else f"bf16 {regime} ({'median SM clock at max' if regime == 'burst' else 'clock below max or power-capped'}), {peak_source}"),
+                     "frac_of_burst": round(achieved / ((2 if fp8_products else 1) * burst), 4) if achieved else None,
+                     "frac_of_sustained": (round(achieved / ((2 if fp8_products else 1) * sustained), 4)
+                                           if achieved else None),
                      "launches_timed": gemm_launches, "gemm_ms_per_step": round(gemm_ms / a.steps, 4),
                      "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH if a.config == "qwen3_30b" else None,
-                     "traffic_unit": "DRAM bytes per launch (ncu, profiles/grouped_gemm_half_qwen3_30b.md)"},
+                     "traffic_unit": "DRAM bytes per launch (ncu capture at half the tokens, scaled)",
+                     "layer": {"achieved": round(layer_tflops, 1), "peak": bf16_peak,
+                               "frac": round(layer_tflops / bf16_peak, 4),
+                               "flop_per_token": flop_per_token(c),
+                               "note": "algorithmic FLOPs of the whole layer step / step time, per GPU"}},
         "e2e": {"value": round(e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": timed_launches,  # libmeep2b kernels launched in the timed steps (counted per call)
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
     }
+    if gpu_base is not None:
+        result["gpu_baseline"] = gpu_base
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(c, a.cpu_tokens)
+        result["cpu_baseline"] = cpu_baseline(c)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -381,60 +414,222 @@ def run_meep2b(a):
         print(json.dumps(result), flush=True)
 
 
-def cpu_baseline(c, tokens):
-    """The oracle port (numpy float32, the reference path's algorithm) on `tokens` tokens of the workload."""
-    import numpy as np
+def bench_config(a, c, world):
+    """The `config` object of the JSON line: the same for both arms of the same run."""
+    return {"workload": a.config + " routed MoE-LoRA layer fwd+bwd", **c, "tokens_per_gpu": c["tokens"],
+            "parallelism": f"dp{world}", "l2": "per-step tensors >> 126 MB L2, no flush"}
 
+
+# ------------------------------------------------------------------------ the reference's path, restated
+
+def reference_lora_delta(x, lhs, rhs, scaling, offsets, is_transposed):
+    """scaling * x @ delta for each expert's rows, delta = lhs @ rhs in the stack's layout: the reference's
+    _grouped_lora (meepsquared/_moe.py:48-67). Two grouped matmuls of rank depth; the rank is padded with zeros to
+    a 16-byte row (the grouped matmul's stride rule) and the scaling goes into the small factor."""
+    import torch
+    from transformers.integrations.moe import _grouped_mm
+
+    pad = -lhs.shape[-1] % (16 // lhs.element_size())
+    if pad:
+        lhs = torch.nn.functional.pad(lhs, (0, pad))
+        rhs = torch.nn.functional.pad(rhs, (0, 0, 0, pad))
+    if is_transposed:  # stack (experts, in, out): x @ lhs @ rhs
+        first, second = (lhs * scaling).contiguous(), rhs.contiguous()
+    else:  # stack (experts, out, in): x @ rhs^T @ lhs^T
+        first, second = (rhs * scaling).transpose(-2, -1).contiguous(), lhs.transpose(-2, -1).contiguous()
+    return _grouped_mm(_grouped_mm(x, first, offs=offsets), second, offs=offsets)
+
+
+def reference_routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
+    """The reference's routed layer (meepsquared/_moe.py:_routed_forward, :70-126) on the branch it takes where its
+    kernel is not wanted (every CPU, and a compute capability 10.0 GPU: _grouped.py:57-67): sort the flat expert
+    ids, gather the rows, Transformers' grouped linear for each stack plus the adapters' change in place, sentinel
+    rows zeroed, the gate, the weighted un-permute. bf16 stacks (or float32 on the CPU) without FP8 scales."""
+    import torch
+    from transformers.integrations.moe import _grouped_linear
+
+    device = hidden_states.device
+    k = top_k_index.size(-1)
+    tokens, hidden_dim = hidden_states.size(0), hidden_states.size(-1)
+    experts_n = experts.num_experts
+    flat_ids = top_k_index.reshape(-1)
+    ids_sorted, perm = torch.sort(flat_ids)
+    rows = hidden_states[perm // k]
+    weights_sorted = top_k_weights.reshape(-1)[perm]
+    counts = torch.histc(ids_sorted.float() if device.type in ("cpu", "mps") else ids_sorted.int(),
+                         bins=experts_n, min=0, max=experts_n - 1)
+    offsets = torch.cumsum(counts, dim=0, dtype=torch.int32)
+    sentinel = (ids_sorted >= experts_n).unsqueeze(-1)
+    ids_sorted.clamp_(max=experts_n - 1)
+    rows = rows.masked_fill(sentinel, 0.0)
+
+    def project(x, name, bias_name):
+        lhs, rhs, scaling = factors.get(name, (None, None, 1.0))
+        bias = getattr(experts, bias_name)[ids_sorted] if experts.has_bias else None
+        out = _grouped_linear(x, getattr(experts, name), offsets, bias=bias, is_transposed=experts.is_transposed)
+        if lhs is not None:
+            out = out.add_(reference_lora_delta(x.to(lhs.dtype), lhs, rhs, scaling, offsets, experts.is_transposed))
+        return out.masked_fill_(sentinel, 0.0)
+
+    if experts.has_gate:
+        gate_up = project(rows, "gate_up_proj", "gate_up_proj_bias")
+        if hasattr(experts, "_apply_gate"):
+            h = experts._apply_gate(gate_up)
+        else:  # Transformers' default gate with the SiLU activation (Qwen3, Mixtral)
+            gate, up = gate_up.chunk(2, dim=-1)
+            h = torch.nn.functional.silu(gate) * up
+    else:
+        h = experts.act_fn(project(rows, "up_proj", "up_proj_bias"))
+    y = project(h, "down_proj", "down_proj_bias")
+    weighted = y * weights_sorted.unsqueeze(-1)
+    inverse = torch.empty_like(perm)
+    inverse[perm] = torch.arange(perm.size(0), device=device)
+    return weighted[inverse].view(tokens, k, hidden_dim).sum(dim=1).to(hidden_states.dtype)
+
+
+def gpu_baseline(c, ex, lora, hidden, idx, w, grad, scaling, steps, warmup, device):
+    """The reference's path on this GPU (reference_routed_forward, bf16), forward + backward with the gradients of
+    the hidden states, the routing weights and the four factors: W untimed steps, then K steps timed with CUDA
+    events on the launching stream."""
+    import torch
+
+    if c.get("quant"):
+        return {"unavailable": "quantised stacks: the reference dequantises FP8 per product and has no NF4 stacks"}
+    leaves = {n: t.detach().clone().requires_grad_() for n, t in lora.items()}
+    factors = {"gate_up_proj": (leaves["lhs1"], leaves["rhs1"], scaling),
+               "down_proj": (leaves["lhs2"], leaves["rhs2"], scaling)}
+    weights = w.detach().clone().requires_grad_()
+
+    def step():
+        h = hidden.detach().requires_grad_()
+        weights.grad = None
+        for t in leaves.values():
+            t.grad = None
+        out = reference_routed_forward(ex, h, idx, weights, factors)
+        out.backward(grad)
+
+    for _ in range(max(1, warmup)):
+        step()
+    stream = torch.cuda.current_stream(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(stop) / steps
+    return {"ms_per_step": ms, "unit": "tokens/s", "steps": steps, "warmup": max(1, warmup),
+            "impl": "the reference's _routed_forward, non-kernel branch (torch grouped_mm + _grouped_lora), bf16",
+            "kind": "port"}
+
+
+# ------------------------------------------------------------------------ the reference's path on the host cores
+
+def cpu_inputs(c, tokens):
+    """The workload's seeded inputs (float32, CPU) for its first `tokens` tokens: the per-token tensors of the full
+    batch cut to a sample, the full stacks and adapters."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import layer_inputs
-    from oracle import layer as olayer
 
-    cfg = {k: v for k, v in c.items() if k != "quant"}  # a quantised config's CPU leg runs the weights dequantised
-    cfg["tokens"] = tokens
+    cfg = {k: v for k, v in c.items() if k not in ("quant",)}  # a quantised config's CPU leg runs bf16-valued stacks
     inp = layer_inputs.layer(**cfg)
-    fac = {"gate_up_proj": (inp["gate_up_lhs"].numpy(), inp["gate_up_rhs"].numpy(), inp["scaling"]),
-           "down_proj": (inp["down_lhs"].numpy(), inp["down_rhs"].numpy(), inp["scaling"])}
-    args = (inp["hidden"].numpy(), inp["top_k_index"].numpy(), inp["top_k_weights"].numpy(), inp["gate_up"].numpy(),
-            inp["down"].numpy(), fac)
+    if tokens < c["tokens"]:
+        for n in ("hidden", "top_k_index", "top_k_weights", "grad"):
+            inp[n] = inp[n][:tokens].contiguous()
+    return inp
+
+
+def run_cpu_reference(inp, c, steps, warmup):
+    """Seconds per step of reference_routed_forward + backward on the host cores, float32, all host threads."""
+    import types
+
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)  # a launcher (torchrun) sets OMP_NUM_THREADS=1 for its ranks
+    ex = types.SimpleNamespace(num_experts=c["experts"], has_gate=True, has_bias=False, is_transposed=False,
+                               gate_up_proj=inp["gate_up"], down_proj=inp["down"])
+    s = inp["scaling"]
 
     def once():
-        out, saved = olayer.forward(*args)
-        olayer.backward(inp["grad"].numpy(), saved, inp["gate_up"].numpy(), inp["down"].numpy(), fac)
+        leaves = {n: inp[n].clone().requires_grad_() for n in ("gate_up_lhs", "gate_up_rhs", "down_lhs", "down_rhs")}
+        factors = {"gate_up_proj": (leaves["gate_up_lhs"], leaves["gate_up_rhs"], s),
+                   "down_proj": (leaves["down_lhs"], leaves["down_rhs"], s)}
+        h = inp["hidden"].clone().requires_grad_()
+        wts = inp["top_k_weights"].clone().requires_grad_()
+        t0 = time.perf_counter()
+        out = reference_routed_forward(ex, h, inp["top_k_index"], wts, factors)
+        out.backward(inp["grad"])
+        return time.perf_counter() - t0
 
-    # all host cores: a launcher (torchrun) sets OMP_NUM_THREADS=1 for its ranks, so the BLAS pool is raised here
-    from threadpoolctl import threadpool_info, threadpool_limits
-
-    with threadpool_limits(limits=os.cpu_count()):
+    for _ in range(warmup):
         once()
-        reps = []
-        t_end = time.perf_counter() + 10.0
-        while len(reps) < 3 or (time.perf_counter() < t_end and len(reps) < 20):
-            t0 = time.perf_counter()
-            once()
-            reps.append(time.perf_counter() - t0)
-        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
-    sec = statistics.median(reps)
-    del np
-    return {"value": round(tokens / sec, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{tokens} tokens of the workload (all {c['experts']} experts), fwd+bwd, float32 numpy, "
-                      f"median of {len(reps)}" + (", stacks already dequantised" if c.get("quant") else "")}
+    return [once() for _ in range(steps)], torch.get_num_threads()
+
+
+def sample_tokens(c, seconds_full, steps, budget_s):
+    """Tokens per step of a CPU leg: the whole batch when `steps` steps of it fit in `budget_s`, else the largest
+    power of two (at least 2048, every expert still ~128 routed rows at config 2) that does."""
+    T = c["tokens"]
+    if seconds_full * steps <= budget_s:
+        return T
+    t = 2048
+    while t * 2 < T and seconds_full * (t * 2 / T) * steps <= budget_s:
+        t *= 2
+    return min(t, T)
+
+
+def cpu_baseline(c):
+    """The reference's CPU path timed on the host cores: the benchmarked workload (its whole batch when a step
+    fits the ~30 s budget, else a leading sample of its tokens) and BASELINE config 1 in full."""
+    import torch
+
+    full = cpu_inputs(c, c["tokens"])
+    probe, _ = run_cpu_reference(full, c, 1, 1)
+    tokens = sample_tokens(c, probe[0], 3, 30.0)
+    inp = full if tokens == c["tokens"] else cpu_inputs(c, tokens)
+    reps, threads = run_cpu_reference(inp, c, 3, 0 if tokens == c["tokens"] else 1)
+    sec = statistics.median(reps + (probe if tokens == c["tokens"] else []))
+    c1 = dict(tokens=512, hidden=256, inter=512, experts=8, top_k=2, rank=8, alpha=16)
+    r1, _ = run_cpu_reference(cpu_inputs(c1, 512), c1, 20, 3)
+    sec1 = statistics.median(r1)
+    del torch
+    return {"value": round(tokens / sec, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "host_cpus": os.cpu_count(),
+            "sample": (f"{tokens} of the workload's {c['tokens']} tokens per step (all {c['experts']} experts), "
+                       f"fwd+bwd, float32 eager PyTorch (the reference's _routed_forward restated), median of "
+                       f"{len(reps)}" + (", stacks bf16-valued" if c.get("quant") else "")),
+            "config1": {"value": round(512 / sec1, 1), "unit": "tokens/s", "ms_per_step": round(sec1 * 1e3, 3),
+                        "config": c1, "sample": "the whole config (512 tokens), median of 20 after 3 warm-ups"}}
 
 
 def run_reference(a):
+    """--impl reference: the reference's path on the host cores (rank 0 alone), float32, the same config, metric and
+    unit as the library's arm. Each step runs the whole batch when W + K steps fit in ~4 minutes, else the same
+    leading sample of its tokens every step."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     c = CONFIGS[a.config]
-    cb = cpu_baseline(c, a.cpu_tokens)
-    value = cb["value"]
+    full = cpu_inputs(c, c["tokens"])
+    probe, _ = run_cpu_reference(full, c, 1, 1)
+    tokens = sample_tokens(c, probe[0], a.steps + a.warmup, 240.0)
+    inp = full if tokens == c["tokens"] else cpu_inputs(c, tokens)
+    reps, threads = run_cpu_reference(inp, c, a.steps, a.warmup)
+    sec = sum(reps) / len(reps)
+    value = round(tokens / sec, 1)
+    sample = (f"{tokens} of the workload's {c['tokens']} tokens per step (all {c['experts']} experts), fwd+bwd, "
+              f"float32 eager PyTorch (the reference's _routed_forward restated), mean of {a.steps} steps after "
+              f"{a.warmup} warm-ups")
     print(json.dumps({
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": round(1e3 * a.cpu_tokens / value, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1e3 * sec, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config shapes)", "impl": "reference",
-        "config": {"workload": a.config + " routed MoE-LoRA layer fwd+bwd", **c},
-        "cpu_baseline": cb, "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                                    "d2h_bytes_per_step": 0}}), flush=True)
+        "config": bench_config(a, c, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "host_cpus": os.cpu_count(), "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
 
 def main():
@@ -444,8 +639,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="meep2b", choices=["meep2b", "reference"])
     ap.add_argument("--config", default="qwen3_30b", choices=sorted(CONFIGS))
-    ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-baseline", action="store_true")
     a = ap.parse_args()
     if a.warmup < 3 and a.impl == "meep2b":
         a.warmup = 3

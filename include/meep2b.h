@@ -64,7 +64,7 @@ size_t meep2b_route_workspace_bytes(int64_t assignments, int32_t experts);
  * perm[i] = flat index of the i-th assignment in expert order (ties keep their flat order; ids >= experts, and
  * negative ids, are sentinels and sort last), expert_ids_g[i] = min(id, experts - 1), offsets[e] = inclusive
  * cumulative row count of experts 0..e (int32, sentinels not counted), inverse[perm[i]] = i (_moe.py:124-125).
- * expert_ids_g and inverse may be NULL. */
+ * expert_ids_g and inverse may be NULL. At most INT32_MAX assignments (positions and offsets are int32). */
 int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
                  int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* workspace,
                  size_t workspace_bytes, void* stream);
@@ -77,11 +77,12 @@ int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts
  * GPU loading the library holds until the process exits; it calls no cudaMalloc, cudaFree or other allocating
  * routine. Limit: ceil(assignments / 4096) * (experts + 1) <= 65536 (for example 262,144 assignments over up to
  * 1023 experts, or 1,048,576 over up to 255); larger requests return MEEP2B_ERR_SHAPE before any work. The first
- * call on a device looks up the array's device address with cudaGetSymbolAddress (with that device current) and
- * caches it, so make that first call before any stream capture. All calls share the one array: calls that overlap
- * on the GPU (two streams, or two host threads on one device) race and must be serialised by the caller. Outputs
- * and arguments as meep2b_route; every table entry a call reads is written earlier in the same call, so nothing
- * from a previous call carries over. */
+ * call on a device looks up the array's device address with cudaGetSymbolAddress (with that device current), so
+ * make that first call before any stream capture; later calls outside a capture look it up again (it can move
+ * after cudaDeviceReset), calls on a capturing stream reuse the last lookup. All calls share the one array: calls
+ * that overlap on the GPU (two streams, or two host threads on one device) race and must be serialised by the
+ * caller. Outputs and arguments as meep2b_route; every table entry a call reads is written earlier in the same
+ * call, so nothing from a previous call carries over. */
 int meep2b_route_noalloc(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
                          int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* stream);
 

@@ -397,8 +397,8 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
             const float ub = hlf ? bf16_hi(uw[b][j]) : bf16_lo(uw[b][j]);
             const float dh_u = __uint_as_float(acc[b][2 * j + hlf]) * sc;
             const float dh = bf16_round(dh_u * rw);
-            const float sig = sigmoid_f(gb);  // one exponential and one reciprocal per element
-            const float act = bf16_round(gb * sig);
+            const float act = bf16_round(silu_f(gb));  // the forward's activation, bit for bit
+            const float sig = sigmoid_f(gb);            // shares the exponential and reciprocal with silu_f
             if (p.w_grad != nullptr && 2 * j + hlf < cnt) wpart += dh_u * bf16_round(act * ub);  // h = bf16(act u)
             const float dact = bf16_round(dh * ub);
             duo[hlf] = dh * act;

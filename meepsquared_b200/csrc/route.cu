@@ -307,7 +307,9 @@ size_t meep2b_route_workspace_bytes(int64_t assignments, int32_t experts) {
 int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
                  int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* workspace,
                  size_t workspace_bytes, void* stream) {
-  if (experts < 1 || experts + 1 > kMaxBuckets || assignments < 0) return MEEP2B_ERR_SHAPE;
+  // positions and offsets are int32 in the kernels (as the reference's int32 offsets, _moe.py:84)
+  if (experts < 1 || experts + 1 > kMaxBuckets || assignments < 0 || assignments > INT32_MAX)
+    return MEEP2B_ERR_SHAPE;
   if (workspace_bytes < meep2b_route_workspace_bytes(assignments, experts)) return MEEP2B_ERR_SHAPE;
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
@@ -430,8 +432,10 @@ int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32
 // must not call cudaMalloc because it would synchronise the device or break a memory budget. For them,
 // meep2b_route_noalloc keeps that table in a fixed array in device memory that this library declares at file
 // scope, so the call allocates nothing. The array lives on every GPU that loads the library until the process
-// exits. Its host-side name is only a stand-in for the symbol: the device address is fetched once per device with
-// cudaGetSymbolAddress and cached.
+// exits. Its host-side name is only a stand-in for the symbol: the device address comes from cudaGetSymbolAddress
+// (which allocates nothing), looked up again on each call made outside a stream capture, so that it stays right
+// after a cudaDeviceReset (the module is loaded anew and the array may move); a call on a stream being captured
+// uses the address of the last lookup on that device.
 namespace meep2b {
 
 constexpr int64_t kNoAllocRouteWords = 65536;  // 256 KB of int32 bucket counts
@@ -441,16 +445,22 @@ constexpr int kMaxDevices = 64;
 static int* g_route_scratch_addr[kMaxDevices] = {nullptr};
 static std::mutex g_route_scratch_mutex;
 
-// The device address of g_route_scratch on the current device, fetched on first use (with that device current).
-static int route_scratch_address(int** out) {
+// The device address of g_route_scratch on the current device (the stream's, made current by bind_stream_device):
+// looked up with that device current unless the stream is being captured and an earlier lookup exists.
+static int route_scratch_address(cudaStream_t stream, int** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
     return MEEP2B_ERR_LAUNCH;
   }
   if (dev < 0 || dev >= kMaxDevices) return MEEP2B_ERR_DEVICE;
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capturing) != cudaSuccess) {
+    cudaGetLastError();
+    return MEEP2B_ERR_LAUNCH;
+  }
   std::lock_guard<std::mutex> lock(g_route_scratch_mutex);
-  if (g_route_scratch_addr[dev] == nullptr) {
+  if (capturing == cudaStreamCaptureStatusNone || g_route_scratch_addr[dev] == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_route_scratch) != cudaSuccess || p == nullptr) {
       cudaGetLastError();
@@ -473,7 +483,7 @@ extern "C" int meep2b_route_noalloc(const int64_t* expert_ids, int64_t assignmen
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
   int* counts = nullptr;
-  MEEP2B_TRY(route_scratch_address(&counts));
+  MEEP2B_TRY(route_scratch_address(s, &counts));
   if (assignments == 0) {
     cudaMemsetAsync(offsets, 0, sizeof(int32_t) * experts, s);
     return launch_status();

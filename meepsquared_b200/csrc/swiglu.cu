@@ -47,8 +47,8 @@ __global__ void __launch_bounds__(256) swiglu_backward_rows(const uint4* __restr
         const float gb = hl ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
         const float ub = hl ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
         const float dh = hl ? bf16_hi(dw[j]) : bf16_lo(dw[j]);
+        const float act = bf16_round(gemm::silu_f(gb));  // the forward's activation, bit for bit
         const float sig = gemm::sigmoid_f(gb);
-        const float act = bf16_round(gb * sig);
         const float dact = bf16_round(dh * ub);
         du[hl] = dh * act;
         dg[hl] = dact * sig * (1.0f + gb * (1.0f - sig));

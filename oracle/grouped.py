@@ -7,6 +7,8 @@ the adapters' (PEFT's lhs / rhs), none for the frozen stack, its scale, the offs
 
 import numpy as np
 
+from .quant import bf16
+
 
 def _segments(offsets):
     start = 0
@@ -103,7 +105,7 @@ def fp8_product(x, codes, scale, offsets, is_transposed, lhs=None, rhs=None, sca
     block_scale: None, or a function (e, b, c) -> the stack's scale of k-block b and 128-column block c (a
     block-scaled stack; then scale is None).
     """
-    from .quant import bf16, e4m3_to_f32, quantize_rows
+    from .quant import e4m3_to_f32, quantize_rows
 
     x = np.asarray(x, dtype=np.float32)
     x8, xs = quantize_rows(x, block)
@@ -141,20 +143,34 @@ def silu(v):
     return (v / (np.float32(1.0) + np.exp(-v))).astype(np.float32)
 
 
-def swiglu(gate_up):
-    """Transformers' _default_apply_gate: gate, up = chunk(2, -1); silu(gate) * up."""
+def swiglu(gate_up, round_bf16=False):
+    """Transformers' _default_apply_gate: gate, up = chunk(2, -1); silu(gate) * up.
+
+    round_bf16: the gate on bf16 tensors, as PyTorch computes it there: act = bf16(silu(gate)), h = bf16(act * up).
+    """
     gu = np.asarray(gate_up, dtype=np.float32)
     i = gu.shape[1] // 2
+    if round_bf16:
+        return bf16(bf16(silu(gu[:, :i])) * gu[:, i:])
     return silu(gu[:, :i]) * gu[:, i:]
 
 
-def swiglu_backward(gate_up, grad_h):
-    """d/d(gate, up) of silu(gate) * up: (dh * up * silu'(gate), dh * silu(gate)) concatenated."""
+def swiglu_backward(gate_up, grad_h, round_bf16=False):
+    """d/d(gate, up) of silu(gate) * up: (dh * up * silu'(gate), dh * silu(gate)) concatenated.
+
+    round_bf16: autograd's gradients on bf16 tensors: d_act = bf16(dh * up), d_up = bf16(dh * bf16(silu(gate))),
+    d_gate = bf16(d_act * sigmoid(gate) * (1 + gate * (1 - sigmoid(gate)))) (SiLU's backward in float32, rounded).
+    """
     gu = np.asarray(gate_up, dtype=np.float32)
     i = gu.shape[1] // 2
     g, u = gu[:, :i], gu[:, i:]
     sig = (np.float32(1.0) / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
     dh = np.asarray(grad_h, dtype=np.float32)
+    if round_bf16:
+        d_act = bf16(dh * u)
+        dg = bf16(d_act * sig * (np.float32(1.0) + g * (np.float32(1.0) - sig)))
+        du = bf16(dh * bf16(silu(g)))
+        return np.concatenate([dg, du], axis=1).astype(np.float32)
     dg = dh * u * sig * (np.float32(1.0) + g * (np.float32(1.0) - sig))
     du = dh * g * sig
     return np.concatenate([dg, du], axis=1).astype(np.float32)

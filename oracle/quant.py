@@ -26,8 +26,9 @@ ABSMAX_BLOCK = 256
 def bf16_bits(x) -> np.ndarray:
     """float32 -> bf16 bit patterns (uint16), round to nearest even; NaN stays NaN."""
     f = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
-    b = f.view(np.uint32).astype(np.uint64)
-    rounded = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    b = f.view(np.uint32)
+    # in uint32: no finite value (nor an infinity) overflows b + 0x8000; NaNs are set below
+    rounded = ((b + (np.uint32(0x7FFF) + ((b >> np.uint32(16)) & np.uint32(1)))) >> np.uint32(16)).astype(np.uint16)
     nan = np.isnan(f)
     if nan.any():
         rounded = rounded.copy()

@@ -13,6 +13,8 @@ Files:
   routing.npz       the reference's sort / histc / cumsum on seeded router outputs (torch.sort, stable and not)
   layer_small.npz   _moe._routed_forward, forward and backward, float32, SMALL config (and a sentinel case)
   layer_config1.npz the same at BASELINE config 1 (T=512, H=256, I=512, E=8, top-2, r=8): slices and norms
+  layer_bf16.npz    _moe._routed_forward on a bf16 model (config 2's H, I and rank, 128 tokens, 16 experts;
+                    the adapters' gradients of every fifth expert)
   fp8_stack.npz     _fp8.quantize_stack / dequantize_stack (one scale per expert)
   fp8_block.npz     axolotl quantize.quantize_fp8 / dequantize_fp8 with 128x128 block scales, tails included
   grouped.npz       _grouped.reference_lora forward + backward, float32, the reference tests' ragged case
@@ -30,6 +32,10 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 import layer_inputs  # noqa: E402
+
+
+# The bf16 case: config 2's hidden and intermediate sizes and rank, 128 tokens over 16 experts
+LAYER_BF16 = dict(layer_inputs.QWEN3_30B, tokens=128, experts=16)
 
 
 def import_reference(root):
@@ -138,6 +144,35 @@ def run_layer(moe, cfg, sentinel=False):
     res = {"out": out.detach().numpy(), "grad_hidden": hidden.grad.numpy(), "grad_weights": weights.grad.numpy()}
     for n, t in leaves.items():
         res[f"grad_{n}"] = t.grad.numpy()
+    return res
+
+
+def run_layer_bf16(moe, cfg):
+    """_moe._routed_forward forward + backward on a bf16 model (a bf16 Qwen3MoeExperts, bf16 hidden states and
+    factors, float32 routing weights, bf16 upstream gradient): the reference's bf16 path, every intermediate tensor
+    rounded where PyTorch rounds it."""
+    from transformers.models.qwen3_moe.configuration_qwen3_moe import Qwen3MoeConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeExperts
+
+    c = dict(cfg)
+    inp = layer_inputs.layer(**c)
+    conf = Qwen3MoeConfig(hidden_size=c["hidden"], moe_intermediate_size=c["inter"], num_experts=c["experts"],
+                          num_experts_per_tok=c["top_k"])
+    experts = Qwen3MoeExperts(conf).to(torch.bfloat16)
+    experts.gate_up_proj = torch.nn.Parameter(inp["gate_up"].to(torch.bfloat16), requires_grad=False)
+    experts.down_proj = torch.nn.Parameter(inp["down"].to(torch.bfloat16), requires_grad=False)
+    hidden = inp["hidden"].to(torch.bfloat16).requires_grad_()
+    weights = inp["top_k_weights"].clone().requires_grad_()
+    leaves = {n: inp[n].to(torch.bfloat16).requires_grad_()
+              for n in ("gate_up_lhs", "gate_up_rhs", "down_lhs", "down_rhs")}
+    factors = {"gate_up_proj": (leaves["gate_up_lhs"], leaves["gate_up_rhs"], inp["scaling"]),
+               "down_proj": (leaves["down_lhs"], leaves["down_rhs"], inp["scaling"])}
+    os.environ.pop("MEEPSQUARED_GROUPED_KERNEL", None)
+    out = moe._routed_forward(experts, hidden, inp["top_k_index"], weights, factors)
+    out.backward(inp["grad"].to(torch.bfloat16))
+    res = {"out": bits(out), "grad_hidden": bits(hidden.grad), "grad_weights": weights.grad.numpy()}
+    for n, t in leaves.items():  # the adapters' gradients of experts 0, 5, 10 and 15
+        res[f"grad_{n}"] = bits(t.grad[::5])
     return res
 
 
@@ -258,6 +293,7 @@ def main(root):
         keep[f"{name}_sample"] = v.reshape(-1)[::97]
         keep[f"{name}_norm"] = np.array(np.linalg.norm(v.astype(np.float64)))
     np.savez_compressed(os.path.join(HERE, "layer_config1.npz"), **keep)
+    np.savez_compressed(os.path.join(HERE, "layer_bf16.npz"), **run_layer_bf16(moe, LAYER_BF16))
     np.savez_compressed(os.path.join(HERE, "fp8_stack.npz"), **fp8_stacks(fp8))
     np.savez_compressed(os.path.join(HERE, "fp8_block.npz"), **fp8_blocks(q))
     np.savez_compressed(os.path.join(HERE, "grouped.npz"), **grouped_case(grouped))

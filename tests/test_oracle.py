@@ -82,6 +82,45 @@ def test_layer_matches_the_reference_at_config1(golden):
         assert abs(np.linalg.norm(v.astype(np.float64)) - float(g[name + "_norm"])) <= 1e-4 * float(g[name + "_norm"])
 
 
+def test_layer_with_bf16_intermediates_stays_within_the_references_bf16_path(golden):
+    """The oracle's bf16 mode (the layer's intermediate tensors rounded to bf16 where they are stored) against the
+    reference's own _routed_forward on a bf16 model (golden vectors at config 2's H, I and rank). The reference's
+    bf16 path rounds more often (the base product and the adapters' change separately, then their sum), so neither
+    side is the other's bits: they agree to bf16 arithmetic's noise, the layer output and input gradient
+    elementwise within the north star's abs 1e-2 + rel 2e-2, every tensor within 1% of its RMS."""
+    g = golden("layer_bf16")
+    inp = layer_inputs.layer(**dict(layer_inputs.QWEN3_30B, tokens=128, experts=16))
+    factors = {"gate_up_proj": (inp["gate_up_lhs"].numpy(), inp["gate_up_rhs"].numpy(), inp["scaling"]),
+               "down_proj": (inp["down_lhs"].numpy(), inp["down_rhs"].numpy(), inp["scaling"])}
+    out, saved = layer.forward(inp["hidden"].numpy(), inp["top_k_index"].numpy(), inp["top_k_weights"].numpy(),
+                               inp["gate_up"].numpy(), inp["down"].numpy(), factors, bf16_intermediates=True)
+    grads = layer.backward(inp["grad"].numpy(), saved, inp["gate_up"].numpy(), inp["down"].numpy(), factors)
+    assert np.array_equal(out, quant.bf16(out)) and np.array_equal(grads["hidden"], quant.bf16(grads["hidden"]))
+    mine = {"out": out, "grad_hidden": grads["hidden"], "grad_weights": grads["top_k_weights"],
+            "grad_gate_up_lhs": grads["gate_up_proj"][0][::5], "grad_gate_up_rhs": grads["gate_up_proj"][1][::5],
+            "grad_down_lhs": grads["down_proj"][0][::5], "grad_down_rhs": grads["down_proj"][1][::5]}
+    for name, v in mine.items():
+        ref = g[name] if g[name].dtype == np.float32 else quant.bf16_to_f32(g[name])
+        err = np.abs(v - ref)
+        assert np.sqrt(np.mean(err ** 2)) <= 0.01 * np.sqrt(np.mean(ref ** 2)), name
+        if name in ("out", "grad_hidden"):
+            assert np.all(err <= 1e-2 + 2e-2 * np.abs(ref)), name
+
+
+def test_bf16_intermediates_are_rounded_where_the_reference_rounds_them():
+    """The bf16 mode differs from the float32 oracle only by the roundings it states: on inputs whose products
+    are exact in float32 (small integers times powers of two) every intermediate is the float32 value rounded."""
+    rng = np.random.default_rng(2)
+    gu = (rng.integers(-300, 300, size=(6, 8)) / 64.0).astype(np.float32)
+    h = grouped.swiglu(gu, round_bf16=True)
+    act = quant.bf16(grouped.silu(gu[:, :4]))
+    np.testing.assert_array_equal(h, quant.bf16(act * gu[:, 4:]))
+    dh = quant.bf16(rng.standard_normal((6, 4)).astype(np.float32))
+    d = grouped.swiglu_backward(gu, dh, round_bf16=True)
+    np.testing.assert_array_equal(d[:, 4:], quant.bf16(dh * act))
+    assert np.array_equal(d, quant.bf16(d))
+
+
 @pytest.mark.parametrize("prefix,is_transposed", [("n_", False), ("t_", True)])
 def test_grouped_product_matches_reference_lora(golden, prefix, is_transposed):
     g = golden("grouped")
