@@ -243,7 +243,7 @@ def run_meep2b(a):
     hidden_leaf = hidden.clone().requires_grad_()
 
     def step(h, ids, wts, g):
-        bucket.zero()
+        bucket.release()  # the layer's reductions write the adapters' gradients into the bucket
         h.grad = None  # the input gradient is made fresh each step (in a model it flows on to the previous layer)
         out = mb.routed_forward(ex, h, ids, wts, factors)
         out.backward(g)

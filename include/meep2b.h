@@ -112,6 +112,13 @@ int meep2b_unpermute_backward(const void* grad_out, const void* y, const int64_t
                               int32_t weights_dtype, const int32_t* offsets, int32_t experts, int64_t assignments,
                               int32_t top_k, int64_t hidden_dim, void* grad_y, float* grad_weights, void* stream);
 
+/* The routing weights' gradient when the un-permute's backward is folded into the down stack's input-gradient
+ * product (meep2b_product.w_grad, per routed row and 96-column block <dh, h> = <g, y>): grad_weights[perm[i]] =
+ * sum_{b < blocks} parts[i * ld + b], summed in order of b in float32, for the experts' rows i < offsets[experts-1],
+ * and 0 for the sentinel rows. The weights' part of the backward of _moe.py:123-126 (weighted = out * w_g). */
+int meep2b_weight_grad(const float* parts, int64_t ld, int32_t blocks, const int64_t* perm, int64_t assignments,
+                       const int32_t* offsets, int32_t experts, float* grad_weights, void* stream);
+
 /* ---------------------------------------------------------------------------------------------- tile map */
 
 /* _grouped.tile_map (_grouped.py:88-103) on the device: tile_expert / tile_row get max_tiles(rows, experts,
@@ -250,9 +257,11 @@ int meep2b_swiglu_backward(const void* gate_up, const void* grad_h, int64_t rows
 
 /* _grouped._reduce / _grouped_reduce_kernel (_grouped.py:233-256,362-370): the adapters' gradients,
  * out[e, j, r] = bf16(scaling * sum over expert e's rows of g[row, j] * low[row, r]) for r < 16; g (rows, n) bf16
- * with row stride ldg, low (rows, 16) bf16, out (experts, n, 16) bf16. */
+ * with row stride ldg, low (rows, 16) bf16, out (experts, n, 16) bf16 (out_layout 0) or (experts, 16, n) (out_layout
+ * 1: a factor stored rank-major, as PEFT's lora_A is, takes its gradient in its own layout). */
 int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int64_t ldg, const void* low,
-                          const int32_t* offsets, int32_t experts, float scaling, void* out, void* stream);
+                          const int32_t* offsets, int32_t experts, float scaling, void* out, int32_t out_layout,
+                          void* stream);
 
 /* The same reduction over rows gathered from a token-major tensor and weighted: out[e, j, r] = bf16(scaling * sum
  * over expert e's rows i of g[g_rows[i], j] * bf16(row_scale[i] * low[i, r])) (row_scale NULL: weight 1). Used
@@ -261,7 +270,7 @@ int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int64_t ldg, c
  * _moe.py:123-126, folded in). rows: the routed rows; g has ldg-strided rows indexed by g_rows. */
 int meep2b_grouped_reduce_rows(const void* g, const int32_t* g_rows, const float* row_scale, int64_t rows,
                                int64_t n, int64_t ldg, const void* low, const int32_t* offsets, int32_t experts,
-                               float scaling, void* out, void* stream);
+                               float scaling, void* out, int32_t out_layout, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- quantised stacks */
 

@@ -473,32 +473,37 @@ def _product(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, 
 
 
 def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: float, g_rows=None,
-            row_scale=None) -> torch.Tensor:
-    """(experts, N, 16) bf16: scaling * sum over each expert's rows of g^T @ low (_grouped.py:362-370).
+            row_scale=None, out=None, layout=0) -> torch.Tensor:
+    """scaling * sum over each expert's rows of g^T @ low (_grouped.py:362-370), bf16: (experts, N, 16) with
+    layout 0, (experts, 16, N) with layout 1.
 
     g_rows (int32): row i is row g_rows[i] of g (the routed rows read where they are); row_scale (float32): row i
-    weighted by row_scale[i].
+    weighted by row_scale[i]. out: a contiguous bf16 tensor of that shape to write into (a gradient bucket's slot).
     """
     experts = offsets.numel()
     N = g.shape[1]
     rows = g_rows.numel() if g_rows is not None else g.shape[0]
     if g.stride(1) != 1 or g.stride(0) % 8:
         g = g.contiguous()
-    out = torch.empty((experts, N, RANK_MULTIPLE), device=g.device, dtype=torch.bfloat16)
+    shape = (experts, N, RANK_MULTIPLE) if layout == 0 else (experts, RANK_MULTIPLE, N)
+    if out is None:
+        out = torch.empty(shape, device=g.device, dtype=torch.bfloat16)
+    elif tuple(out.shape) != shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError(f"a reduction into {tuple(out.shape)} {out.dtype}: {shape} bf16 contiguous expected")
     if rows == 0:
         return out.zero_()
     lib = _lib.load()
     if g_rows is None and row_scale is None:
         _lib.check(lib.meep2b_grouped_reduce(_lib.ptr(g), rows, N, g.stride(0), _lib.ptr(low.contiguous()),
-                                             _lib.ptr(offsets), experts, float(scaling), _lib.ptr(out),
+                                             _lib.ptr(offsets), experts, float(scaling), _lib.ptr(out), layout,
                                              _lib.stream_of(g)), "meep2b_grouped_reduce")
     else:
         if g_rows is None:
             raise ValueError("a weighted reduction reads its rows through g_rows")
         _lib.check(lib.meep2b_grouped_reduce_rows(_lib.ptr(g), _lib.ptr(g_rows), _lib.ptr(row_scale), rows, N,
                                                   g.stride(0), _lib.ptr(low.contiguous()), _lib.ptr(offsets),
-                                                  experts, float(scaling), _lib.ptr(out), _lib.stream_of(g)),
-                   "meep2b_grouped_reduce_rows")
+                                                  experts, float(scaling), _lib.ptr(out), layout,
+                                                  _lib.stream_of(g)), "meep2b_grouped_reduce_rows")
     return out
 
 

@@ -60,10 +60,11 @@ _SIGNATURES = {
     "meep2b_gather": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _i32, _p, _i32, _p, _p, _p]),
     "meep2b_unpermute": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p]),
     "meep2b_unpermute_backward": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p, _p]),
+    "meep2b_weight_grad": (ctypes.c_int, [_p, _i64, _i32, _p, _i64, _p, _i32, _p, _p]),
     "meep2b_tile_map": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _p, _p]),
     "meep2b_grouped_product": (ctypes.c_int, [ctypes.POINTER(Product), _p]),
-    "meep2b_grouped_reduce": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _p]),
-    "meep2b_grouped_reduce_rows": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _p]),
+    "meep2b_grouped_reduce": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _i32, _p]),
+    "meep2b_grouped_reduce_rows": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _i32, _p]),
     "meep2b_fp8_stack_quantize": (ctypes.c_int, [_p, _i32, _i32, _i64, _p, _p, _p, _p]),
     "meep2b_fp8_stack_dequantize": (ctypes.c_int, [_p, _p, _i32, _i64, _p, _p]),
     "meep2b_fp8_block_dequantize": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i32, _i32, _p, _p]),
@@ -131,7 +132,7 @@ KERNELS_PER_CALL = {
     "meep2b_fp8_block_dequantize": 1, "meep2b_nf4_dequantize": 2, "meep2b_nf4_absmax": 1,
     "meep2b_merge_stack": 1,
     "meep2b_quant_multipliers": 1, "meep2b_fp8_rows_quantize": 1, "meep2b_grouped_product_f8": 1,
-    "meep2b_swiglu": 1, "meep2b_swiglu_backward": 1,
+    "meep2b_swiglu": 1, "meep2b_swiglu_backward": 1, "meep2b_weight_grad": 1,
 }
 launches = {}
 

@@ -199,6 +199,7 @@ class _RoutedExperts(torch.autograd.Function):
         kept = (x, gu, h, y) if mode == "copy" else (hidden, gu, h, token_rows, w32)
         ctx.save_for_backward(*kept, *(v for v in (low1, low2) if v is not None))
         ctx.routing, ctx.st, ctx.ad1, ctx.ad2, ctx.mode = routing, st, ad1, ad2, mode
+        ctx.leaves = (lhs1, rhs1, lhs2, rhs2)  # the factors' own tensors: a gradient bucket may hold their slots
         ctx.has_low = (low1 is not None, low2 is not None)
         ctx.weights_dtype = top_k_weights.dtype
         return out
@@ -229,7 +230,8 @@ class _RoutedExperts(torch.autograd.Function):
             # the down stack's input gradient over the upstream gradient's rows, each weighted by its routing weight,
             # SwiGLU's backward in the epilogue, and <dh, h> per row and 96 columns for the routing weights' gradient
             inter = gu.shape[1] // 2
-            parts = torch.zeros((routing.perm.numel(), -(-inter // 96)), dtype=torch.float32, device=grad_out.device)
+            # every expert row's partials are written by the product; the sentinel rows' are not read
+            parts = torch.empty((routing.perm.numel(), -(-inter // 96)), dtype=torch.float32, device=grad_out.device)
             if mode == "gather":
                 g, g_rows = grad_out, token_rows
             else:
@@ -238,28 +240,61 @@ class _RoutedExperts(torch.autograd.Function):
                                           True, backward=True, tiles=tiles, epilogue=_lib.EPI_DSWIGLU, aux=gu,
                                           x_rows=g_rows, row_scale=w32, w_grad=parts)
             grad_w = torch.empty(routing.perm.numel(), dtype=torch.float32, device=grad_out.device)
-            grad_w[routing.perm] = parts.sum(dim=1)  # a fixed order: the same bits on every run
+            _lib.check(_lib.load().meep2b_weight_grad(_lib.ptr(parts), parts.stride(0), parts.shape[1],
+                                                      _lib.ptr(routing.perm), routing.perm.numel(),
+                                                      _lib.ptr(routing.offsets), routing.num_experts, _lib.ptr(grad_w),
+                                                      _lib.stream_of(parts)), "meep2b_weight_grad")
         dsel, low1b = _grouped._launch(dgu, _stack(st.gate_up), st.gate_up_scale, routing.offsets, t, ad1, st.scaling1,
                                        None, True, backward=True, tiles=tiles)
         grads = [None, None, None, None]
         if ad1 is not None:
             if mode == "copy":
-                g_first = _grouped._reduce(sel, low1b, routing.offsets, st.scaling1)
+                first = dict(g=sel, low=low1b)
             else:
-                g_first = _grouped._reduce(hidden, low1b, routing.offsets, st.scaling1, g_rows=token_rows)
-            g_second = _grouped._reduce(dgu, low1, routing.offsets, st.scaling1)
-            grads[0], grads[1] = _grouped._to_lhs_rhs(g_first, g_second, ad1)
+                first = dict(g=hidden, low=low1b, g_rows=token_rows)
+            second = dict(g=dgu, low=low1)
+            grads[0], grads[1] = _adapter_grads(ad1, ctx.leaves[0], ctx.leaves[1], first, second, routing.offsets,
+                                                st.scaling1)
         if ad2 is not None:
-            g_first = _grouped._reduce(h, low2b, routing.offsets, st.scaling2)
+            first = dict(g=h, low=low2b)
             if mode == "copy":
-                g_second = _grouped._reduce(grad_y, low2, routing.offsets, st.scaling2)
+                second = dict(g=grad_y, low=low2)
             else:
-                g_second = _grouped._reduce(grad_out, low2, routing.offsets, st.scaling2, g_rows=token_rows,
-                                            row_scale=w32)
-            grads[2], grads[3] = _grouped._to_lhs_rhs(g_first, g_second, ad2)
+                second = dict(g=grad_out, low=low2, g_rows=token_rows, row_scale=w32)
+            grads[2], grads[3] = _adapter_grads(ad2, ctx.leaves[2], ctx.leaves[3], first, second, routing.offsets,
+                                                st.scaling2)
         grad_hidden = unpermute(dsel, routing, None)
         grad_w = grad_w.view(routing.num_tokens, routing.top_k)
         return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None)
+
+
+def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling):
+    """PEFT's (lhs, rhs) gradients of one stack's adapters from the two reductions of the backward pass (first: the
+    factor the forward applies first, second: the other; _grouped.py:400-405), each written in its factor's own
+    layout: (experts, n, 16) for lhs (E, out, r) or a transposed stack's lhs (E, in, r), (experts, 16, n) for rhs.
+    At rank 16 a factor whose slot in a LoRA-gradient bucket is free (ddp.grad_slot) gets its gradient written
+    there, and autograd adopts it without a copy."""
+    from . import ddp
+
+    rank = ad.rank
+    lhs_first = ad.is_transposed  # a transposed stack applies lhs (E, in, r) first, else rhs^T
+    spec = {"lhs": (first if lhs_first else second, 0, lhs), "rhs": (second if lhs_first else first, 1, rhs)}
+    out = {}
+    for name, (red, layout, leaf) in spec.items():
+        slot = ddp.grad_slot(leaf) if rank == RANK and leaf is not None else None
+        if slot is not None and (slot.dtype != torch.bfloat16 or not slot.is_contiguous()):
+            slot = None
+        n = red["g"].shape[1]
+        want = (offsets.numel(), n, RANK) if layout == 0 else (offsets.numel(), RANK, n)
+        if slot is not None and tuple(slot.shape) != want:
+            slot = None
+        g = _grouped._reduce(red["g"], red["low"], offsets, scaling, g_rows=red.get("g_rows"),
+                             row_scale=red.get("row_scale"), out=slot, layout=layout)
+        out[name] = g if rank == RANK else (g[:, :, :rank] if layout == 0 else g[:, :rank, :])
+    return out["lhs"], out["rhs"]
+
+
+RANK = _grouped.RANK_MULTIPLE
 
 
 class _PerProduct:

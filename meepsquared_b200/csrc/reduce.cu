@@ -5,7 +5,8 @@
 // traffic) and is bound by HBM bandwidth, not by tensor throughput (16 MACs per element of g). The small
 // products run on the warp-level mma.sync m16n8k16 path, fed from shared memory by ldmatrix.trans: the operand
 // tiles are row-major in memory and the MMA wants them transposed. Rows stream through a two-stage cp.async
-// ring of 64-row chunks.
+// ring of 64-row chunks; nothing waits on a plain load inside the loop (the gathered form's row indices are read a
+// chunk ahead, the row weights come in by cp.async with the panel and are applied in shared memory).
 //
 // Grid: (ceil(n / 128), experts); 8 warps, warp w owns columns [16 w, 16 w + 16) of the CTA's 128.
 // The gathered form reads row i of g as g[g_rows[i]] (the routed rows straight from the token-major tensor, no
@@ -46,14 +47,22 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool pred) {
+  const uint32_t d = smem_u32(dst);
+  const int bytes = pred ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+
 __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bfloat16* __restrict__ g, int64_t n,
                                                                  int64_t ldg, const __nv_bfloat16* __restrict__ low,
                                                                  const int32_t* __restrict__ offsets, float scaling,
                                                                  __nv_bfloat16* __restrict__ out,
                                                                  const int32_t* __restrict__ g_rows,
-                                                                 const float* __restrict__ row_scale) {
+                                                                 const float* __restrict__ row_scale,
+                                                                 int out_layout) {
   __shared__ __align__(16) __nv_bfloat16 gs[2][ROWS][G_PITCH];
   __shared__ __align__(16) __nv_bfloat16 ls[2][ROWS][L_PITCH];
+  __shared__ float ws[2][ROWS];
   const int e = blockIdx.y;
   const int64_t c0 = static_cast<int64_t>(blockIdx.x) * COLS;
   const int64_t start = e > 0 ? offsets[e - 1] : 0;
@@ -63,52 +72,66 @@ __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bflo
   float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // [n-tile of 8 ranks][fragment]
   const int chunks = static_cast<int>((end - start + ROWS - 1) / ROWS);
 
-  auto load = [&](int chunk, int buf) {
+  // This thread's four g pieces of a chunk are rows piece_row + 16 i (i < 4) at column piece_col. The source rows of
+  // gathered g are read one chunk ahead of their copies, so that no copy waits for its index.
+  const int piece_row = threadIdx.x >> 4, piece_col = (threadIdx.x & 15) * 8;
+  auto sources = [&](int chunk, int64_t (&src)[4]) {
     const int64_t r0 = start + static_cast<int64_t>(chunk) * ROWS;
-    // g: 64 rows x 128 columns = 1024 16-byte pieces, 4 per thread
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int piece = threadIdx.x + i * THREADS;
-      const int r = piece >> 4, c = (piece & 15) * 8;
-      const int64_t row = r0 + r, col = c0 + c;
-      const bool ok = row < end && col < n;
-      const int64_t src = ok && g_rows != nullptr ? static_cast<int64_t>(g_rows[row]) : row;
-      cp_async16(&gs[buf][r][c], ok ? g + src * ldg + col : g, ok);
+      const int64_t row = r0 + piece_row + 16 * i;
+      src[i] = row < end ? (g_rows != nullptr ? static_cast<int64_t>(__ldg(g_rows + row)) : row) : -1;
     }
-    // low: 64 rows x 16 = 128 pieces
+  };
+  auto load = [&](int chunk, int buf, const int64_t (&src)[4]) {
+    const int64_t r0 = start + static_cast<int64_t>(chunk) * ROWS;
+    // g: 64 rows x 128 columns = 1024 16-byte pieces, 4 per thread
+    const int64_t col = c0 + piece_col;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bool ok = src[i] >= 0 && col < n;
+      cp_async16(&gs[buf][piece_row + 16 * i][piece_col], ok ? g + src[i] * ldg + col : g, ok);
+    }
+    // low: 64 rows x 16 = 128 pieces; the rows' weights (row-scaled form), one float each
     if (threadIdx.x < 128) {
       const int r = threadIdx.x >> 1, c = (threadIdx.x & 1) * 8;
       const int64_t row = r0 + r;
       const bool ok = row < end;
-      if (row_scale == nullptr) {
-        cp_async16(&ls[buf][r][c], ok ? low + row * 16 + c : low, ok);
-      } else {  // bf16(w * low): a plain load, scaled and stored (the ring's barrier also covers these stores)
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (ok) {
-          const uint4 l = *reinterpret_cast<const uint4*>(low + row * 16 + c);
-          const float w = row_scale[row];
-          const uint32_t in[4] = {l.x, l.y, l.z, l.w};
-          uint32_t o[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) o[j] = pack_bf16x2(bf16_lo(in[j]) * w, bf16_hi(in[j]) * w);
-          v = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        *reinterpret_cast<uint4*>(&ls[buf][r][c]) = v;
-      }
+      cp_async16(&ls[buf][r][c], ok ? low + row * 16 + c : low, ok);
+    } else if (row_scale != nullptr && threadIdx.x < 128 + ROWS) {
+      const int r = threadIdx.x - 128;
+      const int64_t row = r0 + r;
+      cp_async4(&ws[buf][r], row < end ? row_scale + row : row_scale, row < end);
     }
     cp_async_commit();
   };
 
-  if (chunks > 0) load(0, 0);
+  int64_t src_next[4];
+  if (chunks > 0) {
+    int64_t src0[4];
+    sources(0, src0);
+    load(0, 0, src0);
+  }
+  if (chunks > 1) sources(1, src_next);
   for (int ch = 0; ch < chunks; ++ch) {
     const int buf = ch & 1;
     if (ch + 1 < chunks) {
-      load(ch + 1, buf ^ 1);
+      load(ch + 1, buf ^ 1, src_next);
+      if (ch + 2 < chunks) sources(ch + 2, src_next);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
+    if (row_scale != nullptr) {  // bf16(w * low) in place: 1024 values, 4 per thread
+      const int r = threadIdx.x >> 2, c = (threadIdx.x & 3) * 4;
+      const float w = ws[buf][r];
+      uint2* p2 = reinterpret_cast<uint2*>(&ls[buf][r][c]);
+      const uint2 v = *p2;
+      *p2 = make_uint2(pack_bf16x2(bf16_lo(v.x) * w, bf16_hi(v.x) * w),
+                       pack_bf16x2(bf16_lo(v.y) * w, bf16_hi(v.y) * w));
+      __syncthreads();
+    }
 #pragma unroll
     for (int kk = 0; kk < ROWS / 16; ++kk) {
       // A (16 columns x 16 rows) = g^T: the four 8x8 blocks (cols 0-7|8-15) x (rows 0-7|8-15), transposed
@@ -143,7 +166,12 @@ __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bflo
       const int64_t col = col_a + h * 8;
       if (col < n) {
         const uint32_t v = pack_bf16x2(acc[nt][2 * h] * scaling, acc[nt][2 * h + 1] * scaling);
-        *reinterpret_cast<uint32_t*>(o + col * 16 + rk) = v;
+        if (out_layout == 0) {
+          *reinterpret_cast<uint32_t*>(o + col * 16 + rk) = v;
+        } else {  // (16, n) per expert
+          o[rk * n + col] = __ushort_as_bfloat16(static_cast<unsigned short>(v & 0xFFFFu));
+          o[(rk + 1) * n + col] = __ushort_as_bfloat16(static_cast<unsigned short>(v >> 16));
+        }
       }
     }
   }
@@ -154,9 +182,9 @@ __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bflo
 
 static int grouped_reduce_launch(const void* g, const int32_t* g_rows, const float* row_scale, int64_t rows,
                                  int64_t n, int64_t ldg, const void* low, const int32_t* offsets, int32_t experts,
-                                 float scaling, void* out, void* stream) {
+                                 float scaling, void* out, int32_t out_layout, void* stream) {
   using namespace meep2b;
-  if (rows < 0 || n < 1 || experts < 1 || ldg < n) return MEEP2B_ERR_SHAPE;
+  if (rows < 0 || n < 1 || experts < 1 || ldg < n || out_layout < 0 || out_layout > 1) return MEEP2B_ERR_SHAPE;
   if (n % 8 || ldg % 8) return MEEP2B_ERR_ALIGN;
   if (!aligned16(g) || !aligned16(low) || !aligned16(out)) return MEEP2B_ERR_ALIGN;
   cudaStream_t s = as_stream(stream);
@@ -164,20 +192,22 @@ static int grouped_reduce_launch(const void* g, const int32_t* g_rows, const flo
   dim3 grid(static_cast<unsigned>((n + reduce::COLS - 1) / reduce::COLS), static_cast<unsigned>(experts));
   reduce::grouped_reduce_kernel<<<grid, reduce::THREADS, 0, s>>>(
       static_cast<const __nv_bfloat16*>(g), n, ldg, static_cast<const __nv_bfloat16*>(low), offsets, scaling,
-      static_cast<__nv_bfloat16*>(out), g_rows, row_scale);
+      static_cast<__nv_bfloat16*>(out), g_rows, row_scale, out_layout);
   return launch_status();
 }
 
 extern "C" int meep2b_grouped_reduce(const void* g, int64_t rows, int64_t n, int64_t ldg, const void* low,
                                      const int32_t* offsets, int32_t experts, float scaling, void* out,
-                                     void* stream) {
-  return grouped_reduce_launch(g, nullptr, nullptr, rows, n, ldg, low, offsets, experts, scaling, out, stream);
+                                     int32_t out_layout, void* stream) {
+  return grouped_reduce_launch(g, nullptr, nullptr, rows, n, ldg, low, offsets, experts, scaling, out, out_layout,
+                               stream);
 }
 
 extern "C" int meep2b_grouped_reduce_rows(const void* g, const int32_t* g_rows, const float* row_scale,
                                           int64_t rows, int64_t n, int64_t ldg, const void* low,
                                           const int32_t* offsets, int32_t experts, float scaling, void* out,
-                                          void* stream) {
+                                          int32_t out_layout, void* stream) {
   if (g_rows == nullptr) return MEEP2B_ERR_SHAPE;
-  return grouped_reduce_launch(g, g_rows, row_scale, rows, n, ldg, low, offsets, experts, scaling, out, stream);
+  return grouped_reduce_launch(g, g_rows, row_scale, rows, n, ldg, low, offsets, experts, scaling, out, out_layout,
+                               stream);
 }

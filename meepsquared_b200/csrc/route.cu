@@ -152,39 +152,58 @@ __device__ __forceinline__ float weight_value(const __nv_bfloat16* w, int64_t i)
 
 // out[t] = bf16(sum_j y[r_j] * w_g[r_j]), r_j = inverse[t * top_k + j]. One CTA per token, 8 bf16 per thread
 // and step. F32 weights: each product rounded to float32 (bf16 * f32 promotes), summed in float32. BF16 weights:
-// each product rounded to bf16 (bf16 * bf16), summed in float32. No weights: a plain float32 sum.
+// each product rounded to bf16 (bf16 * bf16), summed in float32. No weights: a plain float32 sum. The token's row
+// indices and weights are read once into shared memory, and every thread issues the loads of all its rows before
+// it sums them (in order j = 0, 1, ...), so a token costs one round trip to memory rather than top_k.
+constexpr int kUnpermuteGroup = 8;  // rows whose loads are in flight together
 template <typename W>
 __global__ void __launch_bounds__(256) unpermute_rows(const uint4* __restrict__ y, const int64_t* __restrict__ inverse,
                                                      const W* __restrict__ weights_g,
                                                      const int32_t* __restrict__ offsets, int experts,
                                                      int top_k, int64_t vec_per_row, uint4* __restrict__ out) {
+  extern __shared__ int64_t unpermute_smem[];  // the token's rows (-1: a sentinel), then their weights
+  int64_t* rows_s = unpermute_smem;
+  float* w_s = reinterpret_cast<float*>(unpermute_smem + top_k);
   const int64_t t = blockIdx.x;
   const int64_t valid = offsets[experts - 1];
+  for (int j = threadIdx.x; j < top_k; j += blockDim.x) {
+    const int64_t r = inverse[t * top_k + j];
+    rows_s[j] = r < valid ? r : -1;  // a sentinel row: masked to zero (_moe.py:116)
+    w_s[j] = (weights_g != nullptr && r < valid) ? weight_value(weights_g, r) : 1.f;
+  }
+  __syncthreads();
+  const bool round_bf16 = sizeof(W) == 2;
   for (int64_t v = threadIdx.x; v < vec_per_row; v += blockDim.x) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < top_k; ++j) {
-      const int64_t r = inverse[t * top_k + j];
-      if (r >= valid) continue;  // a sentinel row: masked to zero (_moe.py:116)
-      const uint4 q = __ldg(y + r * vec_per_row + v);
-      const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-      if (weights_g == nullptr) {
+    for (int j0 = 0; j0 < top_k; j0 += kUnpermuteGroup) {
+      uint4 q[kUnpermuteGroup];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[2 * e] = __fadd_rn(acc[2 * e], bf16_lo(words[e]));
-          acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], bf16_hi(words[e]));
-        }
-      } else {
-        const float w = weight_value(weights_g, r);
-        const bool round_bf16 = sizeof(W) == 2;
+      for (int j = 0; j < kUnpermuteGroup; ++j) {
+        const int64_t r = j0 + j < top_k ? rows_s[j0 + j] : -1;
+        q[j] = r >= 0 ? __ldg(y + r * vec_per_row + v) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float p0 = __fmul_rn(bf16_lo(words[e]), w), p1 = __fmul_rn(bf16_hi(words[e]), w);
-          if (round_bf16) {
-            p0 = bf16_round(p0);
-            p1 = bf16_round(p1);
+      for (int j = 0; j < kUnpermuteGroup; ++j) {
+        if (j0 + j >= top_k || rows_s[j0 + j] < 0) continue;
+        const uint32_t words[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
+        if (weights_g == nullptr) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[2 * e] = __fadd_rn(acc[2 * e], bf16_lo(words[e]));
+            acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], bf16_hi(words[e]));
           }
-          acc[2 * e] = __fadd_rn(acc[2 * e], p0);
-          acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], p1);
+        } else {
+          const float w = w_s[j0 + j];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float p0 = __fmul_rn(bf16_lo(words[e]), w), p1 = __fmul_rn(bf16_hi(words[e]), w);
+            if (round_bf16) {
+              p0 = bf16_round(p0);
+              p1 = bf16_round(p1);
+            }
+            acc[2 * e] = __fadd_rn(acc[2 * e], p0);
+            acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], p1);
+          }
         }
       }
     }
@@ -243,6 +262,23 @@ __global__ void __launch_bounds__(256) unpermute_backward_rows(const uint4* __re
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
   if (lane == 0) grad_weights[src] = live ? dot : 0.f;
+}
+
+// The routing weights' gradient from the per-row partial dot products of the down stack's input-gradient product:
+// grad_weights[perm[i]] = sum over b < blocks of parts[i * ld + b] (in order b = 0, 1, ...) for the experts' rows,
+// zero for the sentinel rows (whose partials nobody writes). One thread per routed row.
+__global__ void __launch_bounds__(256) weight_grad_rows(const float* __restrict__ parts, int64_t ld, int blocks,
+                                                       const int64_t* __restrict__ perm, int64_t rows,
+                                                       const int32_t* __restrict__ offsets, int experts,
+                                                       float* __restrict__ grad_weights) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows) return;
+  float acc = 0.f;
+  if (i < offsets[experts - 1]) {
+    const float* p = parts + i * ld;
+    for (int b = 0; b < blocks; ++b) acc = __fadd_rn(acc, p[b]);
+  }
+  grad_weights[perm[i]] = acc;
 }
 
 // The tile map: tiles per expert, their running sum, and for every tile index t < max_tiles the expert (by binary
@@ -377,12 +413,14 @@ int meep2b_unpermute(const void* y, const int64_t* inverse, const void* weights_
   if (tokens == 0) return MEEP2B_OK;
   const int64_t vec = hidden_dim / 8;
   const int threads = vec >= 256 ? 256 : static_cast<int>(((vec + 31) / 32) * 32);
+  const size_t smem = static_cast<size_t>(top_k) * (sizeof(int64_t) + sizeof(float));
+  if (smem > 48 * 1024) return MEEP2B_ERR_SHAPE;
   if (weights_g != nullptr && weights_dtype == MEEP2B_BF16)
-    unpermute_rows<__nv_bfloat16><<<static_cast<unsigned>(tokens), threads, 0, s>>>(
+    unpermute_rows<__nv_bfloat16><<<static_cast<unsigned>(tokens), threads, smem, s>>>(
         static_cast<const uint4*>(y), inverse, static_cast<const __nv_bfloat16*>(weights_g), offsets, experts, top_k,
         vec, static_cast<uint4*>(out));
   else
-    unpermute_rows<float><<<static_cast<unsigned>(tokens), threads, 0, s>>>(
+    unpermute_rows<float><<<static_cast<unsigned>(tokens), threads, smem, s>>>(
         static_cast<const uint4*>(y), inverse, static_cast<const float*>(weights_g), offsets, experts, top_k, vec,
         static_cast<uint4*>(out));
   return launch_status();
@@ -407,6 +445,18 @@ int meep2b_unpermute_backward(const void* grad_out, const void* y, const int64_t
     unpermute_backward_rows<float><<<static_cast<unsigned>((assignments + 7) / 8), 256, 0, s>>>(
         static_cast<const uint4*>(grad_out), static_cast<const uint4*>(y), perm, static_cast<const float*>(weights_g),
         offsets, experts, top_k, assignments, vec, static_cast<uint4*>(grad_y), grad_weights);
+  return launch_status();
+}
+
+int meep2b_weight_grad(const float* parts, int64_t ld, int32_t blocks, const int64_t* perm, int64_t assignments,
+                       const int32_t* offsets, int32_t experts, float* grad_weights, void* stream) {
+  if (experts < 1 || assignments < 0 || blocks < 0 || ld < blocks) return MEEP2B_ERR_SHAPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  if (assignments == 0) return MEEP2B_OK;
+  weight_grad_rows<<<static_cast<unsigned>((assignments + 255) / 256), 256, 0, s>>>(parts, ld, blocks, perm,
+                                                                                   assignments, offsets, experts,
+                                                                                   grad_weights);
   return launch_status();
 }
 

@@ -50,13 +50,20 @@ def forward(hidden, top_k_index, top_k_weights, gate_up, down, factors, is_trans
     return out, saved
 
 
-def backward(grad_out, saved, gate_up, down, factors, is_transposed=False, scales=(None, None)):
-    """Gradients: {"hidden", "top_k_weights", "gate_up_proj": (dlhs, drhs), "down_proj": (dlhs, drhs)}."""
+def backward(grad_out, saved, gate_up, down, factors, is_transposed=False, scales=(None, None),
+             round_grad_rows=None):
+    """Gradients: {"hidden", "top_k_weights", "gate_up_proj": (dlhs, drhs), "down_proj": (dlhs, drhs), "rows"}, where
+    "rows" is the gradient of the gathered rows in expert order (the terms the hidden states' gradient sums).
+
+    round_grad_rows: whether the rows' gradient g * w is rounded to bf16 before the down projection's backward, as
+    autograd does over the reference's bf16 graph (the default in bf16 mode); False states a computation that
+    applies the routing weight to the float32 product instead (one rounding fewer, the same function)."""
     r, k, tokens, rb = saved["route"], saved["k"], saved["tokens"], saved.get("bf16", False)
+    round_gy = rb if round_grad_rows is None else round_grad_rows
     lhs1, rhs1, s1 = factors.get("gate_up_proj", (None, None, 1.0))
     lhs2, rhs2, s2 = factors.get("down_proj", (None, None, 1.0))
     grad_y, grad_wg = routing.unpermute_backward(grad_out, saved["y"], saved["w_g"], r["perm"], k)
-    grad_y = _round(grad_y, rb)
+    grad_y = _round(grad_y, round_gy)
     grad_y[r["sentinel"]] = 0
     grad_h, dl2, dr2 = grouped.lora_backward(saved["h"], grad_y, down, scales[1], r["offsets"], is_transposed,
                                              lhs2, rhs2, s2)
@@ -70,4 +77,4 @@ def backward(grad_out, saved, gate_up, down, factors, is_transposed=False, scale
     grad_w = np.zeros(tokens * k, dtype=np.float32)
     grad_w[r["perm"]] = grad_wg
     return {"hidden": _round(grad_hidden, rb), "top_k_weights": grad_w.reshape(tokens, k),
-            "gate_up_proj": (dl1, dr1), "down_proj": (dl2, dr2)}
+            "gate_up_proj": (dl1, dr1), "down_proj": (dl2, dr2), "rows": grad_sel}

@@ -44,6 +44,46 @@ def _average_worker(rank, world, port, queue):
     dist.destroy_process_group()
 
 
+class _WritesIntoSlots(torch.autograd.Function):
+    """A layer that computes its factors' gradients straight into their bucket slots when they are free (as the
+    routed layer's adapter reductions do), a fresh tensor otherwise."""
+
+    @staticmethod
+    def forward(ctx, x, a, b):
+        ctx.save_for_backward(x)
+        ctx.leaves = (a, b)
+        return x * a.sum() + x * b.sum()
+
+    @staticmethod
+    def backward(ctx, g):
+        from meepsquared_b200 import ddp
+
+        (x,) = ctx.saved_tensors
+        out = []
+        for leaf in ctx.leaves:
+            slot = ddp.grad_slot(leaf)
+            dest = slot if slot is not None else torch.empty_like(leaf)
+            dest.fill_(float((g * x).sum()))
+            out.append(dest)
+        return None, out[0], out[1]
+
+
+def _release_worker(rank, world, port, queue):
+    _init(rank, world, port)
+    a, b = torch.nn.Parameter(torch.zeros(3, 4)), torch.nn.Parameter(torch.zeros(2, 5))
+    bucket = LoraGradBucket([a, b])
+    x = torch.full((6,), float(rank + 1))
+    for step in range(2):
+        bucket.release()
+        _WritesIntoSlots.apply(x, a, b).sum().backward()
+        adopted = a.grad.data_ptr() == bucket.flat.data_ptr() and b.grad.data_ptr() == bucket.flat[12:].data_ptr()
+        bucket.reduce()
+        queue.put((rank, step, adopted, a.grad.tolist(), b.grad.tolist(),
+                   a.grad.data_ptr() == bucket.flat.data_ptr()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _failing_worker(rank, world, port, queue):
     _init(rank, world, port, timeout_s=5)
     params = [torch.nn.Parameter(torch.zeros(8))]
@@ -72,7 +112,7 @@ def _run(fn, world=2):
     for p in procs:
         p.start()
     items = []
-    expected = {"_average_worker": 2 * world, "_failing_worker": world}[fn.__name__]
+    expected = {"_average_worker": 2 * world, "_release_worker": 2 * world, "_failing_worker": world}[fn.__name__]
     import queue as _queue
     try:
         while len(items) < expected:
@@ -104,3 +144,36 @@ def test_a_rank_that_leaves_before_the_exchange_ends_the_other_ranks_collective_
     assert outcome[1] == "left"
     assert outcome[0].startswith("error"), outcome[0]
     assert procs[0].exitcode == 0
+
+
+def test_gradients_written_into_the_bucket_are_adopted_without_copies_and_averaged():
+    """release() then backward: the layer writes each gradient into the parameter's slot of the flat buffer and
+    autograd adopts it as .grad (no zeroing, no add); reduce() averages the buffer across the ranks."""
+    procs, items = _run(_release_worker)
+    assert all(p.exitcode == 0 for p in procs)
+    assert len(items) == 4
+    for rank, step, adopted, ga, gb, in_bucket in items:
+        assert adopted and in_bucket
+        # each rank's gradient is 6 (rank + 1): the average over ranks 0 and 1 is 9
+        torch.testing.assert_close(torch.tensor(ga), torch.full((3, 4), 9.0))
+        torch.testing.assert_close(torch.tensor(gb), torch.full((2, 5), 9.0))
+
+
+def test_a_gradient_that_arrives_elsewhere_is_copied_into_the_bucket():
+    """A parameter whose gradient autograd accumulated on its own (the slot was taken: .grad already set) or that
+    got none: adopt() leaves every .grad a view of the flat buffer with the right values."""
+    a, b, c = (torch.nn.Parameter(torch.zeros(4)) for _ in range(3))
+    bucket = LoraGradBucket([a, b, c])
+    bucket.release()
+    a.grad = torch.full((4,), 2.0)        # set outside the bucket
+    (b * 3.0).sum().backward()             # autograd's own accumulation into a fresh tensor
+    bucket.adopt()
+    assert a.grad.data_ptr() == bucket.flat.data_ptr()
+    assert b.grad.data_ptr() == bucket.flat[4:].data_ptr() and c.grad.data_ptr() == bucket.flat[8:].data_ptr()
+    torch.testing.assert_close(bucket.flat, torch.tensor([2.0] * 4 + [3.0] * 4 + [0.0] * 4))
+    # with the slots free, a second layer call would write into them; with .grad set they are not offered
+    from meepsquared_b200 import ddp
+
+    assert ddp.grad_slot(a) is None
+    bucket.release()
+    assert ddp.grad_slot(a) is not None and ddp.grad_slot(a).data_ptr() == bucket.flat.data_ptr()
