@@ -239,7 +239,10 @@ def run_meep2b(a):
     ex, lora, hidden, idx, w, grad = make_layer(c, device, seed=1234 + rank)
     s = c["alpha"] / c["rank"]
     factors = {"gate_up_proj": (lora["lhs1"], lora["rhs1"], s), "down_proj": (lora["lhs2"], lora["rhs2"], s)}
-    bucket = ddp.LoraGradBucket(list(lora.values()))
+    # the down projection's adapter gradients are ready first: their average starts while the gate/up input gradient
+    # runs, the gate/up adapters' at the end of the step
+    bucket = ddp.LoraGradBucket(list(lora.values()),
+                                segments=[[lora["lhs2"], lora["rhs2"]], [lora["lhs1"], lora["rhs1"]]])
     hidden_leaf = hidden.clone().requires_grad_()
 
     def step(h, ids, wts, g):
@@ -358,11 +361,15 @@ def run_meep2b(a):
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms, e_ms, base_ms = times.tolist()
+    clock_summary = clocks.summary()
+    rank_clocks = [clock_summary]
+    if world > 1:  # every rank's clock record (the power cap is box-wide: it shows on all of them)
+        rank_clocks = [None] * world
+        dist.all_gather_object(rank_clocks, clock_summary)
     T = c["tokens"]
     value = world * T * a.steps / (ms / 1e3)
     e_value = world * T * e_steps / (e_ms / 1e3)
     sustained, burst, hbm, peak_source = peaks()
-    clock_summary = clocks.summary()
     bf16_peak, regime = pick_peak(clock_summary, sustained, burst)
     # MEEPSQUARED_FP8_PRODUCTS=1 on an FP8 stack: the frozen stack's products run e4m3 x e4m3 (the activations
     # quantised per row and 128-column tile); their roofline is the FP8 dense peak, taken as twice the measured bf16
@@ -403,6 +410,11 @@ def run_meep2b(a):
         "gpu_launches": timed_launches,  # libmeep2b kernels launched in the timed steps (counted per call)
         "clocks": clock_summary,
     }
+    if world > 1:
+        result["clocks_per_rank"] = rank_clocks
+        result["nccl_ranks"] = dist.get_world_size()
+        result["exchange"] = ("LoRA-gradient average, two NCCL all-reduces per step: the down adapters' slice "
+                              "started during the backward pass, the gate/up adapters' at its end")
     if gpu_base is not None:
         result["gpu_baseline"] = gpu_base
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

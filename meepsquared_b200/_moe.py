@@ -244,9 +244,19 @@ class _RoutedExperts(torch.autograd.Function):
                                                       _lib.ptr(routing.perm), routing.perm.numel(),
                                                       _lib.ptr(routing.offsets), routing.num_experts, _lib.ptr(grad_w),
                                                       _lib.stream_of(parts)), "meep2b_weight_grad")
+        grads = [None, None, None, None]
+        if ad2 is not None:
+            # the down projection's adapter gradients first: a data-parallel gradient bucket can start averaging
+            # them while the gate/up input gradient runs
+            first = dict(g=h, low=low2b)
+            if mode == "copy":
+                second = dict(g=grad_y, low=low2)
+            else:
+                second = dict(g=grad_out, low=low2, g_rows=token_rows, row_scale=w32)
+            grads[2], grads[3] = _adapter_grads(ad2, ctx.leaves[2], ctx.leaves[3], first, second, routing.offsets,
+                                                st.scaling2)
         dsel, low1b = _grouped._launch(dgu, _stack(st.gate_up), st.gate_up_scale, routing.offsets, t, ad1, st.scaling1,
                                        None, True, backward=True, tiles=tiles)
-        grads = [None, None, None, None]
         if ad1 is not None:
             if mode == "copy":
                 first = dict(g=sel, low=low1b)
@@ -255,14 +265,6 @@ class _RoutedExperts(torch.autograd.Function):
             second = dict(g=dgu, low=low1)
             grads[0], grads[1] = _adapter_grads(ad1, ctx.leaves[0], ctx.leaves[1], first, second, routing.offsets,
                                                 st.scaling1)
-        if ad2 is not None:
-            first = dict(g=h, low=low2b)
-            if mode == "copy":
-                second = dict(g=grad_y, low=low2)
-            else:
-                second = dict(g=grad_out, low=low2, g_rows=token_rows, row_scale=w32)
-            grads[2], grads[3] = _adapter_grads(ad2, ctx.leaves[2], ctx.leaves[3], first, second, routing.offsets,
-                                                st.scaling2)
         grad_hidden = unpermute(dsel, routing, None)
         grad_w = grad_w.view(routing.num_tokens, routing.top_k)
         return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None)
@@ -280,6 +282,7 @@ def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling):
     lhs_first = ad.is_transposed  # a transposed stack applies lhs (E, in, r) first, else rhs^T
     spec = {"lhs": (first if lhs_first else second, 0, lhs), "rhs": (second if lhs_first else first, 1, rhs)}
     out = {}
+    written = []
     for name, (red, layout, leaf) in spec.items():
         slot = ddp.grad_slot(leaf) if rank == RANK and leaf is not None else None
         if slot is not None and (slot.dtype != torch.bfloat16 or not slot.is_contiguous()):
@@ -291,6 +294,10 @@ def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling):
         g = _grouped._reduce(red["g"], red["low"], offsets, scaling, g_rows=red.get("g_rows"),
                              row_scale=red.get("row_scale"), out=slot, layout=layout)
         out[name] = g if rank == RANK else (g[:, :, :rank] if layout == 0 else g[:, :rank, :])
+        if slot is not None:
+            written.append(leaf)
+    for leaf in written:  # the bucket may start averaging these slots (they are complete in stream order)
+        ddp.mark_written(leaf)
     return out["lhs"], out["rhs"]
 
 

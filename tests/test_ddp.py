@@ -84,6 +84,51 @@ def _release_worker(rank, world, port, queue):
     dist.destroy_process_group()
 
 
+class _WritesSegments(torch.autograd.Function):
+    """A layer that writes its second factor's gradient first and reports each slot written (as the routed layer
+    does for the down projection's adapters before the gate/up projection's)."""
+
+    @staticmethod
+    def forward(ctx, x, a, b):
+        ctx.save_for_backward(x)
+        ctx.leaves = (a, b)
+        return x * a.sum() + x * b.sum()
+
+    @staticmethod
+    def backward(ctx, g):
+        from meepsquared_b200 import ddp
+
+        (x,) = ctx.saved_tensors
+        a, b = ctx.leaves
+        sb = ddp.grad_slot(b)
+        sb.fill_(float((g * x).sum()) * 2)
+        ddp.mark_written(b)  # completes the first segment: its average starts now
+        started = list(ctx.bucket._started)
+        sa = ddp.grad_slot(a)
+        sa.fill_(float((g * x).sum()))
+        ddp.mark_written(a)
+        ctx.bucket.seen.append((started, list(ctx.bucket._started)))
+        return None, sa, sb
+
+
+def _segments_worker(rank, world, port, queue):
+    _init(rank, world, port)
+    a, b = torch.nn.Parameter(torch.zeros(3, 4)), torch.nn.Parameter(torch.zeros(2, 5))
+    bucket = LoraGradBucket([a, b], segments=[[b], [a]])
+    bucket.seen = []
+    x = torch.full((6,), float(rank + 1))
+    for step in range(2):
+        bucket.release()
+        y = _WritesSegments.apply(x, a, b)
+        y.grad_fn.bucket = bucket
+        y.sum().backward()
+        bucket.reduce()
+        queue.put((rank, step, bucket.seen[-1], a.grad.tolist(), b.grad.tolist(),
+                   b.grad.data_ptr() == bucket.flat.data_ptr(), a.grad.data_ptr() == bucket.flat[10:].data_ptr()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _failing_worker(rank, world, port, queue):
     _init(rank, world, port, timeout_s=5)
     params = [torch.nn.Parameter(torch.zeros(8))]
@@ -112,7 +157,8 @@ def _run(fn, world=2):
     for p in procs:
         p.start()
     items = []
-    expected = {"_average_worker": 2 * world, "_release_worker": 2 * world, "_failing_worker": world}[fn.__name__]
+    expected = {"_average_worker": 2 * world, "_release_worker": 2 * world, "_segments_worker": 2 * world,
+                "_failing_worker": world}[fn.__name__]
     import queue as _queue
     try:
         while len(items) < expected:
@@ -177,3 +223,41 @@ def test_a_gradient_that_arrives_elsewhere_is_copied_into_the_bucket():
     assert ddp.grad_slot(a) is None
     bucket.release()
     assert ddp.grad_slot(a) is not None and ddp.grad_slot(a).data_ptr() == bucket.flat.data_ptr()
+
+
+def test_a_segment_starts_averaging_as_soon_as_its_gradients_are_written():
+    """segments=[[b], [a]]: the layer writes b's slot first; b's average starts then (before a is written), a's
+    when a is written; reduce() joins both. The buffer holds the segments in that order and both gradients are the
+    averages over the ranks."""
+    procs, items = _run(_segments_worker)
+    assert all(p.exitcode == 0 for p in procs)
+    assert len(items) == 4
+    for rank, step, (after_b, after_a), ga, gb, b_first, a_after in items:
+        assert after_b == [True, False] and after_a == [True, True]
+        assert b_first and a_after
+        torch.testing.assert_close(torch.tensor(ga), torch.full((3, 4), 9.0))
+        torch.testing.assert_close(torch.tensor(gb), torch.full((2, 5), 18.0))
+
+
+def test_segments_must_partition_the_parameters():
+    a, b = torch.nn.Parameter(torch.zeros(2)), torch.nn.Parameter(torch.zeros(3))
+    with pytest.raises(ValueError):
+        LoraGradBucket([a, b], segments=[[a]])
+    with pytest.raises(ValueError):
+        LoraGradBucket([a, b], segments=[[a, b], [b]])
+
+
+def test_a_written_gradient_replaced_by_a_hook_is_refused():
+    """With segments a slot may be averaging already when autograd stores the gradient: a hook that replaces the
+    written gradient would race with it, so adopt() refuses instead of copying."""
+    from meepsquared_b200 import ddp
+
+    a = torch.nn.Parameter(torch.zeros(4))
+    bucket = LoraGradBucket([a], segments=[[a]])
+    bucket.release()
+    slot = ddp.grad_slot(a)
+    slot.fill_(1.0)
+    ddp.mark_written(a)
+    a.grad = torch.full((4,), 2.0)  # what a replacing hook would leave
+    with pytest.raises(RuntimeError):
+        bucket.adopt()
