@@ -86,6 +86,18 @@ int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts
 int meep2b_route_noalloc(const int64_t* expert_ids, int64_t assignments, int32_t experts, int64_t* perm,
                          int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* stream);
 
+/* The router that feeds the routing (Transformers' Qwen3MoeTopKRouter.forward, after its linear layer): for each
+ * token t, probs[t, :] = softmax(logits[t, :]) in float32 (logits (tokens, experts) F32 or BF16; probs may be
+ * NULL), the top_k largest in descending order (a tie goes to the smaller expert index) as top_k_index[t, :]
+ * (int64) and their probabilities, divided by their sum when norm_topk_prob, as top_k_weights[t, :] (float32);
+ * then the routing permutation of meep2b_route over those ids, the router's pass doing the sort's histogram.
+ * top_k <= 32 and <= experts; workspace as for meep2b_route. The reference takes the router's outputs as inputs
+ * of the routed layer (_moe.py:70-87); this fuses the two steps. */
+int meep2b_route_logits(const void* logits, int32_t logits_dtype, int64_t tokens, int32_t experts, int32_t top_k,
+                        int32_t norm_topk_prob, float* probs, int64_t* top_k_index, float* top_k_weights,
+                        int64_t* perm, int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* What the routed products need of the permutation without a gathered copy of the rows: per routed row i, the
  * token it reads, token_rows[i] = perm[i] / top_k (int32), and its routing weight weights_g[i] = weights[perm[i]]
  * as float32 (weights F32 or BF16; weights or weights_g may be NULL). */
@@ -105,6 +117,15 @@ int meep2b_gather(const void* hidden, int64_t tokens, int64_t hidden_dim, int32_
 int meep2b_unpermute(const void* y, const int64_t* inverse, const void* weights_g, int32_t weights_dtype,
                      const int32_t* offsets, int32_t experts, int64_t tokens, int32_t top_k, int64_t hidden_dim,
                      void* out, void* stream);
+
+/* The same weighted un-permute over rows stored token-major (the down product's rows placed through the
+ * permutation, meep2b_product.out_rows = perm): out[t] = bf16(sum_j y_tok[t*top_k + j] * w[t*top_k + j]), w the
+ * routing weights in the router's (tokens, top_k) order (NULL: weight 1, the gather's backward), the sum in float32
+ * over j in order, assignments whose inverse[t*top_k + j] >= offsets[experts-1] (sentinels, never stored) count as
+ * zero. Reads each token's rows as one contiguous run: the forward combine of _moe.py:123-126. */
+int meep2b_combine(const void* y_tok, const int64_t* inverse, const void* weights, int32_t weights_dtype,
+                   const int32_t* offsets, int32_t experts, int64_t tokens, int32_t top_k, int64_t hidden_dim,
+                   void* out, void* stream);
 
 /* Backward of the un-permute (autograd of _moe.py:123-126): grad_y[i] = bf16(grad_out[perm[i]/top_k] * w_g[i]),
  * grad_weights[perm[i]] = sum_h grad_out[perm[i]/top_k][h] * y[i][h] (float32); sentinel rows give zeros. */
@@ -187,6 +208,11 @@ typedef struct meep2b_product {
   const float* row_scale;
   float* w_grad;
   int64_t w_ld;
+  /* out_rows (PLAIN epilogue, bf16 stacks): NULL, or product row i is stored at row out_rows[i] of out, e.g. the
+   * routing permutation `perm` (the flat assignment token * top_k + j of each row), so that the rows land in
+   * token-major order (tokens, top_k, n) and the un-permute becomes a streaming sum over each token's top_k
+   * consecutive rows (meep2b_combine). The stored panel `low` stays at row i. */
+  const int64_t* out_rows;
 } meep2b_product;
 
 int meep2b_grouped_product(const meep2b_product* p, void* stream);

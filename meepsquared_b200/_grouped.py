@@ -164,12 +164,25 @@ def _rank_rows(factor: torch.Tensor) -> torch.Tensor:
     return torch.nn.functional.pad(factor.to(torch.bfloat16), (0, 0, 0, RANK_MULTIPLE - r)).contiguous()  # one pass
 
 
+# Zero-padded panel buffers (E, D, width) per device and shape: the padding columns are zeroed once and only the
+# rank's columns are written per use. A buffer is filled and read by the same product launch, in stream order, so
+# products of different layers may share it.
+_PADDED = {}
+
+
 def _rank_cols(factor: torch.Tensor, width: int) -> torch.Tensor:
-    """(E, D, r) -> (E, D, width) bf16 contiguous, zero columns past the rank (width 16 or 64)."""
+    """(E, D, r) -> (E, D, width) bf16 contiguous, zero columns past the rank (width 16 or 64). A padded copy lives
+    in a buffer shared by every product of its shape: it is valid until the next call for that shape."""
     e, d, r = factor.shape
     if r == width and factor.dtype == torch.bfloat16 and factor.is_contiguous():
         return factor
-    return torch.nn.functional.pad(factor.to(torch.bfloat16), (0, width - r)).contiguous()  # values and zeros
+    key = (factor.device, e, d, width, r)
+    buf = _PADDED.get(key)
+    if buf is None:
+        buf = torch.zeros((e, d, width), device=factor.device, dtype=torch.bfloat16)
+        _PADDED[key] = buf
+    buf[:, :, :r].copy_(factor)
+    return buf
 
 
 class _Adapters:
@@ -187,7 +200,6 @@ class _Adapters:
         if self.rank > RANK_MULTIPLE:  # larger ranks go to the products in 16-rank chunks (_rank_chunks)
             raise NotImplementedError(f"LoRA rank {self.rank}: one fused panel takes ranks up to {RANK_MULTIPLE}")
         self.lhs, self.rhs, self.is_transposed = lhs, rhs, is_transposed
-        self._cache = {}
 
     def factors(self, backward: bool):
         """(F1, F2) of the forward product or of the input-gradient product."""
@@ -198,14 +210,11 @@ class _Adapters:
         return (rhs.transpose(1, 2), lhs.transpose(1, 2)) if backward else (lhs, rhs)
 
     def operands(self, b_mn: int, backward: bool):
-        key = (b_mn, backward)
-        if key not in self._cache:
-            f1, f2 = self.factors(backward)
-            if b_mn == 0:
-                self._cache[key] = (_rank_rows(f1.transpose(1, 2)), _rank_cols(f2.transpose(1, 2), 16))
-            else:
-                self._cache[key] = (_rank_cols(f1, 64), _rank_rows(f2))
-        return self._cache[key]
+        """(P, U) of one product, for the launch that follows at once (a padded P lives in a shared buffer)."""
+        f1, f2 = self.factors(backward)
+        if b_mn == 0:
+            return _rank_rows(f1.transpose(1, 2)), _rank_cols(f2.transpose(1, 2), 16)
+        return _rank_cols(f1, 64), _rank_rows(f2)
 
 
 class QuantStack:
@@ -264,12 +273,14 @@ class QuantStack:
 
 
 def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, bias, store_low, backward=False,
-            tiles=None, epilogue=_lib.EPI_PLAIN, aux=None, out=None, x_rows=None, row_scale=None, w_grad=None):
+            tiles=None, epilogue=_lib.EPI_PLAIN, aux=None, out=None, x_rows=None, row_scale=None, w_grad=None,
+            out_rows=None):
     """One launch of the grouped product; returns (out, low). The reference's _launch (_grouped.py:313-345).
 
     k_contiguous_layout: whether the stack is logically (experts, n, k) for this product. x_rows (int32): the
     product's row i is row x_rows[i] of x (the routed rows read from the token-major tensor); row_scale (float32):
-    product row i scaled by row_scale[i]; w_grad (dSwiGLU, float32 (rows, ceil(N/96))): <dh_i, h_i> per 96 columns.
+    product row i scaled by row_scale[i]; w_grad (dSwiGLU, float32 (rows, ceil(N/96))): <dh_i, h_i> per 96 columns;
+    out_rows (int64, plain epilogue, bf16 stacks): product row i stored at row out_rows[i] of the output.
     """
     K = x.shape[1]
     rows = x_rows.numel() if x_rows is not None else x.shape[0]
@@ -322,6 +333,10 @@ def _launch(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, b
     p.row_scale = row_scale.data_ptr() if row_scale is not None else None
     if w_grad is not None:
         p.w_grad, p.w_ld = w_grad.data_ptr(), w_grad.stride(0)
+    if out_rows is not None:
+        if out_rows.dtype != torch.int64 or out_rows.numel() != rows:
+            raise ValueError("out_rows: one int64 destination row per product row")
+        p.out_rows = out_rows.data_ptr()
     p.scale = scale.data_ptr() if scale is not None else None
     p.panel = panel.data_ptr() if panel is not None else None
     p.up = up.data_ptr() if up is not None else None

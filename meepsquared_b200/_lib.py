@@ -30,6 +30,7 @@ class Product(ctypes.Structure):
         ("out", _p), ("ldo", _i64), ("low", _p), ("epilogue", _i32), ("aux", _p), ("sm_limit", _i32),
         ("block_m", _i32), ("wscale", _p),
         ("x_rows", _p), ("x_src_rows", _i64), ("row_scale", _p), ("w_grad", _p), ("w_ld", _i64),
+        ("out_rows", _p),
     ]
 
 
@@ -56,9 +57,11 @@ _SIGNATURES = {
     "meep2b_route_workspace_bytes": (_sz, [_i64, _i32]),
     "meep2b_route": (ctypes.c_int, [_p, _i64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
     "meep2b_route_noalloc": (ctypes.c_int, [_p, _i64, _i32, _p, _p, _p, _p, _p]),
+    "meep2b_route_logits": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "meep2b_routed_rows": (ctypes.c_int, [_p, _i64, _i32, _p, _i32, _p, _p, _p]),
     "meep2b_gather": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _i32, _p, _i32, _p, _p, _p]),
     "meep2b_unpermute": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p]),
+    "meep2b_combine": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p]),
     "meep2b_unpermute_backward": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _i32, _i64, _p, _p, _p]),
     "meep2b_weight_grad": (ctypes.c_int, [_p, _i64, _i32, _p, _i64, _p, _i32, _p, _p]),
     "meep2b_tile_map": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _p, _p]),
@@ -126,13 +129,13 @@ class DeviceError(RuntimeError):
 # Kernels each entry point launches per successful call (the ones this package calls on its hot path), for the
 # count of the library's launches in a timed region (benchmark); `launches` accumulates them per entry point.
 KERNELS_PER_CALL = {
-    "meep2b_route": 3, "meep2b_route_noalloc": 3, "meep2b_routed_rows": 1, "meep2b_gather": 1,
+    "meep2b_route": 3, "meep2b_route_noalloc": 3, "meep2b_route_logits": 3, "meep2b_routed_rows": 1, "meep2b_gather": 1,
     "meep2b_unpermute": 1, "meep2b_unpermute_backward": 1, "meep2b_tile_map": 1, "meep2b_grouped_product": 1,
     "meep2b_grouped_reduce": 1, "meep2b_grouped_reduce_rows": 1, "meep2b_fp8_stack_dequantize": 1,
     "meep2b_fp8_block_dequantize": 1, "meep2b_nf4_dequantize": 2, "meep2b_nf4_absmax": 1,
     "meep2b_merge_stack": 1,
     "meep2b_quant_multipliers": 1, "meep2b_fp8_rows_quantize": 1, "meep2b_grouped_product_f8": 1,
-    "meep2b_swiglu": 1, "meep2b_swiglu_backward": 1, "meep2b_weight_grad": 1,
+    "meep2b_swiglu": 1, "meep2b_swiglu_backward": 1, "meep2b_weight_grad": 1, "meep2b_combine": 1,
 }
 launches = {}
 

@@ -71,6 +71,43 @@ def route(top_k_index: torch.Tensor, top_k_weights, num_experts: int) -> Routing
     return Routing(perm, ids_g, offsets, inverse, weights_g, tokens, k, num_experts)
 
 
+def route_logits(router_logits: torch.Tensor, top_k: int, num_experts: int, norm_topk_prob: bool = True,
+                 probs: bool = True):
+    """The router of Transformers' MoE blocks (Qwen3MoeTopKRouter.forward after its linear layer: softmax in float32,
+    top-k, the weights renormalised when norm_topk_prob) and the routing permutation, in one pass over the logits.
+
+    router_logits (T, E) float32 or bf16. Returns (probs (T, E) float32 or None, top_k_weights (T, k) float32,
+    top_k_index (T, k) int64, Routing): the router's outputs, and the routing that routed_forward(..., routing=)
+    takes instead of sorting the ids again."""
+    if not router_logits.is_cuda:
+        raise RuntimeError("route_logits runs on a CUDA GPU")
+    if router_logits.dim() != 2 or router_logits.shape[1] != num_experts:
+        raise ValueError(f"router logits {tuple(router_logits.shape)}: (tokens, {num_experts}) expected")
+    if router_logits.dtype not in _WEIGHT_DTYPES:
+        raise TypeError(f"router logits in {router_logits.dtype}: float32 or bf16 expected")
+    lib = _lib.load()
+    logits = router_logits.contiguous()
+    tokens = logits.shape[0]
+    n = tokens * top_k
+    dev = logits.device
+    p = torch.empty((tokens, num_experts), dtype=torch.float32, device=dev) if probs else None
+    index = torch.empty((tokens, top_k), dtype=torch.int64, device=dev)
+    weights = torch.empty((tokens, top_k), dtype=torch.float32, device=dev)
+    perm = torch.empty(n, dtype=torch.int64, device=dev)
+    ids_g = torch.empty(n, dtype=torch.int64, device=dev)
+    inverse = torch.empty(n, dtype=torch.int64, device=dev)
+    offsets = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    ws_bytes = lib.meep2b_route_workspace_bytes(n, num_experts)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    _lib.check(lib.meep2b_route_logits(_lib.ptr(logits), _WEIGHT_DTYPES[logits.dtype], tokens, num_experts, top_k,
+                                       int(bool(norm_topk_prob)), _lib.ptr(p), _lib.ptr(index), _lib.ptr(weights),
+                                       _lib.ptr(perm), _lib.ptr(ids_g), _lib.ptr(offsets), _lib.ptr(inverse),
+                                       _lib.ptr(ws), ws_bytes, _lib.stream_of(logits)), "meep2b_route_logits")
+    routing = Routing(perm, ids_g, offsets, inverse, torch.empty(n, dtype=torch.float32, device=dev), tokens,
+                      top_k, num_experts)
+    return p, weights, index, routing
+
+
 def gather(hidden: torch.Tensor, routing: Routing, top_k_weights=None) -> torch.Tensor:
     """selected = hidden[perm // k] with sentinel rows zeroed (_moe.py:80,87); fills routing.weights_g."""
     if hidden.dtype != torch.bfloat16:
@@ -96,6 +133,21 @@ def unpermute(y: torch.Tensor, routing: Routing, weights_g=None) -> torch.Tensor
                                             _lib.ptr(routing.offsets), routing.num_experts, routing.num_tokens,
                                             routing.top_k, y.shape[1], _lib.ptr(out), _lib.stream_of(y)),
                "meep2b_unpermute")
+    return out
+
+
+def combine(y_tok: torch.Tensor, routing: Routing, top_k_weights=None) -> torch.Tensor:
+    """(T, H) bf16: the un-permute of rows stored token-major (row t * k + j: a product that placed its rows through
+    the permutation, out_rows = perm): sum over j of y_tok[t * k + j] * top_k_weights[t, j] (unweighted when None),
+    sentinel assignments contributing nothing. Each token's k rows are one contiguous read."""
+    y_tok = y_tok.contiguous()
+    out = torch.empty((routing.num_tokens, y_tok.shape[1]), dtype=torch.bfloat16, device=y_tok.device)
+    w = top_k_weights.contiguous() if top_k_weights is not None else None
+    wd = _WEIGHT_DTYPES[w.dtype] if w is not None else _lib.F32
+    _lib.check(_lib.load().meep2b_combine(_lib.ptr(y_tok), _lib.ptr(routing.inverse), _lib.ptr(w), wd,
+                                          _lib.ptr(routing.offsets), routing.num_experts, routing.num_tokens,
+                                          routing.top_k, y_tok.shape[1], _lib.ptr(out), _lib.stream_of(y_tok)),
+               "meep2b_combine")
     return out
 
 
@@ -159,8 +211,11 @@ class _RoutedExperts(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, hidden, top_k_weights, lhs1, rhs1, lhs2, rhs2, top_k_index, st: _Stacks):
-        routing = route(top_k_index, top_k_weights, st.num_experts)
+    def forward(ctx, hidden, top_k_weights, lhs1, rhs1, lhs2, rhs2, top_k_index, st: _Stacks, routing=None):
+        if routing is None:
+            routing = route(top_k_index, top_k_weights, st.num_experts)
+        elif routing.weights_g is None or routing.weights_g.dtype != top_k_weights.dtype:
+            routing.weights_g = torch.empty(routing.perm.numel(), dtype=top_k_weights.dtype, device=hidden.device)
         mode = os.environ.get("MEEP2B_ROUTED_ROWS", "fold")
         if (isinstance(st.gate_up, _grouped.QuantStack) or isinstance(st.down, _grouped.QuantStack)
                 or st.down_bias is not None or mode not in ("fold", "gather")):
@@ -193,9 +248,17 @@ class _RoutedExperts(torch.autograd.Function):
                                    st.gate_up_bias, True, tiles=tiles, epilogue=_lib.EPI_SWIGLU, aux=gu,
                                    x_rows=x_rows)
         del gate_up  # a stack dequantised for this product alone is released before the next one is made
-        y, low2 = _grouped._launch(h, _stack(st.down), st.down_scale, routing.offsets, not t, ad2, st.scaling2,
-                                   st.down_bias, True, tiles=tiles)
-        out = unpermute(y, routing, weights_g)
+        if mode == "copy":
+            y, low2 = _grouped._launch(h, _stack(st.down), st.down_scale, routing.offsets, not t, ad2, st.scaling2,
+                                       st.down_bias, True, tiles=tiles)
+            out = unpermute(y, routing, weights_g)
+        else:
+            # the combine of _moe.py:123-126 fused into the down product: its epilogue stores each row at the row's
+            # flat assignment (token-major), and the weighted sum over a token's k rows reads one contiguous run
+            y, low2 = _grouped._launch(h, _stack(st.down), st.down_scale, routing.offsets, not t, ad2, st.scaling2,
+                                       st.down_bias, True, tiles=tiles, out_rows=routing.perm)
+            out = combine(y, routing, top_k_weights)
+            del y
         kept = (x, gu, h, y) if mode == "copy" else (hidden, gu, h, token_rows, w32)
         ctx.save_for_backward(*kept, *(v for v in (low1, low2) if v is not None))
         ctx.routing, ctx.st, ctx.ad1, ctx.ad2, ctx.mode = routing, st, ad1, ad2, mode
@@ -255,8 +318,12 @@ class _RoutedExperts(torch.autograd.Function):
                 second = dict(g=grad_out, low=low2, g_rows=token_rows, row_scale=w32)
             grads[2], grads[3] = _adapter_grads(ad2, ctx.leaves[2], ctx.leaves[3], first, second, routing.offsets,
                                                 st.scaling2)
-        dsel, low1b = _grouped._launch(dgu, _stack(st.gate_up), st.gate_up_scale, routing.offsets, t, ad1, st.scaling1,
-                                       None, True, backward=True, tiles=tiles)
+        gate_up_stack = _stack(st.gate_up)
+        token_major = not isinstance(gate_up_stack, _grouped.QuantStack)  # quantised products store rows in order
+        dsel, low1b = _grouped._launch(dgu, gate_up_stack, st.gate_up_scale, routing.offsets, t, ad1, st.scaling1,
+                                       None, True, backward=True, tiles=tiles,
+                                       out_rows=routing.perm if token_major else None)
+        del gate_up_stack
         if ad1 is not None:
             if mode == "copy":
                 first = dict(g=sel, low=low1b)
@@ -265,9 +332,9 @@ class _RoutedExperts(torch.autograd.Function):
             second = dict(g=dgu, low=low1)
             grads[0], grads[1] = _adapter_grads(ad1, ctx.leaves[0], ctx.leaves[1], first, second, routing.offsets,
                                                 st.scaling1)
-        grad_hidden = unpermute(dsel, routing, None)
+        grad_hidden = combine(dsel, routing, None) if token_major else unpermute(dsel, routing, None)
         grad_w = grad_w.view(routing.num_tokens, routing.top_k)
-        return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None)
+        return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None, None)
 
 
 def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling):
@@ -497,7 +564,7 @@ def _fp8_products_layer(experts, device) -> bool:
     return fp8 and _grouped.fp8_products(device)
 
 
-def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
+def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors, routing=None):
     """The routed layer of an experts module with its adapters: _moe._routed_forward's contract.
 
     experts: a Transformers experts module (num_experts, has_gate, has_bias, is_transposed, gate_up_proj or
@@ -505,7 +572,8 @@ def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
     stacks as an ``_nf4.NF4State`` in the stack's place). factors: {stack name: (lhs, rhs, scaling)} in PEFT's
     layout. A gated module with Transformers' default SiLU gate and a gate/up stack stored (experts, 2I, hidden)
     runs the fused layer (SwiGLU in the products' epilogues, one autograd node); any other module runs the
-    unfused form, its own gate or activation between the products.
+    unfused form, its own gate or activation between the products. routing: the Routing of these ids from
+    route_logits (the router fused with the sort), used instead of sorting them again by the fused layer.
     """
     if not hidden_states.is_cuda:
         raise RuntimeError("the routed layer runs on a CUDA GPU (compute capability 10.0)")
@@ -526,4 +594,4 @@ def routed_forward(experts, hidden_states, top_k_index, top_k_weights, factors):
                  bias2.detach().to(torch.bfloat16).contiguous() if bias2 is not None else None,
                  bool(experts.is_transposed), int(experts.num_experts), float(s1), float(s2))
     return _RoutedExperts.apply(hidden_states.to(torch.bfloat16), top_k_weights, cast(lhs1), cast(rhs1), cast(lhs2),
-                                cast(rhs2), top_k_index, st)
+                                cast(rhs2), top_k_index, st, routing)

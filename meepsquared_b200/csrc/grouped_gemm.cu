@@ -21,6 +21,10 @@
 #ifndef MEEP2B_KSTEP_FENCE
 #define MEEP2B_KSTEP_FENCE 1
 #endif
+// k-steps ahead of the loads at which the producer prefetches the operand tiles into L2 (0: none)
+#ifndef MEEP2B_L2_PREFETCH
+#define MEEP2B_L2_PREFETCH 0
+#endif
 
 namespace meep2b {
 namespace gemm {
@@ -75,6 +79,8 @@ struct Params {
   const float* row_scale;
   float* w_grad;
   int64_t w_ld;
+  // PLAIN epilogue: product row i is stored at row out_rows[i] of out (token-major rows for a streaming combine)
+  const int64_t* out_rows;
 };
 
 // silu(g) = g / (1 + exp(-g)) with the fast exponential and division intrinsics; the result is rounded to bf16.
@@ -317,7 +323,8 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
     }
     if (valid && cols > 0) {
       const __nv_bfloat16* bias = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + n0 : nullptr;
-      __nv_bfloat16* dst = p.out + orow * p.ldo + n0;
+      const int64_t drow = p.out_rows != nullptr ? p.out_rows[row] : orow;
+      __nv_bfloat16* dst = p.out + drow * p.ldo + n0;
 #pragma unroll
       for (int c = 0; c < 6; ++c) {
         const int cnt = min(16, cols - 16 * c);
@@ -587,6 +594,27 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
+          }
+          if (MEEP2B_L2_PREFETCH > 0) {
+            // the operand tiles MEEP2B_L2_PREFETCH k-steps ahead (in this unit or the next one of this CTA) into L2
+            int pk = kb + MEEP2B_L2_PREFETCH, pu2 = u;
+            if (pk >= p.kblocks) pk -= p.kblocks, pu2 += gridDim.x;
+            if (pu2 < total && pk < p.kblocks) {
+              const int t2 = pu2 / p.nblocks, nb2 = pu2 - t2 * p.nblocks;
+              const int e2 = p.tile_expert[t2];
+              if (!GATHER) tma_prefetch_l2_2d(&tm_x, pk * BK, p.tile_row[t2]);
+              if (!B_MN) {
+                if (EPI == MEEP2B_EPI_SWIGLU) {
+                  tma_prefetch_l2_3d(&tm_w, pk * BK, nb2 * 96, e2);
+                  tma_prefetch_l2_3d(&tm_w, pk * BK, p.inter + nb2 * 96, e2);
+                } else {
+                  tma_prefetch_l2_3d(&tm_w, pk * BK, nb2 * BN, e2);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 3; ++j) tma_prefetch_l2_3d(&tm_w, nb2 * BN + 64 * j, pk * BK, e2);
+              }
+            }
           }
           if (LORA && kb == 0 && pu >= 0 && !load_u()) { ok = false; break; }
         }
@@ -879,6 +907,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             stage = 0;
             phase ^= 1;
           }
+          if (MEEP2B_L2_PREFETCH > 0 && !B_MN) {
+            // this CTA's operand tiles MEEP2B_L2_PREFETCH k-steps ahead into L2 (its x rows and its half of B)
+            int pk = kb + MEEP2B_L2_PREFETCH, pu2 = u;
+            if (pk >= p.kblocks) pk -= p.kblocks, pu2 += pairs;
+            if (pu2 < total && pk < p.kblocks) {
+              const int t2 = pu2 / p.nblocks, nb2 = pu2 - t2 * p.nblocks;
+              const int e2 = p.tile_expert[t2];
+              if (!GATHER) tma_prefetch_l2_2d(&m.x, pk * BK, p.tile_row[t2] + 128 * static_cast<int>(rank));
+              const int brow = EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? nb2 * 96 : p.inter + nb2 * 96)
+                                                        : nb2 * BN + 96 * static_cast<int>(rank);
+              tma_prefetch_l2_3d(&m.w96, pk * BK, brow, e2);
+            }
+          }
           if (LORA && kb == 0 && pu >= 0 && !load_u()) { ok = false; break; }
         }
         if (!ok) break;
@@ -1056,6 +1097,7 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
                  !((epi == MEEP2B_EPI_SWIGLU && !a->b_mn) || (epi == MEEP2B_EPI_DSWIGLU && a->b_mn))))
     return MEEP2B_ERR_UNSUPPORTED;
   if (a->w_grad != nullptr && (epi != MEEP2B_EPI_DSWIGLU || a->w_ld < (a->n + 95) / 96)) return MEEP2B_ERR_SHAPE;
+  if (a->out_rows != nullptr && (epi != MEEP2B_EPI_PLAIN || quantised)) return MEEP2B_ERR_UNSUPPORTED;
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
   if (a->rows == 0) return MEEP2B_OK;
@@ -1139,6 +1181,7 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   prm.row_scale = a->row_scale;
   prm.w_grad = a->w_grad;
   prm.w_ld = a->w_ld;
+  prm.out_rows = a->out_rows;
   prm.v8 = aligned32(a->out) && (a->aux == nullptr || aligned32(a->aux)) && (a->low == nullptr || aligned32(a->low)) &&
            a->ldo % 16 == 0 && prm.ld_aux % 16 == 0;
 

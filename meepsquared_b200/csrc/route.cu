@@ -114,6 +114,94 @@ __global__ void __launch_bounds__(kRouteThreads) route_scatter(const int64_t* __
   }
 }
 
+// The router of Transformers' MoE blocks (Qwen3MoeTopKRouter.forward: softmax in float32 over the experts, top-k,
+// the k weights renormalised to sum to one) fused with the first pass of the routing sort: CTA c computes the tokens
+// whose assignments t * top_k + j fall in chunk c (kRouteChunk assignments, the histogram's chunking) and counts the
+// chunk's assignments per expert, so route_scan and route_scatter follow directly. One warp per token, the token's
+// logits spread over the lanes (expert e at lane e % 32, slot e / 32); the maximum and the sum go through butterfly
+// shuffles; the top k by k rounds of a warp arg-max (largest probability, the smaller expert index on a tie), so
+// the k weights come out in descending order as torch.topk returns them. A token whose assignments straddle two
+// chunks is computed by both CTAs, which write the same values.
+constexpr int kRouterWarps = 16;
+
+__device__ __forceinline__ float logit_value(const float* p, int64_t i) { return p[i]; }
+__device__ __forceinline__ float logit_value(const __nv_bfloat16* p, int64_t i) { return __bfloat162float(p[i]); }
+
+template <typename L, int PER>
+__global__ void __launch_bounds__(kRouterWarps * 32) router_topk(const L* __restrict__ logits, int64_t tokens,
+                                                                int experts, int top_k, bool norm,
+                                                                float* __restrict__ probs,
+                                                                int64_t* __restrict__ index,
+                                                                float* __restrict__ weights, int* __restrict__ counts) {
+  extern __shared__ int router_hist[];
+  const int buckets = experts + 1;
+  for (int b = threadIdx.x; b < buckets; b += blockDim.x) router_hist[b] = 0;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t a0 = static_cast<int64_t>(blockIdx.x) * kRouteChunk;
+  const int64_t a1 = min(a0 + kRouteChunk, tokens * top_k);
+  const int64_t t0 = a0 / top_k, t1 = (a1 + top_k - 1) / top_k;
+  for (int64_t t = t0 + warp; t < t1; t += kRouterWarps) {
+    const L* row = logits + t * experts;
+    float v[PER];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = i * 32 + lane;
+      v[i] = e < experts ? logit_value(row, e) : -INFINITY;
+      m = fmaxf(m, v[i]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = i * 32 + lane;
+      v[i] = e < experts ? expf(v[i] - m) : 0.f;
+      sum += v[i];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = i * 32 + lane;
+      v[i] = __fdiv_rn(v[i], sum);
+      if (probs != nullptr && e < experts) probs[t * experts + e] = v[i];
+    }
+    uint32_t taken = 0;
+    float mine_v = 0.f;
+    int mine_i = 0;
+    for (int j = 0; j < top_k; ++j) {
+      float bv = -1.f;
+      int bi = INT_MAX;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = i * 32 + lane;
+        if (e < experts && !((taken >> i) & 1u) && v[i] > bv) bv = v[i], bi = e;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+      }
+      if (bi != INT_MAX && (bi & 31) == lane) taken |= 1u << (bi >> 5);  // (NaN logits select nothing)
+      if (lane == j) mine_v = bv, mine_i = bi;
+    }
+    float wsum = 0.f;
+    for (int j = 0; j < top_k; ++j) wsum += __shfl_sync(0xffffffffu, mine_v, j);
+    if (lane < top_k) {
+      const int64_t a = t * top_k + lane;
+      index[a] = mine_i;
+      weights[a] = norm ? __fdiv_rn(mine_v, wsum) : mine_v;
+      if (a >= a0 && a < a1) atomicAdd(&router_hist[mine_i < experts ? mine_i : experts], 1);
+    }
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < buckets; b += blockDim.x)
+    counts[static_cast<int64_t>(blockIdx.x) * buckets + b] = router_hist[b];
+}
+
 // selected[i] = hidden[perm[i] / top_k] (zero past the real rows); weights_g[i] = weights[perm[i]].
 // One warp per row, 16-byte vectors.
 template <typename W>
@@ -155,8 +243,11 @@ __device__ __forceinline__ float weight_value(const __nv_bfloat16* w, int64_t i)
 // each product rounded to bf16 (bf16 * bf16), summed in float32. No weights: a plain float32 sum. The token's row
 // indices and weights are read once into shared memory, and every thread issues the loads of all its rows before
 // it sums them (in order j = 0, 1, ...), so a token costs one round trip to memory rather than top_k.
+// TOKEN_MAJOR (the combine): y holds the rows in token-major order, row t * top_k + j for the token's j-th
+// assignment (the down product stored them there through the permutation), and weights_g is the routing weights
+// in the same (tokens, top_k) order; inverse only tells which assignments are sentinels (never stored).
 constexpr int kUnpermuteGroup = 8;  // rows whose loads are in flight together
-template <typename W>
+template <typename W, bool TOKEN_MAJOR = false>
 __global__ void __launch_bounds__(256) unpermute_rows(const uint4* __restrict__ y, const int64_t* __restrict__ inverse,
                                                      const W* __restrict__ weights_g,
                                                      const int32_t* __restrict__ offsets, int experts,
@@ -168,8 +259,9 @@ __global__ void __launch_bounds__(256) unpermute_rows(const uint4* __restrict__ 
   const int64_t valid = offsets[experts - 1];
   for (int j = threadIdx.x; j < top_k; j += blockDim.x) {
     const int64_t r = inverse[t * top_k + j];
-    rows_s[j] = r < valid ? r : -1;  // a sentinel row: masked to zero (_moe.py:116)
-    w_s[j] = (weights_g != nullptr && r < valid) ? weight_value(weights_g, r) : 1.f;
+    const int64_t src = TOKEN_MAJOR ? t * top_k + j : r;
+    rows_s[j] = r < valid ? src : -1;  // a sentinel row: masked to zero (_moe.py:116)
+    w_s[j] = (weights_g != nullptr && r < valid) ? weight_value(weights_g, src) : 1.f;
   }
   __syncthreads();
   const bool round_bf16 = sizeof(W) == 2;
@@ -364,6 +456,52 @@ int meep2b_route(const int64_t* expert_ids, int64_t assignments, int32_t experts
   return launch_status();
 }
 
+int meep2b_route_logits(const void* logits, int32_t logits_dtype, int64_t tokens, int32_t experts, int32_t top_k,
+                        int32_t norm_topk_prob, float* probs, int64_t* top_k_index, float* top_k_weights,
+                        int64_t* perm, int64_t* expert_ids_g, int32_t* offsets, int64_t* inverse, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (experts < 1 || experts + 1 > kMaxBuckets || tokens < 0 || top_k < 1 || top_k > 32 || top_k > experts)
+    return MEEP2B_ERR_SHAPE;
+  if (tokens > INT32_MAX / top_k) return MEEP2B_ERR_SHAPE;
+  if (logits_dtype != MEEP2B_F32 && logits_dtype != MEEP2B_BF16) return MEEP2B_ERR_DTYPE;
+  const int64_t assignments = tokens * top_k;
+  if (workspace_bytes < meep2b_route_workspace_bytes(assignments, experts)) return MEEP2B_ERR_SHAPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  if (assignments == 0) {
+    cudaMemsetAsync(offsets, 0, sizeof(int32_t) * experts, s);
+    return launch_status();
+  }
+  const int blocks = static_cast<int>((assignments + kRouteChunk - 1) / kRouteChunk);
+  int* counts = static_cast<int*>(workspace);
+  const size_t hist_smem = sizeof(int) * (experts + 1);
+  const int per = (experts + 31) / 32;
+  const bool norm = norm_topk_prob != 0;
+#define MEEP2B_ROUTER(L, PER)                                                                               \
+  router_topk<L, PER><<<blocks, kRouterWarps * 32, hist_smem, s>>>(static_cast<const L*>(logits), tokens, experts, \
+                                                                  top_k, norm, probs, top_k_index, top_k_weights,  \
+                                                                  counts)
+#define MEEP2B_ROUTER_PER(L)          \
+  if (per <= 1) MEEP2B_ROUTER(L, 1);  \
+  else if (per <= 2) MEEP2B_ROUTER(L, 2); \
+  else if (per <= 4) MEEP2B_ROUTER(L, 4); \
+  else if (per <= 8) MEEP2B_ROUTER(L, 8); \
+  else if (per <= 16) MEEP2B_ROUTER(L, 16); \
+  else MEEP2B_ROUTER(L, 32);
+  if (logits_dtype == MEEP2B_BF16) {
+    MEEP2B_ROUTER_PER(__nv_bfloat16)
+  } else {
+    MEEP2B_ROUTER_PER(float)
+  }
+#undef MEEP2B_ROUTER_PER
+#undef MEEP2B_ROUTER
+  route_scan<<<1, 1024, 0, s>>>(counts, blocks, experts, offsets);
+  const size_t scatter_smem = sizeof(int) * 9 * (experts + 1);
+  route_scatter<<<blocks, kRouteThreads, scatter_smem, s>>>(top_k_index, assignments, experts, counts, perm,
+                                                            expert_ids_g, inverse);
+  return launch_status();
+}
+
 int meep2b_routed_rows(const int64_t* perm, int64_t assignments, int32_t top_k, const void* weights,
                        int32_t weights_dtype, int32_t* token_rows, float* weights_g, void* stream) {
   if (top_k < 1 || assignments < 0) return MEEP2B_ERR_SHAPE;
@@ -422,6 +560,30 @@ int meep2b_unpermute(const void* y, const int64_t* inverse, const void* weights_
   else
     unpermute_rows<float><<<static_cast<unsigned>(tokens), threads, smem, s>>>(
         static_cast<const uint4*>(y), inverse, static_cast<const float*>(weights_g), offsets, experts, top_k, vec,
+        static_cast<uint4*>(out));
+  return launch_status();
+}
+
+int meep2b_combine(const void* y_tok, const int64_t* inverse, const void* weights, int32_t weights_dtype,
+                   const int32_t* offsets, int32_t experts, int64_t tokens, int32_t top_k, int64_t hidden_dim,
+                   void* out, void* stream) {
+  if (top_k < 1 || experts < 1 || tokens < 0 || hidden_dim % 8 != 0) return MEEP2B_ERR_SHAPE;
+  if (!aligned16(y_tok) || !aligned16(out)) return MEEP2B_ERR_ALIGN;
+  if (weights != nullptr && weights_dtype != MEEP2B_F32 && weights_dtype != MEEP2B_BF16) return MEEP2B_ERR_DTYPE;
+  cudaStream_t s = as_stream(stream);
+  MEEP2B_TRY(bind_stream_device(s));
+  if (tokens == 0) return MEEP2B_OK;
+  const int64_t vec = hidden_dim / 8;
+  const int threads = vec >= 256 ? 256 : static_cast<int>(((vec + 31) / 32) * 32);
+  const size_t smem = static_cast<size_t>(top_k) * (sizeof(int64_t) + sizeof(float));
+  if (smem > 48 * 1024) return MEEP2B_ERR_SHAPE;
+  if (weights != nullptr && weights_dtype == MEEP2B_BF16)
+    unpermute_rows<__nv_bfloat16, true><<<static_cast<unsigned>(tokens), threads, smem, s>>>(
+        static_cast<const uint4*>(y_tok), inverse, static_cast<const __nv_bfloat16*>(weights), offsets, experts,
+        top_k, vec, static_cast<uint4*>(out));
+  else
+    unpermute_rows<float, true><<<static_cast<unsigned>(tokens), threads, smem, s>>>(
+        static_cast<const uint4*>(y_tok), inverse, static_cast<const float*>(weights), offsets, experts, top_k, vec,
         static_cast<uint4*>(out));
   return launch_status();
 }

@@ -70,3 +70,18 @@ def tile_map(offsets, rows: int, block_m: int = 128):
     tile_expert = np.minimum(np.searchsorted(ends, t, side="right"), experts - 1)
     tile_row = starts[tile_expert] + (t - (ends - per_expert)[tile_expert]) * block_m
     return tile_expert.astype(np.int32), tile_row.astype(np.int32), int(ends[-1])
+
+
+def router(logits, top_k: int, norm_topk_prob: bool = True):
+    """The router of Transformers' MoE blocks after its linear layer (Qwen3MoeTopKRouter.forward, transformers
+    models/qwen3_moe/modeling_qwen3_moe.py): probs = softmax(logits) in float32 over the experts, the top_k largest
+    in descending order (a tie to the smaller expert index), their probabilities divided by their sum when
+    norm_topk_prob. Returns (probs (T, E), top_k_weights (T, k), top_k_index (T, k) int64), float32."""
+    x = np.asarray(logits, dtype=np.float32)
+    e = np.exp(x - x.max(axis=1, keepdims=True))
+    probs = (e / e.sum(axis=1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    order = np.argsort(-probs, axis=1, kind="stable")[:, :top_k]  # stable: equal values keep the smaller index
+    top = np.take_along_axis(probs, order, axis=1)
+    if norm_topk_prob:
+        top = (top / top.sum(axis=1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    return probs, top, order.astype(np.int64)

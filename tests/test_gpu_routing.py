@@ -93,6 +93,91 @@ def test_gather_and_unpermute_match_the_oracle(wdtype):
     assert_close(as_np(gw).reshape(-1), flat, "grad_weights", scaled=True)  # a sum over the hidden size
 
 
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.bfloat16])
+def test_the_token_major_combine_gives_the_bits_of_the_unpermute(wdtype):
+    """Rows stored at their flat assignment (token-major, as the down product stores them through out_rows = perm)
+    and summed by meep2b_combine with the router-order weights: the same bits as the un-permute of the same rows in
+    expert order with the weights in expert order; sentinel assignments (never stored) count as zero."""
+    cfg = dict(layer_inputs.SMALL)
+    inp = layer_inputs.layer(**cfg)
+    idx = inp["top_k_index"].clone()
+    idx[3, 1] = cfg["experts"]  # a sentinel
+    idx[7, 0] = cfg["experts"] + 5
+    w = inp["top_k_weights"].to(wdtype).to(DEV)
+    r = mb.route(idx.to(DEV), w, cfg["experts"])
+    mb.gather(torch.zeros(cfg["tokens"], 8, dtype=torch.bfloat16, device=DEV), r, w)  # fills r.weights_g
+    rows = r.perm.numel()
+    y = torch.randn(rows, cfg["hidden"], generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).to(DEV)
+    y_tok = torch.full_like(y, float("nan"))  # slots of sentinel assignments are never written
+    valid = int(r.offsets[-1])
+    y_tok[r.perm[:valid]] = y[:valid]
+    for weights, weights_g in ((w, r.weights_g), (None, None)):
+        got = _moe.combine(y_tok, r, weights)
+        want = mb.unpermute(y, r, weights_g)
+        assert torch.equal(got, want)
+
+
+def _same_topk_up_to_ties(got_idx, want_idx, probs):
+    """The selected experts agree, except where the k-th and (k+1)-th probabilities of a token are within a few
+    float32 units (then either choice is a correct top-k of values that differ only by rounding)."""
+    got_idx, want_idx = np.asarray(got_idx), np.asarray(want_idx)
+    differ = np.nonzero((got_idx != want_idx).any(axis=1))[0]
+    srt = -np.sort(-probs, axis=1)
+    for t in differ:
+        k = got_idx.shape[1]
+        assert abs(srt[t, k - 1] - srt[t, k]) <= 4e-7 * srt[t, k - 1] or \
+            abs(srt[t, :k][:-1] - srt[t, 1:k]).min() <= 4e-7 * srt[t, 0], f"token {t}"
+    assert differ.size <= max(1, got_idx.shape[0] // 1000)
+
+
+@pytest.mark.parametrize("logits_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("tokens,experts,k,norm", [(16384, 128, 8, True), (8192, 8, 2, True), (777, 60, 4, False),
+                                                   (300, 1000, 32, True)])
+def test_the_router_fused_with_the_sort_matches_the_oracle(logits_dtype, tokens, experts, k, norm):
+    """route_logits: the router (softmax, top-k, renormalised weights) against the numpy restatement of
+    Transformers' router, and its routing bit-exact with route() over the ids it chose (the router's pass does the
+    sort's histogram)."""
+    gen = torch.Generator().manual_seed(tokens + experts)
+    logits = torch.randn(tokens, experts, generator=gen).to(logits_dtype)
+    probs, weights, index, r = _moe.route_logits(logits.to(DEV), k, experts, norm_topk_prob=norm)
+    p_ref, w_ref, i_ref = oroute.router(logits.float().numpy(), k, norm)
+    np.testing.assert_allclose(as_np(probs), p_ref, rtol=2e-6, atol=1e-9)
+    _same_topk_up_to_ties(as_np(index).astype(np.int64), i_ref, p_ref)
+    same = (as_np(index).astype(np.int64) == i_ref).all(axis=1)
+    np.testing.assert_allclose(as_np(weights)[same], w_ref[same], rtol=2e-6, atol=1e-9)
+    want = mb.route(index, weights, experts)
+    for name in ("perm", "expert_ids_g", "offsets", "inverse"):
+        assert torch.equal(getattr(r, name), getattr(want, name)), name
+    # and against torch's own softmax / topk on the GPU
+    tp = torch.softmax(logits.to(DEV), dim=-1, dtype=torch.float32)
+    torch.testing.assert_close(probs, tp, rtol=2e-6, atol=1e-9)
+
+
+def test_the_fused_router_feeds_the_layer_with_the_bits_of_the_plain_routing():
+    """routed_forward(..., routing=route_logits(...)[3]) gives the bits of routed_forward over the same ids."""
+    cfg = dict(layer_inputs.SMALL)
+    inp = layer_inputs.layer(**cfg)
+    gen = torch.Generator().manual_seed(5)
+    logits = torch.randn(cfg["tokens"], cfg["experts"], generator=gen).to(DEV)
+
+    class Experts(torch.nn.Module):
+        pass
+
+    ex = Experts()
+    ex.num_experts, ex.has_gate, ex.has_bias, ex.is_transposed = cfg["experts"], True, False, False
+    ex.gate_up_proj = inp["gate_up"].to(DEV, torch.bfloat16)
+    ex.down_proj = inp["down"].to(DEV, torch.bfloat16)
+    fac = {"gate_up_proj": (inp["gate_up_lhs"].to(DEV, torch.bfloat16), inp["gate_up_rhs"].to(DEV, torch.bfloat16),
+                            inp["scaling"]),
+           "down_proj": (inp["down_lhs"].to(DEV, torch.bfloat16), inp["down_rhs"].to(DEV, torch.bfloat16),
+                         inp["scaling"])}
+    hidden = inp["hidden"].to(DEV, torch.bfloat16)
+    _, weights, index, r = _moe.route_logits(logits, cfg["top_k"], cfg["experts"])
+    a = mb.routed_forward(ex, hidden, index, weights, fac, routing=r)
+    b = mb.routed_forward(ex, hidden, index, weights, fac)
+    assert torch.equal(a, b)
+
+
 def test_empty_routing():
     r = mb.route(torch.zeros((0, 2), dtype=torch.int64, device=DEV), None, 4)
     assert r.perm.numel() == 0 and r.offsets.cpu().tolist() == [0, 0, 0, 0]

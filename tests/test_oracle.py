@@ -240,3 +240,27 @@ def test_fp8_product_is_exact_on_representable_activations():
     w = quant.e4m3_to_f32(codes)
     want = np.concatenate([x[:15] @ w[0].T * 0.5, x[15:] @ w[1].T * 2.0]).astype(np.float32)
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-3 * np.abs(want).max())
+
+
+def test_the_router_restatement_matches_transformers_router():
+    """oracle.routing.router against Transformers' own Qwen3MoeTopKRouter on the CPU (the router whose outputs the
+    routed layer takes): the same experts in the same order, probabilities and weights within float32 rounding."""
+    import torch
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeTopKRouter
+
+    class Config:
+        num_experts_per_tok, num_experts, norm_topk_prob, hidden_size = 8, 128, True, 64
+
+    for norm in (True, False):
+        Config.norm_topk_prob = norm
+        router = Qwen3MoeTopKRouter(Config())
+        gen = torch.Generator().manual_seed(0)
+        router.weight.data = torch.randn(router.weight.shape, generator=gen)
+        h = torch.randn(512, 64, generator=gen)
+        with torch.no_grad():
+            probs, weights, index = router(h)
+            logits = torch.nn.functional.linear(h, router.weight)
+        p, w, i = routing.router(logits.numpy(), 8, norm)
+        np.testing.assert_array_equal(i, index.numpy())
+        np.testing.assert_allclose(p, probs.numpy(), rtol=1e-5, atol=1e-7)
+        np.testing.assert_allclose(w, weights.numpy(), rtol=1e-5, atol=1e-7)
