@@ -21,10 +21,6 @@
 #ifndef MEEP2B_KSTEP_FENCE
 #define MEEP2B_KSTEP_FENCE 1
 #endif
-// k-steps ahead of the loads at which the producer prefetches the operand tiles into L2 (0: none)
-#ifndef MEEP2B_L2_PREFETCH
-#define MEEP2B_L2_PREFETCH 0
-#endif
 
 namespace meep2b {
 namespace gemm {
@@ -595,27 +591,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             stage = 0;
             phase ^= 1;
           }
-          if (MEEP2B_L2_PREFETCH > 0) {
-            // the operand tiles MEEP2B_L2_PREFETCH k-steps ahead (in this unit or the next one of this CTA) into L2
-            int pk = kb + MEEP2B_L2_PREFETCH, pu2 = u;
-            if (pk >= p.kblocks) pk -= p.kblocks, pu2 += gridDim.x;
-            if (pu2 < total && pk < p.kblocks) {
-              const int t2 = pu2 / p.nblocks, nb2 = pu2 - t2 * p.nblocks;
-              const int e2 = p.tile_expert[t2];
-              if (!GATHER) tma_prefetch_l2_2d(&tm_x, pk * BK, p.tile_row[t2]);
-              if (!B_MN) {
-                if (EPI == MEEP2B_EPI_SWIGLU) {
-                  tma_prefetch_l2_3d(&tm_w, pk * BK, nb2 * 96, e2);
-                  tma_prefetch_l2_3d(&tm_w, pk * BK, p.inter + nb2 * 96, e2);
-                } else {
-                  tma_prefetch_l2_3d(&tm_w, pk * BK, nb2 * BN, e2);
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 3; ++j) tma_prefetch_l2_3d(&tm_w, nb2 * BN + 64 * j, pk * BK, e2);
-              }
-            }
-          }
           if (LORA && kb == 0 && pu >= 0 && !load_u()) { ok = false; break; }
         }
         if (!ok) break;
@@ -906,19 +881,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (++stage == PP::STAGES) {
             stage = 0;
             phase ^= 1;
-          }
-          if (MEEP2B_L2_PREFETCH > 0 && !B_MN) {
-            // this CTA's operand tiles MEEP2B_L2_PREFETCH k-steps ahead into L2 (its x rows and its half of B)
-            int pk = kb + MEEP2B_L2_PREFETCH, pu2 = u;
-            if (pk >= p.kblocks) pk -= p.kblocks, pu2 += pairs;
-            if (pu2 < total && pk < p.kblocks) {
-              const int t2 = pu2 / p.nblocks, nb2 = pu2 - t2 * p.nblocks;
-              const int e2 = p.tile_expert[t2];
-              if (!GATHER) tma_prefetch_l2_2d(&m.x, pk * BK, p.tile_row[t2] + 128 * static_cast<int>(rank));
-              const int brow = EPI == MEEP2B_EPI_SWIGLU ? (rank == 0 ? nb2 * 96 : p.inter + nb2 * 96)
-                                                        : nb2 * BN + 96 * static_cast<int>(rank);
-              tma_prefetch_l2_3d(&m.w96, pk * BK, brow, e2);
-            }
           }
           if (LORA && kb == 0 && pu >= 0 && !load_u()) { ok = false; break; }
         }
