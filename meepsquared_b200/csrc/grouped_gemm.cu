@@ -641,6 +641,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         pend = -1;
         return true;
       };
+      // The descriptors of stage 0, k-slice 0; another stage or k-slice is an add to the start-address field
+      // (bits 0-13, 16-byte units), which stays below 2^14 for every shared-memory address of the plan.
+      const uint64_t a_desc0 = smem_desc(sbase + P::OFF_A, 16, 1024, 2);
+      const uint64_t b_desc0 =
+          B_MN ? smem_desc(sbase + P::OFF_B, 8192, 1024, 2) : smem_desc(sbase + P::OFF_B, 16, 1024, 2);
+      constexpr uint32_t B_KK = B_MN ? 2048 / 16 : 32 / 16;  // one k-slice of 16, in 16-byte units
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++it) {
         const int ab = it & 1;
         const uint32_t aph = (it >> 1) & 1;
@@ -650,15 +656,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait(bar_full(stage), phase)) { ok = false; break; }
           if (MEEP2B_KSTEP_FENCE) tc_fence_after();
-          const uint32_t a_addr = sbase + P::OFF_A + stage * A_BYTES;
-          const uint32_t b_addr = sbase + P::OFF_B + stage * P::B_BYTES;
+          const uint64_t a_st = a_desc0 + static_cast<uint32_t>(stage) * (A_BYTES / 16);
+          const uint64_t b_st = b_desc0 + static_cast<uint32_t>(stage) * (P::B_BYTES / 16);
+          mma_bf16(d, a_st, b_st, IDESC_MAIN, kb != 0);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024, 2);
-            const uint64_t bdesc =
-                B_MN ? smem_desc(b_addr + kk * 2048, 8192, 1024, 2) : smem_desc(b_addr + kk * 32, 16, 1024, 2);
-            mma_bf16(d, adesc, bdesc, IDESC_MAIN, (kb | kk) != 0);
-          }
+          for (int kk = 1; kk < BK / 16; ++kk) mma_bf16(d, a_st + 2 * kk, b_st + B_KK * kk, IDESC_MAIN, 1);
           mma_commit(bar_empty(stage));
           if (++stage == STAGES) {
             stage = 0;
@@ -930,6 +932,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         pend = -1;
         return true;
       };
+      // descriptors of stage 0, k-slice 0, advanced by adds to the start-address field (as in the one-CTA kernel)
+      const uint64_t a_desc0 = smem_desc(sbase, 16, 1024, 2);
+      const uint64_t b_desc0 =
+          B_MN ? smem_desc(sbase + PP::OFF_B, 4096, 512, 4) : smem_desc(sbase + PP::OFF_B, 16, 1024, 2);
+      constexpr uint32_t B_KK = B_MN ? 1024 / 16 : 32 / 16;
       for (int u = pair_id; u < total && ok; u += pairs, ++it) {
         const int ab = it & 1;
         const uint32_t aph = (it >> 1) & 1;
@@ -942,17 +949,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             break;
           }
           if (MEEP2B_KSTEP_FENCE) tc_fence_after();
-          const uint32_t a_addr = sbase + stage * A_BYTES;
-          const uint32_t b_addr = sbase + PP::OFF_B + stage * PP::B_BYTES;
+          const uint64_t a_st = a_desc0 + static_cast<uint32_t>(stage) * (A_BYTES / 16);
+          const uint64_t b_st = b_desc0 + static_cast<uint32_t>(stage) * (PP::B_BYTES / 16);
+          mma_bf16_pair(d, a_st, b_st, IDESC_MAIN, kb != 0);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024, 2);
-            if (B_MN) {
-              mma_bf16_pair(d, adesc, smem_desc(b_addr + kk * 1024, 4096, 512, 4), IDESC_MAIN, (kb | kk) != 0);
-            } else {
-              mma_bf16_pair(d, adesc, smem_desc(b_addr + kk * 32, 16, 1024, 2), IDESC_MAIN, (kb | kk) != 0);
-            }
-          }
+          for (int kk = 1; kk < BK / 16; ++kk) mma_bf16_pair(d, a_st + 2 * kk, b_st + B_KK * kk, IDESC_MAIN, 1);
           mma_commit_pair(bar_empty(stage));
           if (++stage == PP::STAGES) {
             stage = 0;
