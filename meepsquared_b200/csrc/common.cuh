@@ -279,6 +279,22 @@ __device__ __forceinline__ void tma_gather4_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// TMA store of a 2-D tile from this CTA's shared memory (bulk-group completion: commit, then wait for the source
+// to be read before it is rewritten, and for the writes before the kernel ends).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed bulk groups of this thread still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------------ tcgen05
 
 // Shared-memory matrix descriptor (sm_100 format: version 1 in bits 46-47).

@@ -38,20 +38,28 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int ACC_STRIDE = 256;
 
 // Shared-memory plan per mode. K-major: the B tile is 208 rows of 128 bytes; MN-major: four 64-column chunks.
-template <bool B_MN>
+// A staging area for the epilogue's TMA traffic: 8 warps x STG_BUFS tiles of 32 x 32 bf16. K-major and MN-major
+// plain products keep 4 stages (4 KB and 2 KB of staging per warp); the MN-major dSwiGLU product keeps 3 (8 KB
+// per warp: two buffers of a gate and an up tile, and their two load barriers per warp).
+template <bool B_MN, int EPI = MEEP2B_EPI_PLAIN>
 struct Plan {
-  static constexpr int STAGES = B_MN ? 4 : 5;  // the most that fit beside the adapter buffers
+  static constexpr bool DS = B_MN && EPI == MEEP2B_EPI_DSWIGLU;
+  static constexpr int STAGES = DS ? 3 : 4;
+  static constexpr int STG_BUFS = DS ? 4 : (B_MN ? 1 : 2);  // per epilogue warp
   static constexpr int B_BYTES = B_MN ? 4 * 64 * BK * 2 : (BN + RP) * BK * 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_U = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_LOW = OFF_U + U_BYTES;
-  static constexpr int OFF_BAR = OFF_LOW + LOW_BYTES;
-  static constexpr int NUM_BARS = 2 * STAGES + 10;
+  static constexpr int OFF_STG = OFF_LOW + LOW_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + 8 * STG_BUFS * 2048;
+  static constexpr int NUM_BARS = 2 * STAGES + 10 + (DS ? 16 : 0);  // + the staged loads' barriers
+  static constexpr int LD_BAR0 = 2 * STAGES + 10;                    // index of the first of those
   static constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + slack to align the base to 1024
   static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
-  static_assert(B_BYTES % 1024 == 0 && OFF_U % 1024 == 0 && OFF_LOW % 1024 == 0, "swizzle atoms need 1 KB alignment");
+  static_assert(B_BYTES % 1024 == 0 && OFF_U % 1024 == 0 && OFF_LOW % 1024 == 0 && OFF_STG % 1024 == 0,
+                "swizzle atoms need 1 KB alignment");
 };
 
 struct Params {
@@ -77,6 +85,7 @@ struct Params {
   int64_t w_ld;
   // PLAIN epilogue: product row i is stored at row out_rows[i] of out (token-major rows for a streaming combine)
   const int64_t* out_rows;
+  bool staged;  // PLAIN epilogue: the out map exists, whole 32 x 32 tiles go out by TMA stores
 };
 
 // silu(g) = g / (1 + exp(-g)) with the fast exponential and division intrinsics; the result is rounded to bf16.
@@ -189,17 +198,147 @@ __device__ __forceinline__ void tmem_wait_regs16(uint32_t* r) {
                : "memory");
 }
 
+// One row of a 32-row x 16-column bf16 staging tile (32-byte rows with the 32-byte swizzle: the two 16-byte chunks
+// of row r swap when bit 2 of r is set), written by the lane that owns the row: conflict-free 16-byte stores.
+__device__ __forceinline__ void stage_row16(uint32_t tile, int lane, const uint32_t (&w)[8]) {
+  const uint32_t r = tile + static_cast<uint32_t>(lane) * 32u;
+  const uint32_t sw = (static_cast<uint32_t>(lane) >> 2) & 1u;
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(r + (sw << 4)), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3])
+               : "memory");
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(r + ((sw ^ 1u) << 4)), "r"(w[4]), "r"(w[5]),
+               "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// A 32-row x 32-column bf16 tile in shared memory with the 64-byte swizzle (64-byte rows, the four 16-byte chunks
+// of row r at chunk ^ ((r >> 1) & 3)): the lane that owns row `lane` reads or writes its 16 words.
+__device__ __forceinline__ void tile32_read(uint32_t tile, int lane, uint32_t (&w)[16]) {
+  const uint32_t r = tile + static_cast<uint32_t>(lane) * 64u;
+  const uint32_t sw = (static_cast<uint32_t>(lane) >> 1) & 3u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[4 * j]), "=r"(w[4 * j + 1]), "=r"(w[4 * j + 2]), "=r"(w[4 * j + 3])
+                 : "r"(r + ((static_cast<uint32_t>(j) ^ sw) << 4))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tile32_write(uint32_t tile, int lane, const uint32_t (&w)[16]) {
+  const uint32_t r = tile + static_cast<uint32_t>(lane) * 64u;
+  const uint32_t sw = (static_cast<uint32_t>(lane) >> 1) & 3u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(r + ((static_cast<uint32_t>(j) ^ sw) << 4)),
+                 "r"(w[4 * j]), "r"(w[4 * j + 1]), "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                 : "memory");
+}
+
+// The dSwiGLU epilogue of one warp (32 rows, all of the expert, and `cols` <= 96 columns from n0) through shared
+// memory: per 32 columns the warp's lane 0 TMA-loads the gate and up pre-activation tiles (32 x 32 each) into one
+// of two buffers (the next chunk's loads in flight while this one is computed), every lane reads its row, writes
+// dgate and dup over the tiles, and lane 0 TMA-stores them. stg: two buffers of 4 KB (gate tile, then up tile);
+// ldbar: their two load barriers (8 bytes apart); phases: the barriers' next parities (bit b for buffer b).
+template <bool PAIR>
+__device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0, int cols, float sc, float rw,
+                                               uint32_t d, int lane, uint32_t stg, uint32_t ldbar, uint32_t& phases,
+                                               const CUtensorMap* tm_aux, const CUtensorMap* tm_out,
+                                               uint32_t bar_tfull_ab, uint32_t aph, uint32_t bar_tempty_ab,
+                                               int64_t orow) {
+  const int chunks = cols > 0 ? (cols + 31) / 32 : 0;
+  if (chunks == 0) {
+    if (!mbar_wait(bar_tfull_ab, aph)) return false;
+    tc_fence_before();
+    arrive_on<PAIR>(bar_tempty_ab);
+    return true;
+  }
+  auto load = [&](int c) {
+    if (lane == 0) {
+      const uint32_t buf = stg + static_cast<uint32_t>(c & 1) * 4096u;
+      bulk_wait_read<0>();  // this buffer's last tiles have been read by their stores
+      const uint32_t bar = ldbar + 8u * static_cast<uint32_t>(c & 1);
+      mbar_arrive_expect_tx(bar, 4096);
+      tma_load_2d(buf, tm_aux, bar, n0 + 32 * c, row0);
+      tma_load_2d(buf + 2048, tm_aux, bar, p.N + n0 + 32 * c, row0);
+    }
+  };
+  load(0);
+  if (!mbar_wait(bar_tfull_ab, aph)) return false;
+  tc_fence_after();
+  float wpart = 0.0f;
+  bool ok = true;
+  for (int c = 0; c < chunks; ++c) {
+    if (c + 1 < chunks) load(c + 1);
+    uint32_t acc[32];
+    tmem_ld16_async(d + 32 * c, acc);
+    tmem_ld16_async(d + 32 * c + 16, acc + 16);
+    tmem_wait_regs16(acc);
+    tmem_wait_regs16(acc + 16);
+    if (c + 1 == chunks) {
+      tc_fence_before();
+      arrive_on<PAIR>(bar_tempty_ab);  // the whole accumulator is in registers or done
+    }
+    const uint32_t b = static_cast<uint32_t>(c & 1);
+    if (!mbar_wait(ldbar + 8u * b, (phases >> b) & 1u)) { ok = false; break; }
+    phases ^= 1u << b;
+    const uint32_t buf = stg + b * 4096u;
+    uint32_t gw[16], uw[16];
+    tile32_read(buf, lane, gw);
+    tile32_read(buf + 2048, lane, uw);
+    const int cnt = min(32, cols - 32 * c);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float dgo[2], duo[2];
+#pragma unroll
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        const float gb = hlf ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
+        const float ub = hlf ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
+        const float dh_u = __uint_as_float(acc[2 * j + hlf]) * sc;
+        const float dh = bf16_round(dh_u * rw);
+        const float act = bf16_round(silu_f(gb));  // the forward's activation, bit for bit
+        const float sig = sigmoid_f(gb);
+        if (p.w_grad != nullptr && 2 * j + hlf < cnt) wpart += dh_u * bf16_round(act * ub);
+        const float dact = bf16_round(dh * ub);
+        duo[hlf] = dh * act;
+        dgo[hlf] = dact * sig * (1.0f + gb * (1.0f - sig));
+      }
+      gw[j] = pack_bf16x2(dgo[0], dgo[1]);
+      uw[j] = pack_bf16x2(duo[0], duo[1]);
+    }
+    tile32_write(buf, lane, gw);
+    tile32_write(buf + 2048, lane, uw);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm_out, buf, n0 + 32 * c, row0);
+      tma_store_2d(tm_out, buf + 2048, p.N + n0 + 32 * c, row0);
+      bulk_commit();
+    }
+  }
+  if (!ok) return false;
+  if (p.w_grad != nullptr && cols > 0) p.w_grad[orow * p.w_ld + n0 / 96] = wpart;
+  return true;
+}
+
 // The epilogue of one work unit for the 128 accumulator rows this CTA holds (TMEM lane quarter q, column half
 // `half`). row_shift: the offset of this CTA's rows within the tile (128 for the second CTA of a pair). All of a
 // thread's accumulator loads for the unit are issued before one wait (the dSwiGLU epilogue, which also reads the
 // pre-activations, pipelines them by two). Returns false when a bounded wait ran out.
 // SPLIT: the accumulator of an MN-major CTA pair, whose columns are [stack 0..95 | panel 0..7 | stack 96..191 |
 // panel 8..15] (each CTA's half of B is 96 stack columns then 8 panel columns); otherwise [stack 0..191 | panel].
+// stg / tm_out (plain epilogue): this warp's staging buffers in shared memory (stg_bufs of 2 KB, 1 KB-aligned) and
+// the tensor map of `out` (boxes of 32 columns x 32 rows, 64-byte swizzle); when given, a warp whose 32 rows are
+// all the expert's stores its columns as 32 x 32 tiles through shared memory with TMA stores (one bulk copy per
+// tile instead of 32 rows of scattered 32-byte stores), and hands the accumulator back as soon as it is in
+// registers. Rows at an expert's end (a warp with rows past it) and out_rows keep the per-row stores.
 template <int EPI, bool LORA, bool PAIR, bool SPLIT = false>
 __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, int row_shift, uint8_t* smem_low,
                                               uint32_t tmem_base, int q, int half, int lane,
                                               uint32_t bar_lowfull_ab, uint32_t bar_lowready,
-                                              uint32_t bar_tfull_ab, uint32_t bar_tempty_ab) {
+                                              uint32_t bar_tfull_ab, uint32_t bar_tempty_ab, uint32_t stg = 0,
+                                              const CUtensorMap* tm_out = nullptr, int stg_bufs = 0,
+                                              const CUtensorMap* tm_aux = nullptr, uint32_t ldbar = 0,
+                                              uint32_t* phases = nullptr) {
   const int r_in = q * 32 + lane;
   const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
   const int t = u / p.nblocks, nb = u - t * p.nblocks;
@@ -273,6 +412,49 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
         tmem_wait_regs16(uu + 16 * c);
       }
     }
+    if (tm_out != nullptr && tm_aux != nullptr && p.staged && __all_sync(0xffffffffu, valid)) {
+      // staged: per 16 columns the gate and up pre-activations and h as three 32 x 16 tiles, TMA-stored
+      tc_fence_before();
+      arrive_on<PAIR>(bar_tempty_ab);
+      const __nv_bfloat16* bias_g = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + n0h : nullptr;
+      const int row0 = p.tile_row[t] + row_shift + q * 32;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const int cnt = min(16, cols - 16 * c);
+        if (cnt <= 0) break;
+        uint32_t gw[8], uw[8], hw[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = 16 * c + 2 * j;
+          float g0 = __uint_as_float(g[k]) * sc * rw, g1 = __uint_as_float(g[k + 1]) * sc * rw;
+          float u0 = __uint_as_float(uu[k]) * sc * rw, u1 = __uint_as_float(uu[k + 1]) * sc * rw;
+          if (bias_g != nullptr && 2 * j + 1 < cnt) {
+            g0 += __bfloat162float(bias_g[k]);
+            g1 += __bfloat162float(bias_g[k + 1]);
+            u0 += __bfloat162float(bias_g[p.inter + k]);
+            u1 += __bfloat162float(bias_g[p.inter + k + 1]);
+          }
+          gw[j] = pack_bf16x2(g0, g1);
+          uw[j] = pack_bf16x2(u0, u1);
+          const float a0 = bf16_round(silu_f(bf16_lo(gw[j]))), a1 = bf16_round(silu_f(bf16_hi(gw[j])));
+          hw[j] = pack_bf16x2(a0 * bf16_lo(uw[j]), a1 * bf16_hi(uw[j]));
+        }
+        if (lane == 0) bulk_wait_read<0>();  // the previous tiles have left the staging buffer
+        __syncwarp();
+        stage_row16(stg, lane, gw);
+        stage_row16(stg + 1024, lane, uw);
+        stage_row16(stg + 2048, lane, hw);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tm_aux, stg, n0h + 16 * c, row0);
+          tma_store_2d(tm_aux, stg + 1024, p.inter + n0h + 16 * c, row0);
+          tma_store_2d(tm_out, stg + 2048, n0h + 16 * c, row0);
+          bulk_commit();
+        }
+      }
+      return true;
+    }
     if (valid && cols > 0) {
       const __nv_bfloat16* bias_g = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + n0h : nullptr;
       __nv_bfloat16* pre = p.aux + orow * p.ld_aux + n0h;
@@ -317,6 +499,51 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
 #pragma unroll
       for (int c = 0; c < 6; ++c) tmem_wait_regs16(v + 16 * c);
     }
+    if (tm_out != nullptr && p.staged && p.out_rows == nullptr && __all_sync(0xffffffffu, valid)) {
+      tc_fence_before();
+      arrive_on<PAIR>(bar_tempty_ab);  // the accumulator is in registers: the MMA may reuse it
+      const __nv_bfloat16* bias = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + n0 : nullptr;
+      const int row0 = p.tile_row[t] + row_shift + q * 32;
+      if (lane == 0) bulk_wait_read<0>();  // the previous unit's tiles have left the staging buffers
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        if (cols - 32 * c <= 0) break;
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int k = 32 * c + 2 * j;
+          float a = __uint_as_float(v[k]) * sc * rw, b = __uint_as_float(v[k + 1]) * sc * rw;
+          if (bias != nullptr && 2 * j + 1 < cols - 32 * c) {
+            a += __bfloat162float(bias[k]);
+            b += __bfloat162float(bias[k + 1]);
+          }
+          w[j] = pack_bf16x2(a, b);
+        }
+        const uint32_t buf = stg + static_cast<uint32_t>(stg_bufs > 1 ? (c & 1) : 0) * 2048u;
+        if (c >= stg_bufs) {  // the buffer's previous tile must have been read by its TMA store
+          if (lane == 0) {
+            if (stg_bufs > 1) bulk_wait_read<1>(); else bulk_wait_read<0>();
+          }
+          __syncwarp();
+        }
+        // row `lane`, 64 bytes, its four 16-byte chunks at chunk ^ ((row >> 1) & 3) (the 64-byte swizzle)
+        const uint32_t rbase = buf + static_cast<uint32_t>(lane) * 64u;
+        const uint32_t sw = (static_cast<uint32_t>(lane) >> 1) & 3u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rbase + ((j ^ sw) << 4)), "r"(w[4 * j]),
+                       "r"(w[4 * j + 1]), "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                       : "memory");
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tm_out, buf, n0 + 32 * c, row0);
+          bulk_commit();
+        }
+      }
+      return true;
+    }
     if (valid && cols > 0) {
       const __nv_bfloat16* bias = p.bias != nullptr ? p.bias + static_cast<int64_t>(e) * p.N + n0 : nullptr;
       const int64_t drow = p.out_rows != nullptr ? p.out_rows[row] : orow;
@@ -345,6 +572,9 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
     constexpr int HS = SPLIT ? 104 : 96;
     const int n0 = nb * BN + half * 96;
     const int cols = min(96, p.N - n0);
+    if (tm_aux != nullptr && tm_out != nullptr && phases != nullptr && p.staged && __all_sync(0xffffffffu, valid))
+      return dswiglu_staged<PAIR>(p, p.tile_row[t] + row_shift + q * 32, n0, cols, sc, rw, d + half * HS, lane, stg,
+                                  ldbar, *phases, tm_aux, tm_out, bar_tfull_ab, aph, bar_tempty_ab, orow);
     const __nv_bfloat16* gp = p.aux + orow * p.ld_aux + n0;
     __nv_bfloat16* outp = p.out + orow * p.ldo + n0;
     uint32_t gw[2][8], uw[2][8], acc[2][16];
@@ -469,8 +699,9 @@ template <bool B_MN, bool LORA, int EPI, bool GATHER = false>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_u,
+                        const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_aux,
                         const Params p) {
-  using P = Plan<B_MN>;
+  using P = Plan<B_MN, EPI>;
   constexpr int STAGES = P::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -503,6 +734,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(bar_ufull, 1);
     mbar_init(bar_uempty, 1);
     mbar_init(bar_drain, 1);
+    if (P::DS)
+      for (int b = 0; b < 16; ++b) mbar_init(bar0 + 8u * (P::LD_BAR0 + b), 1);  // the epilogue's staged loads
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -689,12 +922,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int q = warp & 3;                    // TMEM lane quarter this warp may read
     const int half = (warp - EPI_WARP0) >> 2;  // which half of the unit's columns
     int it = 0;
+    const uint32_t stg = sbase + P::OFF_STG + static_cast<uint32_t>(warp - EPI_WARP0) * P::STG_BUFS * 2048u;
+    const CUtensorMap* out_map = (EPI != MEEP2B_EPI_DSWIGLU || P::DS) ? &tm_out : nullptr;
+    const CUtensorMap* aux_map = (EPI == MEEP2B_EPI_SWIGLU || P::DS) ? &tm_aux : nullptr;
+    const uint32_t ldbar = bar0 + 8u * (P::LD_BAR0 + 2 * (warp - EPI_WARP0));
+    uint32_t phases = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++it) {
       const int ab = it & 1;
       if (!epilogue_unit<EPI, LORA, false>(p, u, it, 0, smem + P::OFF_LOW, tmem_base, q, half, lane, bar_lowfull(ab),
-                                           bar_lowready, bar_tfull(ab), bar_tempty(ab)))
+                                           bar_lowready, bar_tfull(ab), bar_tempty(ab), stg, out_map, P::STG_BUFS,
+                                           aux_map, ldbar, P::DS ? &phases : nullptr))
         break;
     }
+    if (lane == 0) bulk_wait_all();  // this warp's TMA stores are done before the CTA's shared memory goes away
   }
 
   tc_fence_before();
@@ -713,7 +953,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // same per CTA. All loads are plain TMA tile loads into the loading CTA's own shared memory, completing on the
 // leader's barrier; there is no multicast.
 #ifndef MEEP2B_PAIR_STAGES
-#define MEEP2B_PAIR_STAGES 7
+#define MEEP2B_PAIR_STAGES 6
 #endif
 constexpr int PAIR_STAGES = MEEP2B_PAIR_STAGES;
 constexpr int PAIR_B_ROWS = (BN + RP) / 2;  // 104: each CTA's share of the 208 K-major B rows
@@ -724,7 +964,7 @@ constexpr int PAIR_B_ROWS = (BN + RP) / 2;  // 104: each CTA's share of the 208 
 // MMA reads from it (6 stages).
 template <bool B_MN>
 struct PairPlan {
-  static constexpr int STAGES = B_MN ? 6 : PAIR_STAGES;
+  static constexpr int STAGES = B_MN ? 5 : PAIR_STAGES;
   static constexpr int B_BYTES = B_MN ? 4 * 64 * 64 : PAIR_B_ROWS * BK * 2;  // 16 KB : 13 KB
   static constexpr int PANEL_OFF = 3 * 64 * 64;                            // MN-major panel atom
   static constexpr int U_TX = B_MN ? 4 * RP * 64 : (BN / 2) * RP * 2;      // bytes of U each CTA loads
@@ -732,7 +972,9 @@ struct PairPlan {
   static constexpr int OFF_B = STAGES * A_BYTES;
   static constexpr int OFF_U = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_LOW = OFF_U + U_BYTES;
-  static constexpr int OFF_BAR = OFF_LOW + LOW_BYTES;
+  static constexpr int STG_BUFS = 2;  // 4 KB of staging per epilogue warp (two 32 x 32 tiles, or three 32 x 16)
+  static constexpr int OFF_STG = OFF_LOW + LOW_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + 8 * STG_BUFS * 2048;
   static constexpr int NUM_BARS = 2 * STAGES + 10;
   static constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;
@@ -751,6 +993,8 @@ struct PairMaps {
   CUtensorMap w_mn;  // MN-major stack (n, k, E) box 32 x 64, 64-byte swizzle
   CUtensorMap p_mn;  // MN-major panel (E, k, 64) box 32 x 64 from column 8 * rank, 64-byte swizzle
   CUtensorMap u_mn;  // MN-major up factor (n, 16, E) box 32 x 16, 64-byte swizzle
+  CUtensorMap out;   // the epilogue's TMA stores (as the one-CTA kernel's tm_out)
+  CUtensorMap aux;   // SwiGLU pre-activations (as tm_aux)
 };
 
 template <bool B_MN, bool LORA, int EPI, bool GATHER = false>
@@ -981,12 +1225,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int q = warp & 3;
     const int half = (warp - EPI_WARP0) >> 2;
     int it = 0;
+    const uint32_t stg = sbase + PP::OFF_STG + static_cast<uint32_t>(warp - EPI_WARP0) * PP::STG_BUFS * 2048u;
+    const CUtensorMap* out_map = EPI != MEEP2B_EPI_DSWIGLU ? &m.out : nullptr;
+    const CUtensorMap* aux_map = EPI == MEEP2B_EPI_SWIGLU ? &m.aux : nullptr;
     for (int u = pair_id; u < total; u += pairs, ++it) {
       const int ab = it & 1;
-      if (!epilogue_unit<EPI, LORA, true, B_MN && LORA>(p, u, it, 128 * static_cast<int>(rank), smem + PP::OFF_LOW, tmem_base, q,
-                                          half, lane, bar_lowfull(ab), bar_lowready, bar_tfull(ab), bar_tempty(ab)))
+      if (!epilogue_unit<EPI, LORA, true, B_MN && LORA>(p, u, it, 128 * static_cast<int>(rank), smem + PP::OFF_LOW,
+                                                        tmem_base, q, half, lane, bar_lowfull(ab), bar_lowready,
+                                                        bar_tfull(ab), bar_tempty(ab), stg, out_map, PP::STG_BUFS,
+                                                        aux_map))
         break;
     }
+    if (lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1014,17 +1264,17 @@ static int launch_pair(const PairMaps& maps, const Params& prm, int grid, cudaSt
 
 template <bool B_MN, bool LORA, int EPI, bool GATHER = false>
 static int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tu,
-                  const Params& prm, int grid, cudaStream_t s) {
+                  const CUtensorMap& tout, const CUtensorMap& taux, const Params& prm, int grid, cudaStream_t s) {
   auto kern = grouped_gemm_kernel<B_MN, LORA, EPI, GATHER>;
   static bool configured = false;  // per instantiation; attributes are per device but idempotent
   if (!configured) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<B_MN>::SMEM_BYTES) != cudaSuccess) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<B_MN, EPI>::SMEM_BYTES) != cudaSuccess) {
       cudaGetLastError();
       return MEEP2B_ERR_LAUNCH;
     }
     configured = true;
   }
-  kern<<<grid, THREADS, Plan<B_MN>::SMEM_BYTES, s>>>(tx, tw, tp, tu, prm);
+  kern<<<grid, THREADS, Plan<B_MN, EPI>::SMEM_BYTES, s>>>(tx, tw, tp, tu, tout, taux, prm);
   return launch_status();
 }
 
@@ -1067,7 +1317,39 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
 
   const uint64_t K = a->k, N = a->n, E = a->experts, rows = a->rows;
   const uint64_t x_rows_in_map = gather ? static_cast<uint64_t>(a->x_src_rows) : rows;
-  CUtensorMap tx, tw, tp, tu;
+  CUtensorMap tx, tw, tp, tu, tout, taux;
+  // The epilogue's TMA stores (bf16 stacks): the plain epilogue's out map in 32 x 32 boxes (64-byte swizzle); the
+  // SwiGLU epilogue's h (out) and pre-activation (aux) maps in 16-column x 32-row boxes (32-byte swizzle), when the
+  // gate and up halves are whole 16-column tiles.
+  bool staged = false;
+  if (epi == MEEP2B_EPI_PLAIN && !quantised && a->out_rows == nullptr && a->n >= 32 && a->rows >= 32) {
+    const uint64_t od[2] = {static_cast<uint64_t>(a->n), static_cast<uint64_t>(a->rows)};
+    const uint64_t os[1] = {static_cast<uint64_t>(a->ldo) * 2};
+    const uint32_t ob[2] = {32, 32};
+    staged = encode_tiled(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->out, od, os, ob,
+                          CU_TENSOR_MAP_SWIZZLE_64B) == MEEP2B_OK;
+  } else if (epi == MEEP2B_EPI_DSWIGLU && !quantised && a->b_mn && a->block_m != 256 && a->n % 32 == 0 &&
+             a->rows >= 32) {
+    // the dSwiGLU epilogue's pre-activation loads and gradient stores: (rows, 2n) maps in 32 x 32 boxes
+    const uint64_t od[2] = {static_cast<uint64_t>(2 * a->n), static_cast<uint64_t>(a->rows)};
+    const uint64_t os[1] = {static_cast<uint64_t>(a->ldo) * 2};
+    const uint64_t as[1] = {static_cast<uint64_t>(2 * a->n) * 2};
+    const uint32_t bx[2] = {32, 32};
+    staged = encode_tiled(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->out, od, os, bx,
+                          CU_TENSOR_MAP_SWIZZLE_64B) == MEEP2B_OK &&
+             encode_tiled(&taux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->aux, od, as, bx,
+                          CU_TENSOR_MAP_SWIZZLE_64B) == MEEP2B_OK;
+  } else if (epi == MEEP2B_EPI_SWIGLU && !quantised && (a->n / 2) % 16 == 0 && a->rows >= 32) {
+    const uint64_t od[2] = {static_cast<uint64_t>(a->n / 2), static_cast<uint64_t>(a->rows)};
+    const uint64_t os[1] = {static_cast<uint64_t>(a->ldo) * 2};
+    const uint64_t ad[2] = {static_cast<uint64_t>(a->n), static_cast<uint64_t>(a->rows)};
+    const uint64_t as[1] = {static_cast<uint64_t>(a->n) * 2};
+    const uint32_t bx[2] = {16, 32};
+    staged = encode_tiled(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->out, od, os, bx,
+                          CU_TENSOR_MAP_SWIZZLE_32B) == MEEP2B_OK &&
+             encode_tiled(&taux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->aux, ad, as, bx,
+                          CU_TENSOR_MAP_SWIZZLE_32B) == MEEP2B_OK;
+  }
   {
     const uint64_t dims[2] = {K, x_rows_in_map};
     const uint64_t strides[1] = {static_cast<uint64_t>(a->ldx) * 2};
@@ -1145,6 +1427,9 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   prm.w_grad = a->w_grad;
   prm.w_ld = a->w_ld;
   prm.out_rows = a->out_rows;
+  prm.staged = staged;
+  if (!staged) tout = tx;  // not read
+  if (!staged || epi == MEEP2B_EPI_PLAIN) taux = tx;
   prm.v8 = aligned32(a->out) && (a->aux == nullptr || aligned32(a->aux)) && (a->low == nullptr || aligned32(a->low)) &&
            a->ldo % 16 == 0 && prm.ld_aux % 16 == 0;
 
@@ -1161,6 +1446,8 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
     PairMaps maps;
     maps.x = tx;
     maps.w104 = maps.w96 = maps.w88 = maps.w8 = maps.p16 = maps.u96 = maps.w_mn = maps.p_mn = maps.u_mn = tx;
+    maps.out = tout;
+    maps.aux = taux;
     if (!a->b_mn) {
       const uint32_t heights[4] = {104, 96, 88, 8};
       CUtensorMap* targets[4] = {&maps.w104, &maps.w96, &maps.w88, &maps.w8};
@@ -1227,19 +1514,19 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
   const bool mn = a->b_mn != 0;
   if (gather) {
     if (epi == MEEP2B_EPI_SWIGLU)
-      return lora ? launch<false, true, 1, true>(tx, tw, tp, tu, prm, grid, s)
-                  : launch<false, false, 1, true>(tx, tw, tp, tu, prm, grid, s);
-    return lora ? launch<true, true, 2, true>(tx, tw, tp, tu, prm, grid, s)
-                : launch<true, false, 2, true>(tx, tw, tp, tu, prm, grid, s);
+      return lora ? launch<false, true, 1, true>(tx, tw, tp, tu, tout, taux, prm, grid, s)
+                  : launch<false, false, 1, true>(tx, tw, tp, tu, tout, taux, prm, grid, s);
+    return lora ? launch<true, true, 2, true>(tx, tw, tp, tu, tout, taux, prm, grid, s)
+                : launch<true, false, 2, true>(tx, tw, tp, tu, tout, taux, prm, grid, s);
   }
   switch (epi) {
     case MEEP2B_EPI_PLAIN:
-      if (mn) return lora ? launch<true, true, 0>(tx, tw, tp, tu, prm, grid, s) : launch<true, false, 0>(tx, tw, tp, tu, prm, grid, s);
-      return lora ? launch<false, true, 0>(tx, tw, tp, tu, prm, grid, s) : launch<false, false, 0>(tx, tw, tp, tu, prm, grid, s);
+      if (mn) return lora ? launch<true, true, 0>(tx, tw, tp, tu, tout, taux, prm, grid, s) : launch<true, false, 0>(tx, tw, tp, tu, tout, taux, prm, grid, s);
+      return lora ? launch<false, true, 0>(tx, tw, tp, tu, tout, taux, prm, grid, s) : launch<false, false, 0>(tx, tw, tp, tu, tout, taux, prm, grid, s);
     case MEEP2B_EPI_SWIGLU:
-      return lora ? launch<false, true, 1>(tx, tw, tp, tu, prm, grid, s) : launch<false, false, 1>(tx, tw, tp, tu, prm, grid, s);
+      return lora ? launch<false, true, 1>(tx, tw, tp, tu, tout, taux, prm, grid, s) : launch<false, false, 1>(tx, tw, tp, tu, tout, taux, prm, grid, s);
     default:
-      if (mn) return lora ? launch<true, true, 2>(tx, tw, tp, tu, prm, grid, s) : launch<true, false, 2>(tx, tw, tp, tu, prm, grid, s);
-      return lora ? launch<false, true, 2>(tx, tw, tp, tu, prm, grid, s) : launch<false, false, 2>(tx, tw, tp, tu, prm, grid, s);
+      if (mn) return lora ? launch<true, true, 2>(tx, tw, tp, tu, tout, taux, prm, grid, s) : launch<true, false, 2>(tx, tw, tp, tu, tout, taux, prm, grid, s);
+      return lora ? launch<false, true, 2>(tx, tw, tp, tu, tout, taux, prm, grid, s) : launch<false, false, 2>(tx, tw, tp, tu, tout, taux, prm, grid, s);
   }
 }
