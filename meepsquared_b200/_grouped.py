@@ -103,22 +103,19 @@ class TileMaps:
 
 
 def _pair_tiles(b_mn: int, rows: int, experts: int, k: int, adapters: bool, quant_kind=None) -> bool:
-    """Whether a product runs on CTA pairs (tiles of 256 rows): enough rows per expert on average that the wider
-    tiles waste little, and a long enough contraction (k >= 1024) that the pair's cross-CTA hand-offs at the end
-    of each tile stay hidden. A stack read MN-major (the input gradient) goes to pairs only without adapters: its
-    rank panel arrives as a separate 32-column atom of which the MMA uses 8, and on B200 the one-CTA kernel is
-    measured faster for it. A quantised stack (quant_kind, dequantised in shared memory) goes to pairs when it is
-    NF4, at any k: each SM then converts half of the stack tile, which is what bounds the NF4 products (measured
-    ~1.5x the one-CTA rate at config-2 size); e4m3 stacks stay on one CTA (the two forms measured alike). MN-major
-    quantised products have no pair form. MEEP2B_PAIR=0 or 1 overrides."""
+    """Whether a product runs on CTA pairs (tiles of 256 rows). A bf16 stack runs on one CTA: with the epilogue's
+    tiles going out by TMA stores from shared memory, the one-CTA kernel (4 stages, tiles of 128 rows, about half
+    the padding rows at an expert's end) measures faster than the pair (6 stages) on every product of the
+    BASELINE shapes (config-2 gate/up forward 817 against 860-873 us). A quantised stack (quant_kind, dequantised
+    in shared memory) goes to pairs when it is NF4: each SM then converts half of the stack tile, which is what
+    bounds the NF4 products (measured ~1.5x the one-CTA rate at config-2 size); e4m3 stacks stay on one CTA (the
+    two forms measured alike). MN-major quantised products have no pair form. MEEP2B_PAIR=0 or 1 overrides."""
     forced = os.environ.get("MEEP2B_PAIR")
     if forced in ("0", "1"):
         return forced == "1"
     if quant_kind is not None:
         return quant_kind == _lib.NF4 and b_mn == 0 and rows >= 384 * experts
-    if b_mn != 0 and adapters:
-        return False
-    return rows >= 384 * experts and k >= 1024
+    return False
 
 
 # ------------------------------------------------------------------------------------------------ layouts

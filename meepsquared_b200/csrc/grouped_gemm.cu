@@ -423,11 +423,13 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
         const int cnt = min(16, cols - 16 * c);
         if (cnt <= 0) break;
         uint32_t gw[8], uw[8], hw[8];
+        const bool unit_scale = sc == 1.0f && rw == 1.0f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int k = 16 * c + 2 * j;
-          float g0 = __uint_as_float(g[k]) * sc * rw, g1 = __uint_as_float(g[k + 1]) * sc * rw;
-          float u0 = __uint_as_float(uu[k]) * sc * rw, u1 = __uint_as_float(uu[k + 1]) * sc * rw;
+          float g0 = __uint_as_float(g[k]), g1 = __uint_as_float(g[k + 1]);
+          float u0 = __uint_as_float(uu[k]), u1 = __uint_as_float(uu[k + 1]);
+          if (!unit_scale) g0 = g0 * sc * rw, g1 = g1 * sc * rw, u0 = u0 * sc * rw, u1 = u1 * sc * rw;
           if (bias_g != nullptr && 2 * j + 1 < cnt) {
             g0 += __bfloat162float(bias_g[k]);
             g1 += __bfloat162float(bias_g[k + 1]);
@@ -436,8 +438,8 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
           }
           gw[j] = pack_bf16x2(g0, g1);
           uw[j] = pack_bf16x2(u0, u1);
-          const float a0 = bf16_round(silu_f(bf16_lo(gw[j]))), a1 = bf16_round(silu_f(bf16_hi(gw[j])));
-          hw[j] = pack_bf16x2(a0 * bf16_lo(uw[j]), a1 * bf16_hi(uw[j]));
+          const uint32_t act = pack_bf16x2(silu_f(bf16_lo(gw[j])), silu_f(bf16_hi(gw[j])));  // bf16(silu(gate))
+          hw[j] = pack_bf16x2(bf16_lo(act) * bf16_lo(uw[j]), bf16_hi(act) * bf16_hi(uw[j]));
         }
         if (lane == 0) bulk_wait_read<0>();  // the previous tiles have left the staging buffer
         __syncwarp();
@@ -510,10 +512,12 @@ __device__ __forceinline__ bool epilogue_unit(const Params& p, int u, int it, in
       for (int c = 0; c < 3; ++c) {
         if (cols - 32 * c <= 0) break;
         uint32_t w[16];
+        const bool unit_scale = sc == 1.0f && rw == 1.0f;  // bf16 stacks without routing weights: no multiply
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int k = 32 * c + 2 * j;
-          float a = __uint_as_float(v[k]) * sc * rw, b = __uint_as_float(v[k + 1]) * sc * rw;
+          float a = __uint_as_float(v[k]), b = __uint_as_float(v[k + 1]);
+          if (!unit_scale) a = a * sc * rw, b = b * sc * rw;
           if (bias != nullptr && 2 * j + 1 < cols - 32 * c) {
             a += __bfloat162float(bias[k]);
             b += __bfloat162float(bias[k + 1]);

@@ -26,23 +26,23 @@ def test_quantised_stacks_are_fused_only_with_whole_64_blocks():
 
 
 def test_the_tile_kernel_choice(monkeypatch):
-    """CTA pairs for long K-major bf16 products with many rows per expert, for MN-major ones only without
-    adapters; for quantised stacks only NF4 K-major (at any k); MEEP2B_PAIR overrides."""
+    """bf16 stacks on one CTA (TMA-store epilogues, 4 stages); CTA pairs for quantised stacks only NF4 K-major (at
+    any k); MEEP2B_PAIR overrides."""
     monkeypatch.delenv("MEEP2B_PAIR", raising=False)
     rows, experts = 131072, 128  # 1024 rows per expert
-    assert _grouped._pair_tiles(0, rows, experts, 2048, True)
-    assert not _grouped._pair_tiles(0, rows, experts, 768, True)  # short contraction
-    assert not _grouped._pair_tiles(0, 16384, experts, 2048, True)  # 128 rows per expert
+    assert not _grouped._pair_tiles(0, rows, experts, 2048, True)
+    assert not _grouped._pair_tiles(0, rows, experts, 768, True)
     assert not _grouped._pair_tiles(1, rows, experts, 2048, True)
-    assert _grouped._pair_tiles(1, rows, experts, 2048, False)
+    assert not _grouped._pair_tiles(1, rows, experts, 2048, False)
     assert _grouped._pair_tiles(0, rows, experts, 768, True, _lib.NF4)
     assert not _grouped._pair_tiles(1, rows, experts, 2048, False, _lib.NF4)
     assert not _grouped._pair_tiles(0, rows, experts, 2048, True, _lib.E4M3_BLOCKS)
     assert not _grouped._pair_tiles(0, rows, experts, 2048, True, _lib.E4M3)
     monkeypatch.setenv("MEEP2B_PAIR", "1")
     assert _grouped._pair_tiles(0, 16384, experts, 768, True, _lib.E4M3)
+    assert _grouped._pair_tiles(0, rows, experts, 2048, True)
     monkeypatch.setenv("MEEP2B_PAIR", "0")
-    assert not _grouped._pair_tiles(0, rows, experts, 2048, True)
+    assert not _grouped._pair_tiles(0, rows, experts, 768, True, _lib.NF4)
 
 
 def test_only_the_default_silu_gate_on_a_k_major_stack_is_fused():
