@@ -180,6 +180,14 @@ class _Stacks:
     scaling2: float
 
 
+def _token_major_rows() -> bool:
+    """MEEP2B_COMBINE=token: the down product (and the gate/up input gradient) store their rows token-major through
+    the permutation for the streaming combine; the rows then go out by per-row stores. Default (sorted): rows in
+    expert order, written as whole tiles by the epilogue's TMA stores, then the un-permute (measured faster on B200:
+    the TMA-store epilogue gains more than the contiguous combine reads)."""
+    return os.environ.get("MEEP2B_COMBINE", "sorted") == "token"
+
+
 def routed_rows(routing: Routing, top_k_weights):
     """(token of each routed row (S,) int32, routing weight of each routed row (S,) float32): what the fused
     products read instead of gathered copies of the rows."""
@@ -252,12 +260,18 @@ class _RoutedExperts(torch.autograd.Function):
             y, low2 = _grouped._launch(h, _stack(st.down), st.down_scale, routing.offsets, not t, ad2, st.scaling2,
                                        st.down_bias, True, tiles=tiles)
             out = unpermute(y, routing, weights_g)
-        else:
+        elif _token_major_rows():
             # the combine of _moe.py:123-126 fused into the down product: its epilogue stores each row at the row's
             # flat assignment (token-major), and the weighted sum over a token's k rows reads one contiguous run
             y, low2 = _grouped._launch(h, _stack(st.down), st.down_scale, routing.offsets, not t, ad2, st.scaling2,
                                        st.down_bias, True, tiles=tiles, out_rows=routing.perm)
             out = combine(y, routing, top_k_weights)
+            del y
+        else:
+            # rows in expert order (the epilogue's tiles go out whole by TMA stores), then the weighted un-permute
+            y, low2 = _grouped._launch(h, _stack(st.down), st.down_scale, routing.offsets, not t, ad2, st.scaling2,
+                                       st.down_bias, True, tiles=tiles)
+            out = unpermute(y, routing, w32)
             del y
         kept = (x, gu, h, y) if mode == "copy" else (hidden, gu, h, token_rows, w32)
         ctx.save_for_backward(*kept, *(v for v in (low1, low2) if v is not None))
@@ -319,7 +333,8 @@ class _RoutedExperts(torch.autograd.Function):
             grads[2], grads[3] = _adapter_grads(ad2, ctx.leaves[2], ctx.leaves[3], first, second, routing.offsets,
                                                 st.scaling2)
         gate_up_stack = _stack(st.gate_up)
-        token_major = not isinstance(gate_up_stack, _grouped.QuantStack)  # quantised products store rows in order
+        # quantised products store rows in order
+        token_major = _token_major_rows() and not isinstance(gate_up_stack, _grouped.QuantStack)
         dsel, low1b = _grouped._launch(dgu, gate_up_stack, st.gate_up_scale, routing.offsets, t, ad1, st.scaling1,
                                        None, True, backward=True, tiles=tiles,
                                        out_rows=routing.perm if token_major else None)

@@ -8,7 +8,8 @@
 // ring of 64-row chunks; nothing waits on a plain load inside the loop (the gathered form's row indices are read a
 // chunk ahead, the row weights come in by cp.async with the panel and are applied in shared memory).
 //
-// Grid: (ceil(n / 128), experts); 8 warps, warp w owns columns [16 w, 16 w + 16) of the CTA's 128.
+// Grid: (ceil(n / COLS), experts); COLS / 16 warps, warp w owns columns [16 w, 16 w + 16) of the CTA's COLS
+// (128: 8 warps; the kernel also builds for 64).
 // The gathered form reads row i of g as g[g_rows[i]] (the routed rows straight from the token-major tensor, no
 // expert-sorted copy) and weights it by row_scale[i]; the weight is applied to the rank panel's row
 // (bf16(row_scale * low), 16 values) rather than to the n values of g.
@@ -18,11 +19,8 @@
 namespace meep2b {
 namespace reduce {
 
-constexpr int COLS = 128;
 constexpr int ROWS = 64;
-constexpr int G_PITCH = COLS + 8;   // bf16 elements per smem row of g: 272 bytes, no ldmatrix bank conflicts
 constexpr int L_PITCH = 16 + 8;     // of low: 48 bytes
-constexpr int THREADS = 256;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
   const uint32_t d = smem_u32(dst);
@@ -53,13 +51,18 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool pred)
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
 }
 
-__global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bfloat16* __restrict__ g, int64_t n,
+template <int COLS>
+__global__ void __launch_bounds__(COLS * 2) grouped_reduce_kernel(const __nv_bfloat16* __restrict__ g, int64_t n,
                                                                  int64_t ldg, const __nv_bfloat16* __restrict__ low,
                                                                  const int32_t* __restrict__ offsets, float scaling,
                                                                  __nv_bfloat16* __restrict__ out,
                                                                  const int32_t* __restrict__ g_rows,
                                                                  const float* __restrict__ row_scale,
                                                                  int out_layout) {
+  constexpr int THREADS = COLS * 2;
+  constexpr int G_PITCH = COLS + 8;  // bf16 elements per smem row of g (+16 bytes: no ldmatrix bank conflicts)
+  constexpr int PIECES_PER_ROW = COLS / 8;
+  constexpr int ROWS_PER_PASS = THREADS / PIECES_PER_ROW;  // 16
   __shared__ __align__(16) __nv_bfloat16 gs[2][ROWS][G_PITCH];
   __shared__ __align__(16) __nv_bfloat16 ls[2][ROWS][L_PITCH];
   __shared__ float ws[2][ROWS];
@@ -74,34 +77,38 @@ __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bflo
 
   // This thread's four g pieces of a chunk are rows piece_row + 16 i (i < 4) at column piece_col. The source rows of
   // gathered g are read one chunk ahead of their copies, so that no copy waits for its index.
-  const int piece_row = threadIdx.x >> 4, piece_col = (threadIdx.x & 15) * 8;
+  const int piece_row = threadIdx.x / PIECES_PER_ROW, piece_col = (threadIdx.x % PIECES_PER_ROW) * 8;
+  static_assert(ROWS_PER_PASS * 4 == ROWS, "four passes of 16-byte pieces cover a chunk");
   auto sources = [&](int chunk, int64_t (&src)[4]) {
     const int64_t r0 = start + static_cast<int64_t>(chunk) * ROWS;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int64_t row = r0 + piece_row + 16 * i;
+      const int64_t row = r0 + piece_row + ROWS_PER_PASS * i;
       src[i] = row < end ? (g_rows != nullptr ? static_cast<int64_t>(__ldg(g_rows + row)) : row) : -1;
     }
   };
   auto load = [&](int chunk, int buf, const int64_t (&src)[4]) {
     const int64_t r0 = start + static_cast<int64_t>(chunk) * ROWS;
-    // g: 64 rows x 128 columns = 1024 16-byte pieces, 4 per thread
+    // g: 64 rows x COLS columns of 16-byte pieces, 4 per thread
     const int64_t col = c0 + piece_col;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const bool ok = src[i] >= 0 && col < n;
-      cp_async16(&gs[buf][piece_row + 16 * i][piece_col], ok ? g + src[i] * ldg + col : g, ok);
+      cp_async16(&gs[buf][piece_row + ROWS_PER_PASS * i][piece_col], ok ? g + src[i] * ldg + col : g, ok);
     }
     // low: 64 rows x 16 = 128 pieces; the rows' weights (row-scaled form), one float each
-    if (threadIdx.x < 128) {
-      const int r = threadIdx.x >> 1, c = (threadIdx.x & 1) * 8;
+    for (int i = threadIdx.x; i < 128; i += THREADS) {
+      const int r = i >> 1, c = (i & 1) * 8;
       const int64_t row = r0 + r;
       const bool ok = row < end;
       cp_async16(&ls[buf][r][c], ok ? low + row * 16 + c : low, ok);
-    } else if (row_scale != nullptr && threadIdx.x < 128 + ROWS) {
-      const int r = threadIdx.x - 128;
-      const int64_t row = r0 + r;
-      cp_async4(&ws[buf][r], row < end ? row_scale + row : row_scale, row < end);
+    }
+    if (row_scale != nullptr) {
+      const int r = THREADS >= 128 + ROWS ? static_cast<int>(threadIdx.x) - 128 : static_cast<int>(threadIdx.x);
+      if (r >= 0 && r < ROWS) {
+        const int64_t row = r0 + r;
+        cp_async4(&ws[buf][r], row < end ? row_scale + row : row_scale, row < end);
+      }
     }
     cp_async_commit();
   };
@@ -123,13 +130,15 @@ __global__ void __launch_bounds__(THREADS) grouped_reduce_kernel(const __nv_bflo
       cp_async_wait<0>();
     }
     __syncthreads();
-    if (row_scale != nullptr) {  // bf16(w * low) in place: 1024 values, 4 per thread
-      const int r = threadIdx.x >> 2, c = (threadIdx.x & 3) * 4;
-      const float w = ws[buf][r];
-      uint2* p2 = reinterpret_cast<uint2*>(&ls[buf][r][c]);
-      const uint2 v = *p2;
-      *p2 = make_uint2(pack_bf16x2(bf16_lo(v.x) * w, bf16_hi(v.x) * w),
-                       pack_bf16x2(bf16_lo(v.y) * w, bf16_hi(v.y) * w));
+    if (row_scale != nullptr) {  // bf16(w * low) in place: 1024 values, 4 at a time
+      for (int i = threadIdx.x; i < ROWS * 4; i += THREADS) {
+        const int r = i >> 2, c = (i & 3) * 4;
+        const float w = ws[buf][r];
+        uint2* p2 = reinterpret_cast<uint2*>(&ls[buf][r][c]);
+        const uint2 v = *p2;
+        *p2 = make_uint2(pack_bf16x2(bf16_lo(v.x) * w, bf16_hi(v.x) * w),
+                         pack_bf16x2(bf16_lo(v.y) * w, bf16_hi(v.y) * w));
+      }
       __syncthreads();
     }
 #pragma unroll
@@ -189,8 +198,9 @@ static int grouped_reduce_launch(const void* g, const int32_t* g_rows, const flo
   if (!aligned16(g) || !aligned16(low) || !aligned16(out)) return MEEP2B_ERR_ALIGN;
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
-  dim3 grid(static_cast<unsigned>((n + reduce::COLS - 1) / reduce::COLS), static_cast<unsigned>(experts));
-  reduce::grouped_reduce_kernel<<<grid, reduce::THREADS, 0, s>>>(
+  constexpr int C = 128;  // measured: the 64-column form (twice the CTAs, half the work each) is not faster
+  dim3 grid(static_cast<unsigned>((n + C - 1) / C), static_cast<unsigned>(experts));
+  reduce::grouped_reduce_kernel<C><<<grid, 2 * C, 0, s>>>(
       static_cast<const __nv_bfloat16*>(g), n, ldg, static_cast<const __nv_bfloat16*>(low), offsets, scaling,
       static_cast<__nv_bfloat16*>(out), g_rows, row_scale, out_layout);
   return launch_status();

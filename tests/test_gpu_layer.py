@@ -230,6 +230,19 @@ def test_adapter_gradients_are_written_into_a_gradient_bucket_with_the_same_bits
         assert torch.equal(hidden.grad, plain["grad_hidden"])
 
 
+def test_the_token_major_combine_gives_the_bits_of_the_sorted_rows(monkeypatch):
+    """MEEP2B_COMBINE=token (the down product and the gate/up input gradient store their rows token-major through
+    the permutation, a streaming combine sums them) against the default (rows in expert order, the un-permute):
+    the same bits for the output and every gradient (float32 routing weights)."""
+    inp = layer_inputs.layer(**dict(layer_inputs.QWEN3_30B, tokens=512, experts=32))
+    monkeypatch.setenv("MEEP2B_COMBINE", "sorted")
+    sorted_rows, _ = run_layer(inp, sentinel=True)
+    monkeypatch.setenv("MEEP2B_COMBINE", "token")
+    token_rows, _ = run_layer(inp, sentinel=True)
+    for name, value in sorted_rows.items():
+        assert torch.equal(value, token_rows[name]), name
+
+
 def test_full_size_layer_step_is_finite_and_deterministic():
     """BASELINE config 2 at full size (T=16384, E=128, top-8): two runs give identical bits, all finite."""
     inp = cached_inputs("qwen3_30b_full", layer_inputs.QWEN3_30B)
