@@ -41,6 +41,10 @@ CONFIGS = {
                       quant="fp8_block128"),
     "small_nf4": dict(tokens=2048, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32, quant="nf4"),
     "half": dict(tokens=8192, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32),
+    # a whole Qwen3-30B-A3B-shaped model (its decoder layers at the real sizes, fewer of them, a smaller vocabulary):
+    # the model-level step with the routed layer installed on every experts module (meepsquared_b200.model)
+    "qwen3_30b_model": dict(tokens=16384, hidden=2048, inter=768, experts=128, top_k=8, rank=16, alpha=32,
+                            model=True, layers=4, seq=4096, vocab=16384, heads=32, kv_heads=4, head_dim=128),
 }
 METRIC = "MoE-LoRA layer fwd+bwd tokens/s"
 # DRAM bytes (read + write) per grouped-product launch at config 2, averaged over the step's four launches: from an
@@ -644,6 +648,105 @@ def run_reference(a):
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
 
+def run_model(a):
+    """--config qwen3_30b_model: a training step of a whole Qwen3-MoE model (random weights of the configured
+    sizes, Transformers' Qwen3MoeForCausalLM) with LoRA on every expert stack: forward, the language-model loss on
+    the batch itself, backward, AdamW on the adapters. The experts run the routed layer (meepsquared_b200.model);
+    the same model with its experts on the reference's PyTorch path (reference_routed_forward) is the GPU baseline."""
+    import types
+
+    import torch
+    from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
+
+    import meepsquared_b200 as mb
+    from meepsquared_b200 import _grouped
+
+    c = CONFIGS[a.config]
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    cfg = Qwen3MoeConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=4 * c["hidden"],
+                         moe_intermediate_size=c["inter"], num_hidden_layers=c["layers"],
+                         num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"],
+                         num_experts=c["experts"], num_experts_per_tok=c["top_k"], decoder_sparse_step=1,
+                         mlp_only_layers=[], norm_topk_prob=True, max_position_embeddings=c["seq"])
+    torch.manual_seed(1234)
+    with torch.device(device):
+        model = Qwen3MoeForCausalLM(cfg).to(torch.bfloat16)
+    for p in model.parameters():
+        p.requires_grad_(False)
+    mb.model.install(model, rank=c["rank"], alpha=c["alpha"], generator=torch.Generator().manual_seed(0))
+    params = mb.model.lora_parameters(model)
+    opt = torch.optim.AdamW(params, lr=1e-4)
+    batch = c["tokens"] // c["seq"]
+    ids = torch.randint(0, c["vocab"], (batch, c["seq"]), generator=torch.Generator().manual_seed(1)).to(device)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        out = model(input_ids=ids, labels=ids)
+        out.loss.backward()
+        opt.step()
+        return out.loss
+
+    def timed(n):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(n):
+            step()
+        stop.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(stop) / n
+
+    clocks = ClockSampler(0).__enter__()
+    for _ in range(a.warmup):
+        step()
+    timer = GemmTimer()
+    _grouped.set_launch_observer(timer)
+    timer.active = True
+    clocks.mark_start()
+    launches_before = mb._lib.launch_count()
+    ms = timed(a.steps)
+    timed_launches = mb._lib.launch_count() - launches_before
+    clocks.mark_stop()
+    timer.active = False
+    _grouped.set_launch_observer(None)
+    gemm_ms, gemm_flops, _ = timer.totals()
+    # the same model with its experts on the reference's PyTorch path
+    def reference_forward(self, hidden_states, top_k_index, top_k_weights):
+        factors = {name: (getattr(self, f"lora_{name}_lhs"), getattr(self, f"lora_{name}_rhs"), self.lora_scaling)
+                   for name in self.lora_stacks}
+        return reference_routed_forward(self, hidden_states, top_k_index, top_k_weights, factors)
+
+    saved = {}
+    for name, e in mb.model.experts_modules(model):
+        saved[name] = e.forward
+        e.forward = types.MethodType(reference_forward, e)
+    for _ in range(max(1, a.warmup)):
+        step()
+    base_ms = timed(a.steps)
+    clocks.__exit__()
+    T = c["tokens"]
+    sustained, burst, hbm, peak_source = peaks()
+    clock_summary = clocks.summary()
+    bf16_peak, regime = pick_peak(clock_summary, sustained, burst)
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    print(json.dumps({
+        "metric": "MoE-LoRA model training step tokens/s", "value": round(T / (ms / 1e3), 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random weights and token ids)",
+        "config": {"workload": "qwen3_30b_model: Qwen3-MoE decoder layers at Qwen3-30B-A3B sizes, LoRA on the experts, "
+                               "fwd + loss + bwd + AdamW", **{k: v for k, v in c.items() if k != "model"}},
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm (tcgen05), all product launches of the step",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": bf16_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / bf16_peak, 4) if achieved else None,
+                     "peak_kind": f"bf16 {regime}, {peak_source}", "gemm_ms_per_step": round(gemm_ms / a.steps, 4)},
+        "gpu_launches": timed_launches, "clocks": clock_summary,
+        "gpu_baseline": {"ms_per_step": round(base_ms, 4), "value": round(T / (base_ms / 1e3), 1),
+                         "unit": "tokens/s", "impl": "the same model, experts on the reference's _routed_forward "
+                                                     "non-kernel branch (torch grouped_mm + _grouped_lora)"}}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -656,7 +759,14 @@ def main():
     a = ap.parse_args()
     if a.warmup < 3 and a.impl == "meep2b":
         a.warmup = 3
-    if a.impl == "reference":
+    if CONFIGS[a.config].get("model"):
+        if a.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the model config's reference arm is its "
+                                                                   "gpu_baseline (the same model on the reference's "
+                                                                   "PyTorch path), in the meep2b line"}))
+            return
+        run_model(a)
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_meep2b(a)
