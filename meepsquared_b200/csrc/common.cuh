@@ -287,20 +287,6 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
 }
-// The same store with an L2 evict-first policy: outputs written once and read by a later kernel leave L2 before
-// the operand tiles the running products keep re-reading.
-__device__ __forceinline__ uint64_t l2_evict_first_policy() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-__device__ __forceinline__ void tma_store_2d_evict_first(const CUtensorMap* map, uint32_t src, int32_t c0, int32_t c1,
-                                                         uint64_t pol) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1), "l"(pol)
-               : "memory");
-}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until at most N committed bulk groups of this thread still read their shared-memory source.
 template <int N>
