@@ -29,7 +29,10 @@ def _step(model, ids):
 def test_the_model_step_matches_the_references_path():
     import types
 
-    model = tiny_qwen3_moe().to(DEV, torch.bfloat16)
+    # one decoder layer: its router sees the same hidden states in both runs (with more layers the later routers
+    # see the earlier experts' outputs, which the two paths round differently, and near-tied tokens may switch
+    # experts)
+    model = tiny_qwen3_moe(layers=1).to(DEV, torch.bfloat16)
     mb.model.install(model, rank=16, alpha=32, generator=torch.Generator().manual_seed(1))
     gen = torch.Generator().manual_seed(2)
     for p in mb.model.lora_parameters(model):  # non-zero lhs, so that the adapters change the output
