@@ -156,7 +156,7 @@ int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32
  *   acc += (s low / scale_e) U_e^T   (MMAs of depth 16; the panel as two bf16 planes, hi + lo)
  *   out  = epilogue(scale_e acc + bias_e)
  * Layouts (b_mn == 0, "K-major"): weight (experts, n, k), panel (experts, 16, k), up (experts, n, 16).
- *         (b_mn == 1, "MN-major"): weight (experts, k, n), panel (experts, k, 64) [columns 16..63 zero],
+ *         (b_mn == 1, "MN-major"): weight (experts, k, n), panel (experts, k, 16),
  *                                  up (experts, 16, n).
  * The rank is padded to 16 with zeros (_grouped.py:275-282). x is (rows, k) with row stride ldx; rows of one
  * expert are contiguous, offsets[e] is the end of expert e's rows (int32, inclusive cumsum). tile_expert /

@@ -189,7 +189,7 @@ class _Adapters:
     lhs is (E, out, r) and rhs (E, r, in); for (E, in, out) lhs is (E, in, r) and rhs (E, r, out).
     A product computes rows @ F1 (the rank panel, rows x r) and then panel @ F2, F1 (E, k, r) and F2 (E, r, n).
     The kernel takes F1 as its panel P and F2 as its up factor U: with b_mn=0 P is (E, 16, k) and U (E, n, 16),
-    with b_mn=1 P is (E, k, 64) and U (E, 16, n); the rank is padded with zeros.
+    with b_mn=1 P is (E, k, 16) and U (E, 16, n); the rank is padded with zeros.
     """
 
     def __init__(self, lhs, rhs, is_transposed):
@@ -211,7 +211,7 @@ class _Adapters:
         f1, f2 = self.factors(backward)
         if b_mn == 0:
             return _rank_rows(f1.transpose(1, 2)), _rank_cols(f2.transpose(1, 2), 16)
-        return _rank_cols(f1, 64), _rank_rows(f2)
+        return _rank_cols(f1, RANK_MULTIPLE), _rank_rows(f2)
 
 
 class QuantStack:

@@ -1390,8 +1390,10 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
       MEEP2B_TRY(encode_tiled(&tu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->up, ud, us, ubx,
                               CU_TENSOR_MAP_SWIZZLE_32B));
     } else {
-      const uint64_t pd[3] = {64, K, E};
-      const uint64_t ps[2] = {128, K * 128};
+      // the (E, k, 16) panel read as 64-column boxes: the 48 columns past its width arrive as zeros (the box's
+      // out-of-bounds fill), the panel atom of the MN-major B tile
+      const uint64_t pd[3] = {RP, K, E};
+      const uint64_t ps[2] = {RP * 2, K * RP * 2};
       const uint32_t pb[3] = {64, 64, 1};
       MEEP2B_TRY(encode_tiled(&tp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->panel, pd, ps, pb,
                               CU_TENSOR_MAP_SWIZZLE_128B));
@@ -1478,8 +1480,8 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
       MEEP2B_TRY(encode_tiled(&maps.w_mn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->weight, wd, ws, wb,
                               CU_TENSOR_MAP_SWIZZLE_64B));
       if (lora) {
-        const uint64_t pd[3] = {64, K, E};  // the (E, k, 64) panel, 32 columns from column 8 * rank
-        const uint64_t ps[2] = {128, K * 128};
+        const uint64_t pd[3] = {RP, K, E};  // the (E, k, 16) panel, 32 columns from column 8 * rank (zeros past 16)
+        const uint64_t ps[2] = {RP * 2, K * RP * 2};
         const uint32_t pb[3] = {32, 64, 1};
         MEEP2B_TRY(encode_tiled(&maps.p_mn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->panel, pd, ps, pb,
                                 CU_TENSOR_MAP_SWIZZLE_64B));
