@@ -48,9 +48,8 @@ CONFIGS = {
 }
 METRIC = "MoE-LoRA layer fwd+bwd tokens/s"
 # DRAM bytes (read + write) per grouped-product launch at config 2, averaged over the step's four launches: from an
-# ncu capture of the same launches at half the tokens (the profile summary of the grouped products), the weight
-# bytes kept and the activation bytes doubled to the full workload.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = 1.67e9
+# ncu capture of the four products at the full config-2 size (dram__bytes_read.sum + dram__bytes_write.sum).
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 1.643e9
 
 
 def flop_per_token(c):
@@ -404,7 +403,7 @@ def run_meep2b(a):
                                            if achieved else None),
                      "launches_timed": gemm_launches, "gemm_ms_per_step": round(gemm_ms / a.steps, 4),
                      "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH if a.config == "qwen3_30b" else None,
-                     "traffic_unit": "DRAM bytes per launch (ncu capture at half the tokens, scaled)",
+                     "traffic_unit": "DRAM bytes per launch (ncu capture of the four products at full size)",
                      "layer": {"achieved": round(layer_tflops, 1), "peak": bf16_peak,
                                "frac": round(layer_tflops / bf16_peak, 4),
                                "flop_per_token": flop_per_token(c),
