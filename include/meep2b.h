@@ -298,6 +298,22 @@ int meep2b_grouped_reduce_rows(const void* g, const int32_t* g_rows, const float
                                int64_t n, int64_t ldg, const void* low, const int32_t* offsets, int32_t experts,
                                float scaling, void* out, int32_t out_layout, void* stream);
 
+/* The gathered reduction of meep2b_grouped_reduce_rows (same result up to the order of float32 additions; bitwise
+ * deterministic from call to call) for n = 768, 1536 or 2048 (MEEP2B_ERR_UNSUPPORTED otherwise): each CTA reads
+ * whole rows, one bulk copy per row, over a chunk of up to meep2b_reduce_chunk_rows() rows of one expert, and
+ * writes the chunk's float32 sums to `partial`; a second kernel adds each expert's chunks in order. The chunk map
+ * (chunk_expert, chunk_row, chunks: device int32, max_chunks entries) is meep2b_tile_map's output for a tile height
+ * of meep2b_reduce_chunk_rows(). partial: device float32 scratch of max_chunks x n x 16 entries (partial_bytes its
+ * size; MEEP2B_ERR_SHAPE when smaller). */
+int meep2b_grouped_reduce_rows_full(const void* g, const int32_t* g_rows, const float* row_scale, int64_t rows,
+                                    int64_t n, int64_t ldg, const void* low, const int32_t* offsets, int32_t experts,
+                                    float scaling, void* out, int32_t out_layout, const int32_t* chunk_expert,
+                                    const int32_t* chunk_row, const int32_t* chunks, int64_t max_chunks,
+                                    float* partial, size_t partial_bytes, void* stream);
+
+/* Rows per chunk of meep2b_grouped_reduce_rows_full (the tile height of its chunk map). */
+int meep2b_reduce_chunk_rows(void);
+
 /* ---------------------------------------------------------------------------------------------- quantised stacks */
 
 /* _fp8.quantize_stack (_fp8.py:122-128): scale[e] = max(amax_e, 1e-12) / 448, codes = e4m3(w / scale[e]) (round

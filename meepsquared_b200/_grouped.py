@@ -484,13 +484,19 @@ def _product(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, 
                    tiles=tiles)
 
 
+# widths of g whose gathered reductions take the whole-row form (the layer's hidden and upstream-gradient rows at
+# the benchmarked shapes; the kernel is built for these three)
+_FULL_ROW_WIDTHS = (768, 1536, 2048)
+
+
 def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: float, g_rows=None,
-            row_scale=None, out=None, layout=0) -> torch.Tensor:
+            row_scale=None, out=None, layout=0, tiles=None) -> torch.Tensor:
     """scaling * sum over each expert's rows of g^T @ low (_grouped.py:362-370), bf16: (experts, N, 16) with
     layout 0, (experts, 16, N) with layout 1.
 
     g_rows (int32): row i is row g_rows[i] of g (the routed rows read where they are); row_scale (float32): row i
     weighted by row_scale[i]. out: a contiguous bf16 tensor of that shape to write into (a gradient bucket's slot).
+    tiles: the offsets' TileMaps, whose chunk map the whole-row form of a gathered reduction reuses.
     """
     experts = offsets.numel()
     N = g.shape[1]
@@ -509,6 +515,17 @@ def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: 
         _lib.check(lib.meep2b_grouped_reduce(_lib.ptr(g), rows, N, g.stride(0), _lib.ptr(low.contiguous()),
                                              _lib.ptr(offsets), experts, float(scaling), _lib.ptr(out), layout,
                                              _lib.stream_of(g)), "meep2b_grouped_reduce")
+    elif g_rows is not None and N in _FULL_ROW_WIDTHS:
+        # gathered rows arrive whole, one bulk copy each (meep2b_grouped_reduce_rows_full): a CTA per chunk of an
+        # expert's rows, the chunks' float32 sums added in order by a second kernel
+        chunk = int(lib.meep2b_reduce_chunk_rows())
+        cmap = tiles.get(chunk) if tiles is not None else tile_map(offsets, rows, chunk)
+        partial = torch.empty(cmap[0].numel() * N * RANK_MULTIPLE, device=g.device, dtype=torch.float32)
+        _lib.check(lib.meep2b_grouped_reduce_rows_full(
+            _lib.ptr(g), _lib.ptr(g_rows), _lib.ptr(row_scale), rows, N, g.stride(0), _lib.ptr(low.contiguous()),
+            _lib.ptr(offsets), experts, float(scaling), _lib.ptr(out), layout, _lib.ptr(cmap[0]), _lib.ptr(cmap[1]),
+            _lib.ptr(cmap[2]), cmap[0].numel(), _lib.ptr(partial), partial.numel() * 4, _lib.stream_of(g)),
+            "meep2b_grouped_reduce_rows_full")
     else:
         if g_rows is None:
             raise ValueError("a weighted reduction reads its rows through g_rows")

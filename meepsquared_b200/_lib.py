@@ -68,6 +68,9 @@ _SIGNATURES = {
     "meep2b_grouped_product": (ctypes.c_int, [ctypes.POINTER(Product), _p]),
     "meep2b_grouped_reduce": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _i32, _p]),
     "meep2b_grouped_reduce_rows": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _i32, _p]),
+    "meep2b_grouped_reduce_rows_full": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i32, _f32, _p, _i32,
+                                                       _p, _p, _p, _i64, _p, _sz, _p]),
+    "meep2b_reduce_chunk_rows": (ctypes.c_int, []),
     "meep2b_fp8_stack_quantize": (ctypes.c_int, [_p, _i32, _i32, _i64, _p, _p, _p, _p]),
     "meep2b_fp8_stack_dequantize": (ctypes.c_int, [_p, _p, _i32, _i64, _p, _p]),
     "meep2b_fp8_block_dequantize": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i32, _i32, _p, _p]),
@@ -131,7 +134,8 @@ class DeviceError(RuntimeError):
 KERNELS_PER_CALL = {
     "meep2b_route": 3, "meep2b_route_noalloc": 3, "meep2b_route_logits": 3, "meep2b_routed_rows": 1, "meep2b_gather": 1,
     "meep2b_unpermute": 1, "meep2b_unpermute_backward": 1, "meep2b_tile_map": 1, "meep2b_grouped_product": 1,
-    "meep2b_grouped_reduce": 1, "meep2b_grouped_reduce_rows": 1, "meep2b_fp8_stack_dequantize": 1,
+    "meep2b_grouped_reduce": 1, "meep2b_grouped_reduce_rows": 1, "meep2b_grouped_reduce_rows_full": 2,
+    "meep2b_fp8_stack_dequantize": 1,
     "meep2b_fp8_block_dequantize": 1, "meep2b_nf4_dequantize": 2, "meep2b_nf4_absmax": 1,
     "meep2b_merge_stack": 1,
     "meep2b_quant_multipliers": 1, "meep2b_fp8_rows_quantize": 1, "meep2b_grouped_product_f8": 1,

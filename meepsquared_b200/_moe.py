@@ -331,7 +331,7 @@ class _RoutedExperts(torch.autograd.Function):
             else:
                 second = dict(g=grad_out, low=low2, g_rows=token_rows, row_scale=w32)
             grads[2], grads[3] = _adapter_grads(ad2, ctx.leaves[2], ctx.leaves[3], first, second, routing.offsets,
-                                                st.scaling2)
+                                                st.scaling2, tiles)
         gate_up_stack = _stack(st.gate_up)
         # quantised products store rows in order
         token_major = _token_major_rows() and not isinstance(gate_up_stack, _grouped.QuantStack)
@@ -346,13 +346,13 @@ class _RoutedExperts(torch.autograd.Function):
                 first = dict(g=hidden, low=low1b, g_rows=token_rows)
             second = dict(g=dgu, low=low1)
             grads[0], grads[1] = _adapter_grads(ad1, ctx.leaves[0], ctx.leaves[1], first, second, routing.offsets,
-                                                st.scaling1)
+                                                st.scaling1, tiles)
         grad_hidden = combine(dsel, routing, None) if token_major else unpermute(dsel, routing, None)
         grad_w = grad_w.view(routing.num_tokens, routing.top_k)
         return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None, None)
 
 
-def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling):
+def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling, tiles=None):
     """PEFT's (lhs, rhs) gradients of one stack's adapters from the two reductions of the backward pass (first: the
     factor the forward applies first, second: the other; _grouped.py:400-405), each written in its factor's own
     layout: (experts, n, 16) for lhs (E, out, r) or a transposed stack's lhs (E, in, r), (experts, 16, n) for rhs.
@@ -374,7 +374,7 @@ def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling):
         if slot is not None and tuple(slot.shape) != want:
             slot = None
         g = _grouped._reduce(red["g"], red["low"], offsets, scaling, g_rows=red.get("g_rows"),
-                             row_scale=red.get("row_scale"), out=slot, layout=layout)
+                             row_scale=red.get("row_scale"), out=slot, layout=layout, tiles=tiles)
         out[name] = g if rank == RANK else (g[:, :, :rank] if layout == 0 else g[:, :rank, :])
         if slot is not None:
             written.append(leaf)

@@ -68,3 +68,40 @@ def test_the_weighted_gathered_reduction_matches_float32():
     lw = as_np(low) * as_np(w32)[:, None]
     want = ogrouped.reduce_adapter(rows, lw, as_np(routing.offsets), 2.0)
     assert_close(got, want, "reduce", scaled=True)
+
+
+@pytest.mark.parametrize("n", [768, 1536, 2048])
+@pytest.mark.parametrize("weighted", [False, True])
+@pytest.mark.parametrize("layout", [0, 1])
+def test_the_whole_row_gathered_reduction_matches_float32(n, weighted, layout):
+    """The widths whose gathered reductions read whole rows per CTA (chunks of an expert's rows, the chunks' sums
+    added in order): an expert with no rows, one with a few, the rest over several chunks with a ragged last one; g
+    a column slice of a wider tensor (row pitch above n)."""
+    tokens, experts, k = 1500, 8, 3
+    gen = torch.Generator().manual_seed(5 + n)
+    probs = torch.tensor([0.3, 0.2, 0.2, 0.15, 0.1, 0.05, 0.0, 0.0])
+    idx = torch.multinomial(probs.expand(tokens, experts), k, replacement=False, generator=gen)
+    idx[:5, 2] = 6  # five rows for expert 6, none for expert 7
+    idx = idx.to(DEV)
+    w = torch.rand(tokens, k, generator=gen).to(DEV)
+    routing = _moe.route(idx, w, experts)
+    token_rows, w32 = _moe.routed_rows(routing, w)
+    counts = np.diff(np.concatenate([[0], as_np(routing.offsets)]))
+    chunk = int(_lib.load().meep2b_reduce_chunk_rows())
+    assert counts[7] == 0 and counts[6] == 5 and counts.max() > 2 * chunk
+    wide = torch.randn(tokens, n + 64, generator=gen).to(DEV, torch.bfloat16)
+    g = wide[:, :n]
+    low = torch.randn(routing.perm.numel(), 16, generator=gen).to(DEV, torch.bfloat16)
+    scale = w32 if weighted else None
+    got = _grouped._reduce(g, low, routing.offsets, 2.0, g_rows=token_rows, row_scale=scale, layout=layout,
+                           tiles=routing.tile_map())
+    rows = as_np(g)[as_np(token_rows).astype(np.int64)]
+    lw = as_np(low) * (as_np(w32)[:, None] if weighted else 1.0)
+    want = ogrouped.reduce_adapter(rows, lw, as_np(routing.offsets), 2.0)
+    if layout == 1:
+        want = want.transpose(0, 2, 1)
+    assert_close(got, want, f"reduce n={n}", scaled=True)
+    assert not as_np(got)[7].any()
+    # deterministic: the chunks' sums are added in a fixed order (the chunk map built anew here)
+    again = _grouped._reduce(g, low, routing.offsets, 2.0, g_rows=token_rows, row_scale=scale, layout=layout)
+    assert torch.equal(got.view(torch.int16), again.view(torch.int16))
