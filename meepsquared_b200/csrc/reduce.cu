@@ -202,12 +202,6 @@ constexpr int FR_STAGES = 3;
 constexpr int FR_CHUNK = 512;
 constexpr int FR_CONSUMERS = 8;  // warps
 
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
-
 __host__ __device__ constexpr int fr_gpitch(int n) { return n + 8; }  // bf16 per smem row of g (+16 bytes)
 __host__ __device__ constexpr int fr_stage_bytes(int n) { return FR_ROWS * fr_gpitch(n) * 2 + FR_ROWS * 32; }
 // stages, then the chunk's row indices and weights (FR_CHUNK each), then 2 x FR_STAGES barriers

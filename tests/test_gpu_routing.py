@@ -58,6 +58,23 @@ def test_tile_map_matches_the_reference_kats(golden):
         np.testing.assert_array_equal(tr.cpu().numpy(), g[f"{name}_tile_row"], err_msg=name)
 
 
+@pytest.mark.parametrize("hidden_dim,tokens", [(768, 3001), (2048, 3001), (4096, 1500), (8192, 300)])
+def test_gather_of_many_rows_matches_the_oracle(hidden_dim, tokens):
+    """Rows gathered by bulk copies over several stages per SM (the last stage ragged), sentinel rows zeroed, the
+    weights gathered with them; 8192 columns take the per-warp form (stages too large for shared memory)."""
+    experts, k = 16, 3
+    gen = torch.Generator().manual_seed(hidden_dim)
+    idx = torch.stack([torch.randperm(experts + 1, generator=gen)[:k] for _ in range(tokens)])  # id 16: a sentinel
+    w = torch.rand(tokens, k, generator=gen)
+    hidden = torch.randn(tokens, hidden_dim, generator=gen).to(torch.bfloat16)
+    r = mb.route(idx.to(DEV), w.to(DEV), experts)
+    sel = mb.gather(hidden.to(DEV), r, w.to(DEV))
+    want = oroute.route(idx.numpy(), experts)
+    assert want["sentinel"].any()
+    np.testing.assert_array_equal(as_np(sel), oroute.gather(as_np(hidden), want["perm"], k, want["sentinel"]))
+    np.testing.assert_array_equal(as_np(r.weights_g), as_np(w).reshape(-1)[want["perm"]])
+
+
 @pytest.mark.parametrize("wdtype", [torch.float32, torch.bfloat16])
 def test_gather_and_unpermute_match_the_oracle(wdtype):
     cfg = dict(layer_inputs.SMALL)
