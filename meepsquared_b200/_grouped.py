@@ -96,9 +96,6 @@ class TileMaps:
     def __init__(self, offsets: torch.Tensor, rows: int):
         self.offsets, self.rows, self._maps = offsets, rows, {}
 
-    def built(self, block_m: int) -> bool:
-        return block_m in self._maps
-
     def get(self, block_m: int):
         if block_m not in self._maps:
             self._maps[block_m] = tile_map(self.offsets, self.rows, block_m)
@@ -487,11 +484,6 @@ def _product(x, weight, scale, offsets, k_contiguous_layout, adapters, scaling, 
                    tiles=tiles)
 
 
-def reduce_chunk_rows() -> int:
-    """Rows per chunk of the whole-row gathered reduction (the tile height of its chunk map)."""
-    return int(_lib.load().meep2b_reduce_chunk_rows())
-
-
 # widths of g whose gathered reductions take the whole-row form (the layer's hidden and upstream-gradient rows at
 # the benchmarked shapes; the kernel is built for these three)
 _FULL_ROW_WIDTHS = (768, 1536, 2048)
@@ -526,7 +518,7 @@ def _reduce(g: torch.Tensor, low: torch.Tensor, offsets: torch.Tensor, scaling: 
     elif g_rows is not None and N in _FULL_ROW_WIDTHS:
         # gathered rows arrive whole, one bulk copy each (meep2b_grouped_reduce_rows_full): a CTA per chunk of an
         # expert's rows, the chunks' float32 sums added in order by a second kernel
-        chunk = reduce_chunk_rows()
+        chunk = int(lib.meep2b_reduce_chunk_rows())
         cmap = tiles.get(chunk) if tiles is not None else tile_map(offsets, rows, chunk)
         partial = torch.empty(cmap[0].numel() * N * RANK_MULTIPLE, device=g.device, dtype=torch.float32)
         _lib.check(lib.meep2b_grouped_reduce_rows_full(

@@ -339,12 +339,6 @@ class _RoutedExperts(torch.autograd.Function):
                                        None, True, backward=True, tiles=tiles,
                                        out_rows=routing.perm if token_major else None)
         del gate_up_stack
-        # the input gradient's combine first: it streams from HBM while the gate/up adapters' reduction over the
-        # hidden rows (bound by L2) runs beside it on the side stream
-        fork = torch.cuda.Event()
-        fork.record()
-        grad_hidden = combine(dsel, routing, None) if token_major else unpermute(dsel, routing, None)
-        del dsel
         if ad1 is not None:
             if mode == "copy":
                 first = dict(g=sel, low=low1b)
@@ -352,40 +346,26 @@ class _RoutedExperts(torch.autograd.Function):
                 first = dict(g=hidden, low=low1b, g_rows=token_rows)
             second = dict(g=dgu, low=low1)
             grads[0], grads[1] = _adapter_grads(ad1, ctx.leaves[0], ctx.leaves[1], first, second, routing.offsets,
-                                                st.scaling1, tiles, fork)
+                                                st.scaling1, tiles)
+        grad_hidden = combine(dsel, routing, None) if token_major else unpermute(dsel, routing, None)
         grad_w = grad_w.view(routing.num_tokens, routing.top_k)
         return (grad_hidden, grad_w.to(ctx.weights_dtype), grads[0], grads[1], grads[2], grads[3], None, None, None)
 
 
-def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling, tiles=None, fork=None):
+def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling, tiles=None):
     """PEFT's (lhs, rhs) gradients of one stack's adapters from the two reductions of the backward pass (first: the
     factor the forward applies first, second: the other; _grouped.py:400-405), each written in its factor's own
     layout: (experts, n, 16) for lhs (E, out, r) or a transposed stack's lhs (E, in, r), (experts, 16, n) for rhs.
     At rank 16 a factor whose slot in a LoRA-gradient bucket is free (ddp.grad_slot) gets its gradient written
-    there, and autograd adopts it without a copy. fork: an event on the current stream after which the reductions'
-    operands are ready (default: now)."""
+    there, and autograd adopts it without a copy."""
     from . import ddp
 
     rank = ad.rank
     lhs_first = ad.is_transposed  # a transposed stack applies lhs (E, in, r) first, else rhs^T
     spec = {"lhs": (first if lhs_first else second, 0, lhs), "rhs": (second if lhs_first else first, 1, rhs)}
-    # The two reductions run at once: the one over rows read through the routing (bound by L2 latency) on a side
-    # stream, the other (streaming its operand from HBM) on the current one.
-    main = torch.cuda.current_stream(offsets.device)
-    side_name = "lhs" if spec["lhs"][0].get("g_rows") is not None else "rhs"
-    side = _side_stream(offsets.device) if _concurrent_reductions() else None
-    if side is not None:
-        chunk = _grouped.reduce_chunk_rows()
-        fresh = tiles is not None and not tiles.built(chunk)
-        if tiles is not None:
-            tiles.get(chunk)  # the chunk map, built on the current stream
-        if fork is None or fresh:
-            side.wait_stream(main)
-        else:
-            side.wait_event(fork)
     out = {}
     written = []
-    for name, (red, layout, leaf) in sorted(spec.items(), key=lambda kv: kv[0] != side_name):
+    for name, (red, layout, leaf) in spec.items():
         slot = ddp.grad_slot(leaf) if rank == RANK and leaf is not None else None
         if slot is not None and (slot.dtype != torch.bfloat16 or not slot.is_contiguous()):
             slot = None
@@ -393,38 +373,17 @@ def _adapter_grads(ad, lhs, rhs, first, second, offsets, scaling, tiles=None, fo
         want = (offsets.numel(), n, RANK) if layout == 0 else (offsets.numel(), RANK, n)
         if slot is not None and tuple(slot.shape) != want:
             slot = None
-        on_side = side is not None and name == side_name
-        with torch.cuda.stream(side if on_side else main):
-            g = _grouped._reduce(red["g"], red["low"], offsets, scaling, g_rows=red.get("g_rows"),
-                                 row_scale=red.get("row_scale"), out=slot, layout=layout, tiles=tiles)
-        if on_side and slot is None:
-            g.record_stream(main)  # made on the side stream, used and freed on the current one
+        g = _grouped._reduce(red["g"], red["low"], offsets, scaling, g_rows=red.get("g_rows"),
+                             row_scale=red.get("row_scale"), out=slot, layout=layout, tiles=tiles)
         out[name] = g if rank == RANK else (g[:, :, :rank] if layout == 0 else g[:, :rank, :])
         if slot is not None:
             written.append(leaf)
-    if side is not None:
-        main.wait_stream(side)
     for leaf in written:  # the bucket may start averaging these slots (they are complete in stream order)
         ddp.mark_written(leaf)
     return out["lhs"], out["rhs"]
 
 
 RANK = _grouped.RANK_MULTIPLE
-_SIDE_STREAMS = {}
-
-
-def _side_stream(device):
-    """The stream a layer's backward pass runs one adapter reduction on, per device."""
-    key = torch.device(device).index
-    if key not in _SIDE_STREAMS:
-        _SIDE_STREAMS[key] = torch.cuda.Stream(device=device)
-    return _SIDE_STREAMS[key]
-
-
-def _concurrent_reductions() -> bool:
-    """MEEP2B_REDUCE_STREAMS: 2 (default) runs a stack's two adapter reductions on two streams at once, 1 one after
-    the other on the current stream (the same results either way)."""
-    return os.environ.get("MEEP2B_REDUCE_STREAMS", "2") != "1"
 
 
 class _PerProduct:

@@ -5,7 +5,6 @@
 //
 // Replaces _moe._routed_forward's sort / histc / cumsum / gather / weighted sum (meepsquared/_moe.py:75-87,
 // 123-126) and _grouped.tile_map (meepsquared/_grouped.py:88-103).
-#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -234,106 +233,6 @@ __global__ void __launch_bounds__(256) gather_rows(const uint4* __restrict__ hid
   } else {
     for (int64_t v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
   }
-}
-
-// The same gather with bulk copies, a warp per CTA and one CTA per SM: each stage of GB_ROWS consecutive
-// destination rows comes in as one bulk copy per source row (a lane each) and goes out as one bulk store of the
-// stage's contiguous rows; `lookahead` stages of loads are in flight while GB_PENDING stores may still be reading
-// their stages. Sentinel rows (past the real rows) are written as zeros by plain stores.
-constexpr int GB_ROWS = 4;
-constexpr int GB_PENDING = 3;  // stores that may still read shared memory when a stage is reloaded
-constexpr int GB_MAX_STAGES = 12;
-
-template <typename W>
-__global__ void __launch_bounds__(32) gather_rows_bulk(const uint8_t* __restrict__ hidden, int64_t row_bytes,
-                                                       int top_k, const int64_t* __restrict__ perm,
-                                                       const int32_t* __restrict__ offsets, int experts, int64_t rows,
-                                                       int64_t rows_per_cta, int stages,
-                                                       const W* __restrict__ weights, W* __restrict__ weights_g,
-                                                       uint8_t* __restrict__ selected) {
-  extern __shared__ __align__(128) uint8_t gb_smem[];
-  const int lane = threadIdx.x;
-  const int lookahead = stages - GB_PENDING - 1;
-  const int64_t first = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
-  const int64_t last = min(rows, first + rows_per_cta);
-  if (first >= last) return;
-  const int64_t valid = offsets[experts - 1];
-  const int iters = static_cast<int>((last - first + GB_ROWS - 1) / GB_ROWS);
-  const uint32_t stage_bytes = static_cast<uint32_t>(GB_ROWS * row_bytes);
-  const uint32_t sbase = smem_u32(gb_smem);
-  const uint32_t bar0 = sbase + stages * stage_bytes;
-  if (lane == 0) {
-    for (int s = 0; s < stages; ++s) mbar_init(bar0 + 8u * s, 1);
-    fence_barrier_init();
-  }
-  __syncwarp();
-  // The permutation is read 32 rows (8 iterations) at a time, a block ahead of its use: lane j holds the source of
-  // row first + 32 b + j of block b; a block's routing weights are loaded when the block comes into use and stored
-  // when the next one does, so that no load stalls the warp in the loop.
-  static_assert(GB_ROWS * 8 == 32, "a block of the permutation covers eight iterations");
-  auto perm_at = [&](int64_t row) -> int64_t { return row < last ? perm[row] : 0; };
-  int64_t blk_cur = perm_at(first + lane), blk_next = perm_at(first + 32 + lane);
-  int cur_block = 0;
-  W w_cur{};
-  const bool weighted = weights_g != nullptr;
-  if (weighted && first + lane < last) w_cur = weights[blk_cur];
-  // the rows of iteration `it` into its stage: lane j < GB_ROWS copies row first + GB_ROWS it + j if it is real
-  auto issue = [&](int it) {
-    const int b = it >> 3;
-    if (b != cur_block) {  // issue order is monotone: b == cur_block + 1
-      if (weighted && first + 32 * cur_block + lane < last) weights_g[first + 32 * cur_block + lane] = w_cur;
-      blk_cur = blk_next;
-      cur_block = b;
-      blk_next = perm_at(first + 32 * static_cast<int64_t>(b + 1) + lane);
-      if (weighted && first + 32 * b + lane < last) w_cur = weights[blk_cur];
-    }
-    const int s = it % stages;
-    const int64_t r = first + static_cast<int64_t>(it) * GB_ROWS;
-    const int n = static_cast<int>(min(static_cast<int64_t>(GB_ROWS), last - r));
-    const int nv = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(n), valid - r)));
-    const int64_t src = __shfl_sync(0xffffffffu, blk_cur, (it & 7) * GB_ROWS + (lane & (GB_ROWS - 1)));
-    const uint32_t bar = bar0 + 8u * s;
-    if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nv) * static_cast<uint32_t>(row_bytes));
-    __syncwarp();
-    if (lane < nv)
-      bulk_load(sbase + s * stage_bytes + lane * static_cast<uint32_t>(row_bytes), hidden + (src / top_k) * row_bytes,
-                static_cast<uint32_t>(row_bytes), bar);
-  };
-  for (int it = 0; it < lookahead && it < iters; ++it) issue(it);
-  int failed_at = -1;
-  for (int it = 0; it < iters; ++it) {
-    const int s = it % stages;
-    if (it + lookahead < iters) {
-      // the stage of it + lookahead was last stored at iteration it + lookahead - stages, GB_PENDING + 1 stores ago
-      if (lane == 0) bulk_wait_read<GB_PENDING>();
-      __syncwarp();
-      issue(it + lookahead);
-    }
-    const int64_t r = first + static_cast<int64_t>(it) * GB_ROWS;
-    const int n = static_cast<int>(min(static_cast<int64_t>(GB_ROWS), last - r));
-    const int nv = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(n), valid - r)));
-    if (!__all_sync(0xffffffffu, mbar_wait(bar0 + 8u * s, static_cast<uint32_t>((it / stages) & 1)))) {
-      failed_at = it;
-      break;
-    }
-    if (lane == 0) {
-      if (nv > 0) bulk_store(selected + r * row_bytes, sbase + s * stage_bytes, static_cast<uint32_t>(nv * row_bytes));
-      bulk_commit();  // one group per iteration, empty or not, so that the count of pending groups stays exact
-    }
-    for (int j = nv; j < n; ++j)  // sentinel rows: zeros
-      for (int64_t v = lane; v < row_bytes / 16; v += 32)
-        reinterpret_cast<uint4*>(selected + (r + j) * row_bytes)[v] = make_uint4(0, 0, 0, 0);
-  }
-  if (failed_at < 0 && weighted && first + 32 * cur_block + lane < last)
-    weights_g[first + 32 * cur_block + lane] = w_cur;  // the last block's weights
-  if (failed_at >= 0 && lane == 0) {
-    // a wait gave up (the error is recorded): wait (bounded) for the loads issued and not yet consumed, the
-    // latest phase of their stages
-    const int issued = min(iters, failed_at + lookahead + 1);
-    for (int it = failed_at; it < issued; ++it)
-      mbar_wait_drain(bar0 + 8u * (it % stages), static_cast<uint32_t>((it / stages) & 1));
-  }
-  if (lane == 0) bulk_wait_all();
 }
 
 __device__ __forceinline__ float weight_value(const float* w, int64_t i) { return w[i]; }
@@ -640,8 +539,6 @@ int meep2b_routed_rows(const int64_t* perm, int64_t assignments, int32_t top_k, 
   return launch_status();
 }
 
-constexpr int64_t kGatherSmem = 196608;  // shared memory of the bulk gather's stages
-
 int meep2b_gather(const void* hidden, int64_t tokens, int64_t hidden_dim, int32_t top_k, const int64_t* perm,
                   const int32_t* offsets, int32_t experts, const void* weights, int32_t weights_dtype,
                   void* weights_g, void* selected, void* stream) {
@@ -653,30 +550,6 @@ int meep2b_gather(const void* hidden, int64_t tokens, int64_t hidden_dim, int32_
   const int64_t rows = tokens * top_k;
   if (rows == 0) return MEEP2B_OK;
   const int64_t vec = hidden_dim / 8;
-  const int64_t row_bytes = hidden_dim * 2;
-  const int stages = static_cast<int>(std::min<int64_t>(GB_MAX_STAGES, kGatherSmem / (GB_ROWS * row_bytes)));
-  if (stages >= GB_PENDING + 2) {
-    int sms = 0, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms < 1) sms = 148;
-    const int64_t per = ((rows + sms - 1) / sms + GB_ROWS - 1) / GB_ROWS * GB_ROWS;
-    const unsigned grid = static_cast<unsigned>((rows + per - 1) / per);
-    const int smem = stages * GB_ROWS * static_cast<int>(row_bytes) + 8 * stages;
-    auto run = [&](auto kern, const auto* w, auto* wg) -> int {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
-        cudaGetLastError();
-        return MEEP2B_ERR_LAUNCH;
-      }
-      kern<<<grid, 32, smem, s>>>(static_cast<const uint8_t*>(hidden), row_bytes, top_k, perm, offsets, experts, rows,
-                                  per, stages, w, wg, static_cast<uint8_t*>(selected));
-      return launch_status();
-    };
-    if (weights_dtype == MEEP2B_BF16)
-      return run(gather_rows_bulk<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(weights),
-                 static_cast<__nv_bfloat16*>(weights_g));
-    return run(gather_rows_bulk<float>, static_cast<const float*>(weights), static_cast<float*>(weights_g));
-  }
   const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
   if (weights_dtype == MEEP2B_BF16)
     gather_rows<__nv_bfloat16><<<grid, 256, 0, s>>>(

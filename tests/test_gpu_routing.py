@@ -60,8 +60,8 @@ def test_tile_map_matches_the_reference_kats(golden):
 
 @pytest.mark.parametrize("hidden_dim,tokens", [(768, 3001), (2048, 3001), (4096, 1500), (8192, 300)])
 def test_gather_of_many_rows_matches_the_oracle(hidden_dim, tokens):
-    """Rows gathered by bulk copies over several stages per SM (the last stage ragged), sentinel rows zeroed, the
-    weights gathered with them; 8192 columns take the per-warp form (stages too large for shared memory)."""
+    """Thousands of rows of 768 to 8192 columns gathered into expert order, sentinel rows zeroed, the routing
+    weights gathered with them."""
     experts, k = 16, 3
     gen = torch.Generator().manual_seed(hidden_dim)
     idx = torch.stack([torch.randperm(experts + 1, generator=gen)[:k] for _ in range(tokens)])  # id 16: a sentinel
