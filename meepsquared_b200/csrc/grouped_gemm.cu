@@ -44,12 +44,9 @@ constexpr int ACC_STRIDE = 256;
 template <bool B_MN, int EPI = MEEP2B_EPI_PLAIN>
 struct Plan {
   static constexpr bool DS = B_MN && EPI == MEEP2B_EPI_DSWIGLU;
-  static constexpr int STAGES = 4;
-  // per epilogue warp, in 2 KB buffers: the dSwiGLU epilogue's gate and up tiles (one 32-column chunk at a time)
-  static constexpr int STG_BUFS = DS ? 2 : (B_MN ? 1 : 2);
-  // MN-major B: the 192 stack columns as six 32-column atoms with the 64-byte swizzle (64 k-rows x 64 B each), then
-  // the panel's atom (its 16 columns and 16 of zeros); K-major: 208 rows of 128 B
-  static constexpr int B_BYTES = B_MN ? 7 * 64 * 64 : (BN + RP) * BK * 2;
+  static constexpr int STAGES = DS ? 3 : 4;
+  static constexpr int STG_BUFS = DS ? 4 : (B_MN ? 1 : 2);  // per epilogue warp
+  static constexpr int B_BYTES = B_MN ? 4 * 64 * BK * 2 : (BN + RP) * BK * 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_U = OFF_B + STAGES * B_BYTES;
@@ -238,11 +235,10 @@ __device__ __forceinline__ void tile32_write(uint32_t tile, int lane, const uint
 }
 
 // The dSwiGLU epilogue of one warp (32 rows, all of the expert, and `cols` <= 96 columns from n0) through shared
-// memory: per 32 columns the warp's lane 0 TMA-loads the gate and up pre-activation tiles (32 x 32 each) into its
-// buffer, every lane reads its row, writes dgate and dup over the tiles, and lane 0 TMA-stores them; the next
-// chunk's tiles are loaded once the stores have read the buffer (one buffer, so that the operand ring keeps four
-// stages). stg: the 4 KB buffer (gate tile, then up tile); ldbar: its load barrier; phases: the barrier's next
-// parity (bit 0).
+// memory: per 32 columns the warp's lane 0 TMA-loads the gate and up pre-activation tiles (32 x 32 each) into one
+// of two buffers (the next chunk's loads in flight while this one is computed), every lane reads its row, writes
+// dgate and dup over the tiles, and lane 0 TMA-stores them. stg: two buffers of 4 KB (gate tile, then up tile);
+// ldbar: their two load barriers (8 bytes apart); phases: the barriers' next parities (bit b for buffer b).
 template <bool PAIR>
 __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0, int cols, float sc, float rw,
                                                uint32_t d, int lane, uint32_t stg, uint32_t ldbar, uint32_t& phases,
@@ -258,10 +254,12 @@ __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0
   }
   auto load = [&](int c) {
     if (lane == 0) {
-      bulk_wait_read<0>();  // the buffer's last tiles have been read by their stores
-      mbar_arrive_expect_tx(ldbar, 4096);
-      tma_load_2d(stg, tm_aux, ldbar, n0 + 32 * c, row0);
-      tma_load_2d(stg + 2048, tm_aux, ldbar, p.N + n0 + 32 * c, row0);
+      const uint32_t buf = stg + static_cast<uint32_t>(c & 1) * 4096u;
+      bulk_wait_read<0>();  // this buffer's last tiles have been read by their stores
+      const uint32_t bar = ldbar + 8u * static_cast<uint32_t>(c & 1);
+      mbar_arrive_expect_tx(bar, 4096);
+      tma_load_2d(buf, tm_aux, bar, n0 + 32 * c, row0);
+      tma_load_2d(buf + 2048, tm_aux, bar, p.N + n0 + 32 * c, row0);
     }
   };
   load(0);
@@ -270,6 +268,7 @@ __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0
   float wpart = 0.0f;
   bool ok = true;
   for (int c = 0; c < chunks; ++c) {
+    if (c + 1 < chunks) load(c + 1);
     uint32_t acc[32];
     tmem_ld16_async(d + 32 * c, acc);
     tmem_ld16_async(d + 32 * c + 16, acc + 16);
@@ -279,9 +278,10 @@ __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0
       tc_fence_before();
       arrive_on<PAIR>(bar_tempty_ab);  // the whole accumulator is in registers or done
     }
-    if (!mbar_wait(ldbar, phases & 1u)) { ok = false; break; }
-    phases ^= 1u;
-    const uint32_t buf = stg;
+    const uint32_t b = static_cast<uint32_t>(c & 1);
+    if (!mbar_wait(ldbar + 8u * b, (phases >> b) & 1u)) { ok = false; break; }
+    phases ^= 1u << b;
+    const uint32_t buf = stg + b * 4096u;
     uint32_t gw[16], uw[16];
     tile32_read(buf, lane, gw);
     tile32_read(buf + 2048, lane, uw);
@@ -314,7 +314,6 @@ __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0
       tma_store_2d(tm_out, buf + 2048, p.N + n0 + 32 * c, row0);
       bulk_commit();
     }
-    if (c + 1 < chunks) load(c + 1);
   }
   if (!ok) return false;
   if (p.w_grad != nullptr && cols > 0) p.w_grad[orow * p.w_ld + n0 / 96] = wpart;
@@ -765,7 +764,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_prefetch_desc(&tm_p);
         tma_prefetch_desc(&tm_u);
       }
-      constexpr uint32_t B_TX = 64 * BN * 2 + (LORA ? (B_MN ? 32 * 64 * 2 : RP * 64 * 2) : 0);
+      constexpr uint32_t B_TX = 64 * BN * 2 + (LORA ? (B_MN ? 64 * 64 * 2 : RP * 64 * 2) : 0);
       constexpr uint32_t STAGE_TX = A_BYTES + B_TX;
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool { return mbar_wait(bar, parity); };
       int stage = 0;
@@ -819,8 +818,8 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (LORA) tma_load_3d(b_dst + BN * 128, &tm_p, fb, kb * BK, 0, e);
             } else {
 #pragma unroll
-              for (int j = 0; j < 6; ++j) tma_load_3d(b_dst + j * 4096, &tm_w, fb, nb * BN + 32 * j, kb * BK, e);
-              if (LORA) tma_load_3d(b_dst + 6 * 4096, &tm_p, fb, 0, kb * BK, e);
+              for (int j = 0; j < 3; ++j) tma_load_3d(b_dst + j * 8192, &tm_w, fb, nb * BN + 64 * j, kb * BK, e);
+              if (LORA) tma_load_3d(b_dst + 3 * 8192, &tm_p, fb, 0, kb * BK, e);
             }
           }
           issued[stage] = true;
@@ -883,8 +882,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       // (bits 0-13, 16-byte units), which stays below 2^14 for every shared-memory address of the plan.
       const uint64_t a_desc0 = smem_desc(sbase + P::OFF_A, 16, 1024, 2);
       const uint64_t b_desc0 =
-          B_MN ? smem_desc(sbase + P::OFF_B, 4096, 512, 4) : smem_desc(sbase + P::OFF_B, 16, 1024, 2);
-      constexpr uint32_t B_KK = B_MN ? 1024 / 16 : 32 / 16;  // one k-slice of 16, in 16-byte units
+          B_MN ? smem_desc(sbase + P::OFF_B, 8192, 1024, 2) : smem_desc(sbase + P::OFF_B, 16, 1024, 2);
+      constexpr uint32_t B_KK = B_MN ? 2048 / 16 : 32 / 16;  // one k-slice of 16, in 16-byte units
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++it) {
         const int ab = it & 1;
         const uint32_t aph = (it >> 1) & 1;
@@ -1372,12 +1371,11 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
     MEEP2B_TRY(encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->weight, dims, strides, box,
                             CU_TENSOR_MAP_SWIZZLE_128B));
   } else {
-    // read MN-major: 32-column atoms (64 k-rows x 64 B) with the 64-byte swizzle
     const uint64_t dims[3] = {N, K, E};
     const uint64_t strides[2] = {N * 2, K * N * 2};
-    const uint32_t box[3] = {32, 64, 1};
+    const uint32_t box[3] = {64, 64, 1};
     MEEP2B_TRY(encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->weight, dims, strides, box,
-                            CU_TENSOR_MAP_SWIZZLE_64B));
+                            CU_TENSOR_MAP_SWIZZLE_128B));
   }
   if (lora) {
     if (!a->b_mn) {
@@ -1392,14 +1390,13 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
       MEEP2B_TRY(encode_tiled(&tu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->up, ud, us, ubx,
                               CU_TENSOR_MAP_SWIZZLE_32B));
     } else {
-      // the (E, k, 16) panel read as 32-column boxes with the 64-byte swizzle (the bf16 B tile's seventh atom;
-      // the 16 columns past its width arrive as zeros, the box's out-of-bounds fill), or as 64-column boxes with
-      // the 128-byte swizzle for a quantised stack's converted tile
+      // the (E, k, 16) panel read as 64-column boxes: the 48 columns past its width arrive as zeros (the box's
+      // out-of-bounds fill), the panel atom of the MN-major B tile
       const uint64_t pd[3] = {RP, K, E};
       const uint64_t ps[2] = {RP * 2, K * RP * 2};
-      const uint32_t pb[3] = {quantised ? 64u : 32u, 64, 1};
+      const uint32_t pb[3] = {64, 64, 1};
       MEEP2B_TRY(encode_tiled(&tp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->panel, pd, ps, pb,
-                              quantised ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
+                              CU_TENSOR_MAP_SWIZZLE_128B));
       const uint64_t ud[3] = {N, RP, E};
       const uint64_t us[2] = {N * 2, RP * N * 2};
       const uint32_t ubx[3] = {64, RP, 1};
