@@ -651,8 +651,13 @@ int meep2b_tile_map(const int32_t* offsets, int32_t experts, int64_t rows, int32
   cudaStream_t s = as_stream(stream);
   MEEP2B_TRY(bind_stream_device(s));
   const int64_t max_tiles = rows / block_m + experts;
-  tile_map_kernel<<<1, 1024, sizeof(int) * 2 * experts, s>>>(offsets, experts, block_m, max_tiles, tile_expert,
-                                                             tile_row, tiles);
+  const int smem = static_cast<int>(sizeof(int)) * 2 * experts;  // up to 128 KB at 16384 experts
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(tile_map_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return MEEP2B_ERR_LAUNCH;
+  }
+  tile_map_kernel<<<1, 1024, smem, s>>>(offsets, experts, block_m, max_tiles, tile_expert, tile_row, tiles);
   return launch_status();
 }
 

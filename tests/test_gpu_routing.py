@@ -58,6 +58,23 @@ def test_tile_map_matches_the_reference_kats(golden):
         np.testing.assert_array_equal(tr.cpu().numpy(), g[f"{name}_tile_row"], err_msg=name)
 
 
+@pytest.mark.parametrize("experts", [1, 100, 1023, 1025, 10000, 16384])
+@pytest.mark.parametrize("block_m", [128, 512])
+def test_tile_map_matches_the_oracle_for_many_experts(experts, block_m):
+    """Expert counts around the scan's 1024 threads and up to the limit (whose table takes 128 KB of shared
+    memory), some experts empty, against the oracle's tile map."""
+    gen = torch.Generator().manual_seed(experts + block_m)
+    counts = torch.randint(0, 3 * block_m, (experts,), generator=gen)
+    counts[torch.rand(experts, generator=gen) < 0.3] = 0
+    offsets = torch.cumsum(counts, 0).to(torch.int32)
+    rows = int(offsets[-1])
+    te, tr, tiles = mb.tile_map(offsets.to(DEV), rows, block_m)
+    want_e, want_r, want_n = oroute.tile_map(offsets.numpy(), rows, block_m)
+    assert tiles.item() == want_n
+    np.testing.assert_array_equal(te.cpu().numpy()[:want_n], want_e[:want_n])
+    np.testing.assert_array_equal(tr.cpu().numpy()[:want_n], want_r[:want_n])
+
+
 @pytest.mark.parametrize("hidden_dim,tokens", [(768, 3001), (2048, 3001), (4096, 1500), (8192, 300)])
 def test_gather_of_many_rows_matches_the_oracle(hidden_dim, tokens):
     """Thousands of rows of 768 to 8192 columns gathered into expert order, sentinel rows zeroed, the routing
