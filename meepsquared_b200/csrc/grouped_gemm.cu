@@ -44,8 +44,9 @@ constexpr int ACC_STRIDE = 256;
 template <bool B_MN, int EPI = MEEP2B_EPI_PLAIN>
 struct Plan {
   static constexpr bool DS = B_MN && EPI == MEEP2B_EPI_DSWIGLU;
-  static constexpr int STAGES = DS ? 3 : 4;
-  static constexpr int STG_BUFS = DS ? 4 : (B_MN ? 1 : 2);  // per epilogue warp
+  static constexpr int STAGES = 4;
+  // per epilogue warp, in 2 KB buffers (the dSwiGLU epilogue: one 16-column chunk's gate and up tiles)
+  static constexpr int STG_BUFS = DS ? 1 : (B_MN ? 1 : 2);
   static constexpr int B_BYTES = B_MN ? 4 * 64 * BK * 2 : (BN + RP) * BK * 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
@@ -211,6 +212,21 @@ __device__ __forceinline__ void stage_row16(uint32_t tile, int lane, const uint3
                : "memory");
 }
 
+// The row `lane` of a 32-row x 16-column bf16 tile with the 32-byte swizzle (stage_row16's layout): 8 words, and
+// the same row written back.
+__device__ __forceinline__ void tile16_read(uint32_t tile, int lane, uint32_t (&w)[8]) {
+  const uint32_t r = tile + static_cast<uint32_t>(lane) * 32u;
+  const uint32_t sw = (static_cast<uint32_t>(lane) >> 2) & 1u;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+               : "r"(r + (sw << 4))
+               : "memory");
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+               : "r"(r + ((sw ^ 1u) << 4))
+               : "memory");
+}
+
 // A 32-row x 32-column bf16 tile in shared memory with the 64-byte swizzle (64-byte rows, the four 16-byte chunks
 // of row r at chunk ^ ((r >> 1) & 3)): the lane that owns row `lane` reads or writes its 16 words.
 __device__ __forceinline__ void tile32_read(uint32_t tile, int lane, uint32_t (&w)[16]) {
@@ -235,17 +251,18 @@ __device__ __forceinline__ void tile32_write(uint32_t tile, int lane, const uint
 }
 
 // The dSwiGLU epilogue of one warp (32 rows, all of the expert, and `cols` <= 96 columns from n0) through shared
-// memory: per 32 columns the warp's lane 0 TMA-loads the gate and up pre-activation tiles (32 x 32 each) into one
-// of two buffers (the next chunk's loads in flight while this one is computed), every lane reads its row, writes
-// dgate and dup over the tiles, and lane 0 TMA-stores them. stg: two buffers of 4 KB (gate tile, then up tile);
-// ldbar: their two load barriers (8 bytes apart); phases: the barriers' next parities (bit b for buffer b).
+// memory, 16 columns at a time: the warp's lane 0 TMA-loads the chunk's gate and up pre-activation tiles (32 x 16
+// each, 32-byte swizzle) into the warp's 2 KB buffer while the lanes read the chunk's accumulator words, every
+// lane reads its row, writes dgate and dup over the tiles, and lane 0 TMA-stores them; the next chunk's tiles are
+// loaded once the stores have read the buffer (one small buffer per warp, so that the operand ring keeps four
+// stages). ldbar: the buffer's load barrier; phases: its next parity (bit 0).
 template <bool PAIR>
 __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0, int cols, float sc, float rw,
                                                uint32_t d, int lane, uint32_t stg, uint32_t ldbar, uint32_t& phases,
                                                const CUtensorMap* tm_aux, const CUtensorMap* tm_out,
                                                uint32_t bar_tfull_ab, uint32_t aph, uint32_t bar_tempty_ab,
                                                int64_t orow) {
-  const int chunks = cols > 0 ? (cols + 31) / 32 : 0;
+  const int chunks = cols > 0 ? (cols + 15) / 16 : 0;
   if (chunks == 0) {
     if (!mbar_wait(bar_tfull_ab, aph)) return false;
     tc_fence_before();
@@ -254,12 +271,10 @@ __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0
   }
   auto load = [&](int c) {
     if (lane == 0) {
-      const uint32_t buf = stg + static_cast<uint32_t>(c & 1) * 4096u;
-      bulk_wait_read<0>();  // this buffer's last tiles have been read by their stores
-      const uint32_t bar = ldbar + 8u * static_cast<uint32_t>(c & 1);
-      mbar_arrive_expect_tx(bar, 4096);
-      tma_load_2d(buf, tm_aux, bar, n0 + 32 * c, row0);
-      tma_load_2d(buf + 2048, tm_aux, bar, p.N + n0 + 32 * c, row0);
+      bulk_wait_read<0>();  // the buffer's last tiles have been read by their stores
+      mbar_arrive_expect_tx(ldbar, 2048);
+      tma_load_2d(stg, tm_aux, ldbar, n0 + 16 * c, row0);
+      tma_load_2d(stg + 1024, tm_aux, ldbar, p.N + n0 + 16 * c, row0);
     }
   };
   load(0);
@@ -268,26 +283,21 @@ __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0
   float wpart = 0.0f;
   bool ok = true;
   for (int c = 0; c < chunks; ++c) {
-    if (c + 1 < chunks) load(c + 1);
-    uint32_t acc[32];
-    tmem_ld16_async(d + 32 * c, acc);
-    tmem_ld16_async(d + 32 * c + 16, acc + 16);
+    uint32_t acc[16];
+    tmem_ld16_async(d + 16 * c, acc);
     tmem_wait_regs16(acc);
-    tmem_wait_regs16(acc + 16);
     if (c + 1 == chunks) {
       tc_fence_before();
       arrive_on<PAIR>(bar_tempty_ab);  // the whole accumulator is in registers or done
     }
-    const uint32_t b = static_cast<uint32_t>(c & 1);
-    if (!mbar_wait(ldbar + 8u * b, (phases >> b) & 1u)) { ok = false; break; }
-    phases ^= 1u << b;
-    const uint32_t buf = stg + b * 4096u;
-    uint32_t gw[16], uw[16];
-    tile32_read(buf, lane, gw);
-    tile32_read(buf + 2048, lane, uw);
-    const int cnt = min(32, cols - 32 * c);
+    if (!mbar_wait(ldbar, phases & 1u)) { ok = false; break; }
+    phases ^= 1u;
+    uint32_t gw[8], uw[8];
+    tile16_read(stg, lane, gw);
+    tile16_read(stg + 1024, lane, uw);
+    const int cnt = min(16, cols - 16 * c);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 8; ++j) {
       float dgo[2], duo[2];
 #pragma unroll
       for (int hlf = 0; hlf < 2; ++hlf) {
@@ -305,15 +315,16 @@ __device__ __forceinline__ bool dswiglu_staged(const Params& p, int row0, int n0
       gw[j] = pack_bf16x2(dgo[0], dgo[1]);
       uw[j] = pack_bf16x2(duo[0], duo[1]);
     }
-    tile32_write(buf, lane, gw);
-    tile32_write(buf + 2048, lane, uw);
+    stage_row16(stg, lane, gw);
+    stage_row16(stg + 1024, lane, uw);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(tm_out, buf, n0 + 32 * c, row0);
-      tma_store_2d(tm_out, buf + 2048, p.N + n0 + 32 * c, row0);
+      tma_store_2d(tm_out, stg, n0 + 16 * c, row0);
+      tma_store_2d(tm_out, stg + 1024, p.N + n0 + 16 * c, row0);
       bulk_commit();
     }
+    if (c + 1 < chunks) load(c + 1);
   }
   if (!ok) return false;
   if (p.w_grad != nullptr && cols > 0) p.w_grad[orow * p.w_ld + n0 / 96] = wpart;
@@ -1332,17 +1343,17 @@ extern "C" int meep2b_grouped_product(const meep2b_product* a, void* stream) {
     const uint32_t ob[2] = {32, 32};
     staged = encode_tiled(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->out, od, os, ob,
                           CU_TENSOR_MAP_SWIZZLE_64B) == MEEP2B_OK;
-  } else if (epi == MEEP2B_EPI_DSWIGLU && !quantised && a->b_mn && a->block_m != 256 && a->n % 32 == 0 &&
+  } else if (epi == MEEP2B_EPI_DSWIGLU && !quantised && a->b_mn && a->block_m != 256 && a->n % 16 == 0 &&
              a->rows >= 32) {
-    // the dSwiGLU epilogue's pre-activation loads and gradient stores: (rows, 2n) maps in 32 x 32 boxes
+    // the dSwiGLU epilogue's pre-activation loads and gradient stores: (rows, 2n) maps in 16-column x 32-row boxes
     const uint64_t od[2] = {static_cast<uint64_t>(2 * a->n), static_cast<uint64_t>(a->rows)};
     const uint64_t os[1] = {static_cast<uint64_t>(a->ldo) * 2};
     const uint64_t as[1] = {static_cast<uint64_t>(2 * a->n) * 2};
-    const uint32_t bx[2] = {32, 32};
+    const uint32_t bx[2] = {16, 32};
     staged = encode_tiled(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->out, od, os, bx,
-                          CU_TENSOR_MAP_SWIZZLE_64B) == MEEP2B_OK &&
+                          CU_TENSOR_MAP_SWIZZLE_32B) == MEEP2B_OK &&
              encode_tiled(&taux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->aux, od, as, bx,
-                          CU_TENSOR_MAP_SWIZZLE_64B) == MEEP2B_OK;
+                          CU_TENSOR_MAP_SWIZZLE_32B) == MEEP2B_OK;
   } else if (epi == MEEP2B_EPI_SWIGLU && !quantised && (a->n / 2) % 16 == 0 && a->rows >= 32) {
     const uint64_t od[2] = {static_cast<uint64_t>(a->n / 2), static_cast<uint64_t>(a->rows)};
     const uint64_t os[1] = {static_cast<uint64_t>(a->ldo) * 2};
