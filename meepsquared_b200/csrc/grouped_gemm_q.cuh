@@ -83,14 +83,34 @@ struct QPlan {
 
 
 
+// Shared-memory accesses by shared-window address (ld/st.shared: no generic-address resolution on the path).
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts_v4(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
 // 8 bf16 from 4 code bytes of NF4 (two codes a byte, the first in the high nibble), each bf16(level * m): the 16
-// levels are read from shared memory (one word per level: a warp's reads hit distinct banks or broadcast).
-__device__ __forceinline__ uint4 nf4_chunk(uint32_t w, float m, const float* lv) {
+// levels are read from shared memory at lv (one word per level: a warp's reads hit distinct banks or broadcast).
+__device__ __forceinline__ uint4 nf4_chunk(uint32_t w, float m, uint32_t lv) {
   uint32_t o[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t b = (w >> (8 * j)) & 0xFFu;
-    o[j] = pack_bf16x2(__fmul_rn(lv[b >> 4], m), __fmul_rn(lv[b & 15u], m));
+    o[j] = pack_bf16x2(__fmul_rn(lds_f32(lv + 4u * (b >> 4)), m), __fmul_rn(lds_f32(lv + 4u * (b & 15u)), m));
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -125,6 +145,7 @@ __device__ __forceinline__ void convert_tasks(int ct, int rows, const uint8_t* r
   constexpr int RAW_ROW = QF == QF_NF4 ? 32 : 64;
   constexpr int MAXT = (ROWS * 8 + NT - 1) / NT;
   const int total = rows * 8;
+  const uint32_t raw_s = smem_u32(raw), mult_s = smem_u32(mult), bdst_s = smem_u32(bdst), lv_s = smem_u32(lv);
   uint2 code[MAXT];
   float m[MAXT];
 #pragma unroll
@@ -134,17 +155,15 @@ __device__ __forceinline__ void convert_tasks(int ct, int rows, const uint8_t* r
     m[i] = 1.0f;
     if (q < total) {
       const int r = q >> 3, c = q & 7;
-      const uint8_t* src = raw + r * RAW_ROW;
+      const uint32_t src = raw_s + static_cast<uint32_t>(r * RAW_ROW);
       if (QF == QF_NF4) {
         const uint32_t rsw = (r >> 2) & 1;
-        code[i].x = *reinterpret_cast<const uint32_t*>(src + (((static_cast<uint32_t>(c) >> 2) ^ rsw) << 4) +
-                                                       ((c & 3) << 2));
+        code[i].x = lds_u32(src + (((static_cast<uint32_t>(c) >> 2) ^ rsw) << 4) + ((c & 3) << 2));
       } else {
         const uint32_t rsw = (r >> 1) & 3;
-        code[i] = *reinterpret_cast<const uint2*>(src + (((static_cast<uint32_t>(c) >> 1) ^ rsw) << 4) +
-                                                  ((c & 1) << 3));
+        code[i] = lds_v2(src + (((static_cast<uint32_t>(c) >> 1) ^ rsw) << 4) + ((c & 1) << 3));
       }
-      if (QF != QF_E4M3) m[i] = mult[r];
+      if (QF != QF_E4M3) m[i] = lds_f32(mult_s + 4u * static_cast<uint32_t>(r));
     }
   }
 #pragma unroll
@@ -156,12 +175,12 @@ __device__ __forceinline__ void convert_tasks(int ct, int rows, const uint8_t* r
       if (!valid(r)) {
         o = make_uint4(0u, 0u, 0u, 0u);
       } else if (QF == QF_NF4) {
-        o = nf4_chunk(code[i].x, m[i], lv);
+        o = nf4_chunk(code[i].x, m[i], lv_s);
       } else {
         o = e4m3_chunk<QF>(code[i], __float2bfloat162_rn(m[i]));  // m holds a bf16 value: exact
       }
-      *reinterpret_cast<uint4*>(bdst + r * 128 + ((static_cast<uint32_t>(c) ^ static_cast<uint32_t>(r & 7)) << 4)) =
-          o;
+      sts_v4(bdst_s + static_cast<uint32_t>(r * 128) + ((static_cast<uint32_t>(c) ^ static_cast<uint32_t>(r & 7)) << 4),
+             o);
     }
   }
 }
